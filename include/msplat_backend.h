@@ -1,0 +1,178 @@
+/*
+ * msplat_backend.h — C ABI of the B200 (sm_100a) training-step backend.
+ *
+ * Drop-in for the reference's backend boundary core/metal/bindings.h, whose
+ * functions take MTensor (a Metal buffer plus shape). Here every tensor is a
+ * plain CUDA device pointer with the reference's layout and the functions are
+ * extern "C", so cgo/JNI/ctypes/Swift-C callers can bind them directly:
+ *
+ *   means [N,3]  scales [N,2] (log)  quats [N,4]  opacities [N] (logit)
+ *   features_dc [N,3]  features_rest [N,K,3] (K = (degree+1)^2 - 1)
+ *   images [H,W,3] float32, row-major; tiles are 16x16.
+ *
+ * Errors: every entry point returns MSPLAT_OK (0) or an error code and never
+ * throws across the boundary; msplat_last_error() describes the last failure
+ * of the calling thread. The reference prints to stderr and asserts instead
+ * (core/metal/msplat_metal.mm:215-220, 560-575).
+ *
+ * Threading: one workspace per CUDA device, reused across calls and grown on
+ * demand (the reference's FusedTensorCache, msplat_metal.mm:353-537). Calls on
+ * the same device must not overlap; tensors returned by msplat_last_tensor
+ * alias the workspace and are invalidated by the next call, as the reference's
+ * msplat_last_* accessors are.
+ */
+#ifndef MSPLAT_BACKEND_H
+#define MSPLAT_BACKEND_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    MSPLAT_OK = 0,
+    MSPLAT_ERR_ARGUMENT = 1,   /* bad pointer, size or degree */
+    MSPLAT_ERR_CUDA = 2,       /* a CUDA runtime call failed */
+    MSPLAT_ERR_CAPACITY = 3,   /* an intersection buffer could not be sized */
+    MSPLAT_ERR_NONFINITE = 4   /* the loss came out NaN or infinite */
+};
+
+/* Status flags raised by the last step (msplat_last_status_flags). */
+#define MSPLAT_FLAG_TILE_OVERFLOW 0x1u /* some tile had > 2048 intersections; the 2048 lowest ids were kept */
+
+/* Camera prepared by the host (Model::prepareCam, core/src/model.cpp:500-544). */
+typedef struct MsplatCamera {
+    float viewmat[16]; /* row-major world -> camera */
+    float projmat[16]; /* row-major world -> clip */
+    float fx, fy, cx, cy;
+    int32_t width, height;
+    float cam_pos[3];
+} MsplatCamera;
+
+/* Gaussian parameters, device pointers in the reference layout. */
+typedef struct MsplatGaussians {
+    int32_t num_points;
+    int32_t sh_degree; /* degree of the stored coefficients, 0..3 */
+    float* means;
+    float* scales;
+    float* quats;
+    float* opacities;
+    float* features_dc;
+    float* features_rest; /* may be NULL when sh_degree == 0 */
+} MsplatGaussians;
+
+/* Adam state for the six groups in Model order (means, scales, quats,
+ * features_dc, features_rest, opacities): model.hpp:117-123. */
+typedef struct MsplatAdamState {
+    float* exp_avg[6];
+    float* exp_avg_sq[6];
+    float lr[6];
+    int32_t step; /* step count AFTER this update (>= 1) */
+    float beta1, beta2, eps;
+} MsplatAdamState;
+
+/* Reference-shaped tensor view returned by msplat_last_tensor. dtype: 0 f32,
+ * 1 i32, 2 i64 (metal_tensor.hpp:18-24 numbering). */
+typedef struct MsplatTensorRef {
+    void* data;
+    int64_t shape[4];
+    int32_t ndim;
+    int32_t dtype;
+} MsplatTensorRef;
+
+/* Replaces msplat_render (core/metal/bindings.h:139-148, impl
+ * msplat_metal.mm:545-772): projection, binning, sort and forward
+ * rasterisation. The image and side outputs stay in the workspace
+ * (msplat_last_tensor "out_img", "out_depth", ...); when out_img is non-NULL
+ * the image is also copied there (device pointer). background is a host
+ * float[3]. Asynchronous on `stream` apart from one small read of the
+ * intersection count. */
+int msplat_render(const MsplatGaussians* g, const MsplatCamera* cam, float glob_scale, float clip_thresh,
+                  int32_t degrees_to_use, const float background[3], float* out_img, void* stream);
+
+/* Replaces msplat_train_step_2dgs (core/metal/bindings.h:48-60, impl
+ * msplat_metal.mm:935-1331): forward, L1 + DSSIM (+ distortion) loss,
+ * backward. Per-Gaussian gradients are left in the workspace (names
+ * "dL_dmean3D", "dL_dscale", "dL_dquat", "dL_dopacity", "dL_dfeatures_dc",
+ * "dL_dfeatures_rest", "dL_dmean2D", "dL_dtransMat", "dL_dnormal3D",
+ * "dL_dcolors"), the densify statistics are updated in place, and the loss is
+ * returned in *loss after synchronising the stream (as the reference does).
+ * gt is a device [H,W,3] image. */
+int msplat_train_step_2dgs(const MsplatGaussians* g, const MsplatCamera* cam, float glob_scale,
+                           float clip_thresh, int32_t degrees_to_use, const float background[3], const float* gt,
+                           float lambda_l1, float lambda_dist, float lambda_dssim, float* xys_grad_norm,
+                           float* vis_counts, float* max_2d_size, float inv_max_dim, float* loss, void* stream);
+
+/* Replaces msplat_fused_adam (core/metal/bindings.h:100-105, impl
+ * msplat_metal.mm:884-906): one Adam step on one flat group. Asynchronous. */
+int msplat_fused_adam(float* params, const float* grads, float* exp_avg, float* exp_avg_sq, uint32_t n,
+                      float step_size, float beta1, float beta2, float bc2_sqrt, float eps, void* stream);
+
+/* Model::fullIteration (core/src/model.cpp:762-829) as one device pipeline:
+ * forward, loss, backward and Adam on all six groups, with the gradients kept
+ * in registers between the projection VJP and the optimiser. Parameters and
+ * moments are updated in place. The loss is written to loss_dev (a device
+ * float) and the call does not wait for the GPU beyond one small read of the
+ * intersection count. write_grads != 0 additionally materialises the
+ * reference-shaped gradients in the workspace. */
+int msplat_train_step_fused(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
+                            const float background[3], const float* gt, float lambda_l1, float lambda_dist,
+                            float lambda_dssim, const MsplatAdamState* adam, float* xys_grad_norm,
+                            float* vis_counts, float* max_2d_size, float* loss_dev, int32_t write_grads,
+                            void* stream);
+
+/* Tile-sharded pieces of the step for multi-GPU runs (one process per GPU).
+ * Part 1 projects all N Gaussians, bins and rasterises the tile rows
+ * [tile_row_begin, tile_row_end) plus a one-tile-row halo, evaluates the
+ * loss on the owned rows and rasterises the backward there; it leaves the
+ * raster-space gradients [N,16] in raster_grads_out (device, zeroed by the
+ * call) and the three loss partial sums (l1, ssim, distortion) in
+ * loss_parts_dev (device double[3]). After the caller sums raster_grads across
+ * ranks (reduce-scatter), part 2 runs the projection VJP and Adam on
+ * Gaussians [g_begin, g_end). */
+int msplat_shard_forward_backward(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
+                                  const float background[3], const float* gt, float lambda_l1, float lambda_dist,
+                                  float lambda_dssim, int32_t tile_row_begin, int32_t tile_row_end,
+                                  float* raster_grads_out, double* loss_parts_dev, void* stream);
+int msplat_shard_project_backward_adam(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
+                                       const float* raster_grads, int32_t g_begin, int32_t g_end,
+                                       const MsplatAdamState* adam, float* xys_grad_norm, float* vis_counts,
+                                       float* max_2d_size, void* stream);
+
+/* Accessor for the workspace tensors of the last call (the msplat_last_*
+ * family, core/metal/bindings.h:36-43, 107-131). Names: out_img, out_depth,
+ * out_normal, out_alpha, out_median_depth, out_distortion, final_Ts,
+ * final_idx, dL_dout_img, radii, depths, xys, transMats, normal_opacity,
+ * colors, num_tiles_hit, tile_bins, gaussian_ids, raw_tile_counts and the
+ * dL_d* gradients listed above. Returns MSPLAT_ERR_ARGUMENT for an unknown
+ * name or a tensor the last call did not produce. */
+int msplat_last_tensor(const char* name, MsplatTensorRef* out);
+
+/* Number of kept tile intersections of the last call. */
+int64_t msplat_last_num_intersections(void);
+/* MSPLAT_FLAG_* bits raised by the last call. */
+uint32_t msplat_last_status_flags(void);
+/* Stage timing with CUDA events recorded on the launch stream at stage
+ * boundaries (the reference's PROFILE_STAGES intent, msplat_metal.mm:84-129).
+ * Enabling (or disabling) resets the totals. msplat_stage_times waits for the
+ * recorded steps, writes the accumulated milliseconds and the number of
+ * samples per stage, and returns the number of stages (or -1 on error). */
+int msplat_set_stage_timing(int32_t enable);
+int32_t msplat_stage_times(double* total_ms, int64_t* counts, int32_t max_stages);
+const char* msplat_stage_name(int32_t i);
+/* Kernel launches issued by this library since load (for launch accounting). */
+int64_t msplat_launch_count(void);
+/* Per-thread description of the last error ("" if none). */
+const char* msplat_last_error(void);
+
+/* msplat_commit / msplat_gpu_sync (core/metal/bindings.h:21-24). */
+void msplat_commit(void);
+void msplat_gpu_sync(void);
+/* cleanup_msplat_metal (core/metal/bindings.h:8): frees every workspace. */
+void msplat_backend_cleanup(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,696 @@
+// backend.cu — the C ABI of include/msplat_backend.h: per-device workspace,
+// stage sequencing on one stream, reference-shaped accessors.
+//
+// Stage order of one training step (msplat_train_step_2dgs,
+// core/metal/msplat_metal.mm:935-1331, plus Model::fullIteration's Adam loop,
+// core/src/model.cpp:800-826):
+//   project (+ tile difference array) -> tile counts/scans -> [read totals]
+//   -> emit keys -> per-tile select/sort -> rasterise forward -> fused
+//   L1+DSSIM loss fwd/bwd -> loss finalize -> rasterise backward ->
+//   projection VJP (+ Adam on all groups).
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/msplat_backend.h"
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace msplat {
+
+static std::atomic<int64_t> g_launches{0};
+void note_launches(int k) { g_launches.fetch_add(k, std::memory_order_relaxed); }
+
+namespace {
+
+thread_local std::string t_last_error;
+
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define CK(call)                                                                                    \
+    do {                                                                                            \
+        cudaError_t e_ = (call);                                                                    \
+        if (e_ != cudaSuccess)                                                                      \
+            throw Error(MSPLAT_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));       \
+    } while (0)
+
+// Device buffer that only grows.
+struct Buf {
+    void* p = nullptr;
+    size_t cap = 0;
+    void ensure(size_t bytes) {
+        if (bytes <= cap) return;
+        if (p) CK(cudaFree(p));
+        p = nullptr;
+        cap = 0;
+        size_t want = bytes + bytes / 8 + 256;
+        CK(cudaMalloc(&p, want));
+        cap = want;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+    }
+    template <typename T>
+    T* as() const { return static_cast<T*>(p); }
+};
+
+struct Workspace {
+    int device = -1;
+    // per Gaussian
+    Buf records, rects, depths, radii, raster_grads;
+    Buf xys, transmats, num_tiles_hit, normal_opacity, colors, aabb;
+    Buf dL_dmean3D, dL_dscale, dL_dquat, dL_dmean2D, dL_dfeatures_dc, dL_dfeatures_rest, dL_dopacity;
+    Buf dL_dtransMat, dL_dnormal3D, dL_dcolors;
+    // per tile / intersection
+    Buf tile_diff, raw_counts, raw_start, tile_bins, fill, raw_keys, gaussian_ids;
+    // per pixel
+    Buf final_Ts, final_idx, out_img, out_depth, out_normal, out_alpha, out_median, out_dist, dL_dout_img;
+    // scalars
+    Buf loss_partials, loss_out, loss_f, err, totals;
+    int64_t* h_totals = nullptr;  // pinned [2]
+    uint32_t* h_err = nullptr;    // pinned [1]
+    // shape bookkeeping of the last call
+    int n = 0, K = 0, W = 0, H = 0, tx = 0, ty = 0;
+    int64_t kept = 0;
+    uint32_t flags = 0;
+    bool flags_pending = false;       // err word not yet read back
+    cudaStream_t last_stream = nullptr;
+    // stage timing (msplat_set_stage_timing): per step, (stage id, event) at
+    // each stage boundary; stage id -1 closes the step
+    std::vector<std::vector<std::pair<int, cudaEvent_t>>> ev_pending;
+    std::vector<cudaEvent_t> ev_pool;
+    bool have_ref_proj = false, have_grads = false, have_pixels = false, have_dimg = false;
+
+    void release_all() {
+        Buf* all[] = {&records, &rects, &depths, &radii, &raster_grads, &xys, &transmats, &num_tiles_hit,
+                      &normal_opacity, &colors, &aabb, &dL_dmean3D, &dL_dscale, &dL_dquat, &dL_dmean2D,
+                      &dL_dfeatures_dc, &dL_dfeatures_rest, &dL_dopacity, &dL_dtransMat, &dL_dnormal3D,
+                      &dL_dcolors, &tile_diff, &raw_counts, &raw_start, &tile_bins, &fill, &raw_keys,
+                      &gaussian_ids, &final_Ts, &final_idx, &out_img, &out_depth, &out_normal, &out_alpha,
+                      &out_median, &out_dist, &dL_dout_img, &loss_partials, &loss_out, &loss_f, &err, &totals};
+        for (Buf* b : all) b->release();
+        for (auto& set : ev_pending)
+            for (auto& m : set) cudaEventDestroy(m.second);
+        for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
+        ev_pending.clear();
+        ev_pool.clear();
+        if (h_totals) cudaFreeHost(h_totals);
+        if (h_err) cudaFreeHost(h_err);
+        h_totals = nullptr;
+        h_err = nullptr;
+    }
+};
+
+std::mutex g_ws_mu;
+std::vector<Workspace*> g_ws;
+
+// Stage timing: CUDA events recorded on the launch stream at stage
+// boundaries, read back only when msplat_stage_times() is called.
+enum Stage { kStProject = 0, kStCounts, kStEmit, kStSort, kStRasterFwd, kStLoss, kStRasterBwd, kStProjectBwd,
+             kNumStages };
+const char* kStageNames[kNumStages] = {"project_forward", "tile_counts", "emit_keys", "tile_sort",
+                                       "rasterize_forward", "loss_ssim", "rasterize_backward",
+                                       "project_backward_adam"};
+bool g_timing = false;
+double g_stage_ms[kNumStages] = {};
+int64_t g_stage_n[kNumStages] = {};
+
+Workspace& workspace() {
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(g_ws_mu);
+    if ((int)g_ws.size() <= dev) g_ws.resize(dev + 1, nullptr);
+    if (!g_ws[dev]) {
+        g_ws[dev] = new Workspace();
+        g_ws[dev]->device = dev;
+    }
+    Workspace& w = *g_ws[dev];
+    if (!w.h_totals) {
+        CK(cudaHostAlloc(reinterpret_cast<void**>(&w.h_totals), 2 * sizeof(int64_t), cudaHostAllocDefault));
+        CK(cudaHostAlloc(reinterpret_cast<void**>(&w.h_err), sizeof(uint32_t), cudaHostAllocDefault));
+    }
+    return w;
+}
+
+cudaEvent_t take_event(Workspace& w) {
+    if (!w.ev_pool.empty()) {
+        cudaEvent_t e = w.ev_pool.back();
+        w.ev_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e;
+    CK(cudaEventCreate(&e));
+    return e;
+}
+
+// Marks the start of `stage` (stage -1 marks the end of the step).
+void mark(Workspace& w, int stage, cudaStream_t s) {
+    if (!g_timing) return;
+    if (stage == kStProject) w.ev_pending.emplace_back();
+    if (w.ev_pending.empty()) return;
+    cudaEvent_t e = take_event(w);
+    CK(cudaEventRecord(e, s));
+    w.ev_pending.back().emplace_back(stage, e);
+}
+
+// Waits for every recorded step and adds its stage durations.
+void flush_timing(Workspace& w) {
+    for (auto& set : w.ev_pending) {
+        if (set.size() >= 2) {
+            CK(cudaEventSynchronize(set.back().second));
+            for (size_t k = 0; k + 1 < set.size(); ++k) {
+                const int st = set[k].first;
+                if (st < 0 || st >= kNumStages) continue;
+                float ms = 0.f;
+                CK(cudaEventElapsedTime(&ms, set[k].second, set[k + 1].second));
+                g_stage_ms[st] += ms;
+                g_stage_n[st] += 1;
+            }
+        }
+        for (auto& m : set) w.ev_pool.push_back(m.second);
+    }
+    w.ev_pending.clear();
+}
+
+int sh_rest_bases(int degree) { return (degree + 1) * (degree + 1) - 1; }
+
+void check_inputs(const MsplatGaussians* g, const MsplatCamera* cam, int degrees_to_use) {
+    if (!g || !cam) throw Error(MSPLAT_ERR_ARGUMENT, "null gaussians or camera");
+    if (g->num_points < 0 || g->num_points > (1 << 24))
+        throw Error(MSPLAT_ERR_ARGUMENT, "num_points must be in [0, 2^24]");
+    if (g->sh_degree < 0 || g->sh_degree > 3) throw Error(MSPLAT_ERR_ARGUMENT, "sh_degree must be 0..3");
+    if (degrees_to_use < 0 || degrees_to_use > g->sh_degree)
+        throw Error(MSPLAT_ERR_ARGUMENT, "degrees_to_use must be in [0, sh_degree]");
+    if (cam->width <= 0 || cam->height <= 0 || cam->width > 65535 * 16 || cam->height > 65535 * 16)
+        throw Error(MSPLAT_ERR_ARGUMENT, "bad image size");
+    if (g->num_points > 0 && (!g->means || !g->scales || !g->quats || !g->opacities || !g->features_dc))
+        throw Error(MSPLAT_ERR_ARGUMENT, "null parameter pointer");
+    if (g->sh_degree > 0 && g->num_points > 0 && !g->features_rest)
+        throw Error(MSPLAT_ERR_ARGUMENT, "features_rest is null for sh_degree > 0");
+}
+
+CameraDev make_cam(const MsplatCamera* c) {
+    CameraDev d;
+    std::memcpy(d.viewmat, c->viewmat, sizeof(d.viewmat));
+    std::memcpy(d.projmat, c->projmat, sizeof(d.projmat));
+    d.fx = c->fx; d.fy = c->fy; d.cx = c->cx; d.cy = c->cy;
+    d.width = c->width; d.height = c->height;
+    d.tiles_x = (c->width + kTile - 1) / kTile;
+    d.tiles_y = (c->height + kTile - 1) / kTile;
+    d.cam_pos[0] = c->cam_pos[0]; d.cam_pos[1] = c->cam_pos[1]; d.cam_pos[2] = c->cam_pos[2];
+    return d;
+}
+
+// Projection, binning, sort and forward rasterisation of tile rows
+// [row0, row1). Fills the workspace; returns nothing.
+void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam, int degrees_to_use,
+                   float glob_scale, float clip, const float bg[3], bool ref_outputs, int row0, int row1,
+                   cudaStream_t s) {
+    const int n = g->num_points;
+    const int K = sh_rest_bases(g->sh_degree);
+    const int tx = cam.tiles_x, ty = cam.tiles_y, T = tx * ty;
+    const size_t P = (size_t)cam.width * cam.height;
+    w.n = n; w.K = K; w.W = cam.width; w.H = cam.height; w.tx = tx; w.ty = ty;
+    w.flags = 0;
+    w.have_ref_proj = ref_outputs;
+    w.have_grads = false;
+    w.have_dimg = false;
+    const size_t nn = (size_t)(n > 0 ? n : 1);
+    w.records.ensure(nn * kRecordF4 * sizeof(float4));
+    w.rects.ensure(nn * sizeof(uint2));
+    w.depths.ensure(nn * sizeof(float));
+    w.radii.ensure(nn * sizeof(int32_t));
+    if (ref_outputs) {
+        w.xys.ensure(nn * 2 * 4); w.transmats.ensure(nn * 9 * 4); w.num_tiles_hit.ensure(nn * 4);
+        w.normal_opacity.ensure(nn * 4 * 4); w.colors.ensure(nn * 3 * 4); w.aabb.ensure(nn * 2 * 4);
+    }
+    w.tile_diff.ensure((size_t)(tx + 1) * (ty + 1) * 4);
+    w.raw_counts.ensure((size_t)T * 4);
+    w.raw_start.ensure((size_t)T * 8);
+    w.tile_bins.ensure((size_t)T * sizeof(int2));
+    w.fill.ensure((size_t)T * 4);
+    w.totals.ensure(2 * sizeof(int64_t));
+    w.err.ensure(sizeof(uint32_t));
+    w.final_Ts.ensure(P * 3 * 4); w.final_idx.ensure(P * 2 * 4); w.out_img.ensure(P * 3 * 4);
+    w.out_depth.ensure(P * 4); w.out_normal.ensure(P * 3 * 4); w.out_alpha.ensure(P * 4);
+    w.out_median.ensure(P * 4); w.out_dist.ensure(P * 4);
+
+    CK(cudaMemsetAsync(w.tile_diff.p, 0, (size_t)(tx + 1) * (ty + 1) * 4, s));
+    CK(cudaMemsetAsync(w.fill.p, 0, (size_t)T * 4, s));
+    CK(cudaMemsetAsync(w.err.p, 0, sizeof(uint32_t), s));
+
+    ProjFwdArgs pa{};
+    pa.n = n;
+    pa.means = g->means; pa.scales = g->scales; pa.quats = g->quats; pa.opacities = g->opacities;
+    pa.f_dc = g->features_dc; pa.f_rest = g->features_rest;
+    pa.rest_bases = K; pa.degrees_to_use = degrees_to_use;
+    pa.glob_scale = glob_scale; pa.clip_thresh = clip;
+    pa.cam = cam;
+    pa.records = w.records.as<float4>(); pa.rects = w.rects.as<uint2>(); pa.depths = w.depths.as<float>();
+    pa.radii = w.radii.as<int32_t>(); pa.tile_diff = w.tile_diff.as<int32_t>();
+    if (ref_outputs) {
+        pa.xys = w.xys.as<float>(); pa.transmats = w.transmats.as<float>();
+        pa.num_tiles_hit = w.num_tiles_hit.as<int32_t>(); pa.normal_opacity = w.normal_opacity.as<float>();
+        pa.colors = w.colors.as<float>(); pa.aabb = w.aabb.as<float>();
+    }
+    mark(w, kStProject, s);
+    launch_project_forward(pa, s);
+    mark(w, kStCounts, s);
+    launch_tile_counts(w.tile_diff.as<int32_t>(), tx, ty, w.raw_counts.as<int32_t>(), w.raw_start.as<int64_t>(),
+                       w.tile_bins.as<int2>(), w.totals.as<int64_t>(), s);
+    // The one host read of the step: buffer sizes for the intersections.
+    CK(cudaMemcpyAsync(w.h_totals, w.totals.p, 2 * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    const int64_t raw_total = w.h_totals[0], kept = w.h_totals[1];
+    if (raw_total < 0 || kept < 0 || kept > raw_total) throw Error(MSPLAT_ERR_CAPACITY, "corrupt tile totals");
+    w.kept = kept;
+    w.raw_keys.ensure((size_t)(raw_total > 0 ? raw_total : 1) * sizeof(uint64_t));
+    w.gaussian_ids.ensure((size_t)(kept > 0 ? kept : 1) * sizeof(int32_t));
+    mark(w, kStEmit, s);
+    launch_emit_keys(n, w.rects.as<uint2>(), w.depths.as<float>(), tx, w.raw_start.as<int64_t>(),
+                     w.fill.as<int32_t>(), w.raw_keys.as<uint64_t>(), s);
+    mark(w, kStSort, s);
+    launch_tile_sort(T, w.raw_counts.as<int32_t>(), w.raw_start.as<int64_t>(), w.raw_keys.as<uint64_t>(),
+                     w.tile_bins.as<int2>(), w.gaussian_ids.as<int32_t>(), w.err.as<uint32_t>(), s);
+    RasterFwdArgs ra{};
+    ra.width = cam.width; ra.height = cam.height; ra.tiles_x = tx; ra.tiles_y = ty;
+    ra.tile_row_begin = row0; ra.tile_row_end = row1;
+    ra.tile_bins = w.tile_bins.as<int2>(); ra.gaussian_ids = w.gaussian_ids.as<int32_t>();
+    ra.records = w.records.as<float4>();
+    ra.bg[0] = bg[0]; ra.bg[1] = bg[1]; ra.bg[2] = bg[2];
+    ra.final_Ts = w.final_Ts.as<float>(); ra.final_idx = w.final_idx.as<int32_t>(); ra.out_img = w.out_img.as<float>();
+    ra.out_depth = w.out_depth.as<float>(); ra.out_normal = w.out_normal.as<float>();
+    ra.out_alpha = w.out_alpha.as<float>(); ra.out_median_depth = w.out_median.as<float>();
+    ra.out_distortion = w.out_dist.as<float>();
+    mark(w, kStRasterFwd, s);
+    launch_rasterize_forward(ra, s);
+    w.have_pixels = true;
+    w.flags_pending = true;
+    w.last_stream = s;
+}
+
+// Loss forward/backward over pixel rows [prow0, prow1); finalize into
+// loss_out (double[4]) and loss_f (float).
+void stage_loss(Workspace& w, const CameraDev& cam, const float* gt, float l1, float ldist, float ldssim, int prow0,
+                int prow1, bool finalize, cudaStream_t s) {
+    const size_t P = (size_t)cam.width * cam.height;
+    w.dL_dout_img.ensure(P * 3 * 4);
+    const int nb = loss_num_blocks(cam.width, prow0, prow1);
+    w.loss_partials.ensure((size_t)(nb > 0 ? nb : 1) * 3 * sizeof(double));
+    w.loss_out.ensure(4 * sizeof(double));
+    w.loss_f.ensure(sizeof(float));
+    LossArgs la{};
+    la.width = cam.width; la.height = cam.height; la.row_begin = prow0; la.row_end = prow1;
+    la.out_img = w.out_img.as<float>(); la.gt = gt; la.out_distortion = w.out_dist.as<float>();
+    la.lambda_l1 = l1; la.lambda_dist = ldist; la.lambda_dssim = ldssim;
+    la.inv_num = 1.0f / (float)(cam.height * cam.width * 3);
+    la.dL_dout_img = w.dL_dout_img.as<float>();
+    la.partials = w.loss_partials.as<double>();
+    mark(w, kStLoss, s);
+    launch_loss_ssim(la, s);
+    if (finalize)
+        launch_loss_finalize(w.loss_partials.as<double>(), nb, ldssim, la.inv_num, w.loss_out.as<double>(),
+                             w.loss_f.as<float>(), w.err.as<uint32_t>(), s);
+    w.have_dimg = true;
+}
+
+void stage_raster_backward(Workspace& w, const CameraDev& cam, const float bg[3], float ldist, int row0, int row1,
+                           float* raster_grads, cudaStream_t s) {
+    RasterBwdArgs ba{};
+    ba.width = cam.width; ba.height = cam.height; ba.tiles_x = cam.tiles_x; ba.tiles_y = cam.tiles_y;
+    ba.tile_row_begin = row0; ba.tile_row_end = row1;
+    ba.tile_bins = w.tile_bins.as<int2>(); ba.gaussian_ids = w.gaussian_ids.as<int32_t>();
+    ba.records = w.records.as<float4>();
+    ba.bg[0] = bg[0]; ba.bg[1] = bg[1]; ba.bg[2] = bg[2];
+    ba.final_Ts = w.final_Ts.as<float>(); ba.final_idx = w.final_idx.as<int32_t>();
+    ba.dL_dout_img = w.dL_dout_img.as<float>();
+    ba.dL_dout_distortion = ldist * (1.0f / (float)(cam.height * cam.width * 3)) * 3.0f;  // lambda_dist / HW
+    ba.raster_grads = raster_grads;
+    mark(w, kStRasterBwd, s);
+    launch_rasterize_backward(ba, s);
+}
+
+ProjBwdArgs make_proj_bwd(Workspace& w, const MsplatGaussians* g, const CameraDev& cam, int degrees_to_use,
+                          float glob_scale, const float* raster_grads, int g0, int g1) {
+    ProjBwdArgs pb{};
+    pb.g_begin = g0; pb.g_end = g1;
+    pb.means = g->means; pb.scales = g->scales; pb.quats = g->quats; pb.f_dc = g->features_dc;
+    pb.f_rest = g->features_rest; pb.opacities = g->opacities;
+    pb.rest_bases = sh_rest_bases(g->sh_degree); pb.degrees_to_use = degrees_to_use;
+    pb.glob_scale = glob_scale; pb.cam = cam;
+    pb.radii = w.radii.as<int32_t>();
+    pb.raster_grads = raster_grads;
+    pb.inv_max_dim = 1.0f / (float)std::max(cam.width, cam.height);
+    return pb;
+}
+
+void set_adam(ProjBwdArgs& pb, const MsplatAdamState* adam) {
+    if (!adam) throw Error(MSPLAT_ERR_ARGUMENT, "null adam state");
+    if (adam->step < 1) throw Error(MSPLAT_ERR_ARGUMENT, "adam step must be >= 1");
+    pb.do_adam = 1;
+    // Model::fullIteration: bc1/bc2 from std::pow(float, int) (double), model.cpp:767-769, 815-818.
+    const float bc1 = 1.0f - std::pow(adam->beta1, adam->step);
+    const float bc2 = 1.0f - std::pow(adam->beta2, adam->step);
+    for (int k = 0; k < 6; ++k) {
+        pb.exp_avg[k] = adam->exp_avg[k];
+        pb.exp_avg_sq[k] = adam->exp_avg_sq[k];
+        pb.step_size[k] = adam->lr[k] / bc1;
+    }
+    pb.beta1 = adam->beta1; pb.beta2 = adam->beta2; pb.eps = adam->eps;
+    pb.bc2_sqrt = std::sqrt(bc2);
+}
+
+template <typename F>
+int guarded(F&& f) {
+    try {
+        f();
+        t_last_error.clear();
+        return MSPLAT_OK;
+    } catch (const Error& e) {
+        t_last_error = e.what();
+        return e.code;
+    } catch (const std::exception& e) {
+        t_last_error = e.what();
+        return MSPLAT_ERR_CUDA;
+    }
+}
+
+}  // namespace
+}  // namespace msplat
+
+using namespace msplat;
+
+extern "C" {
+
+int msplat_render(const MsplatGaussians* g, const MsplatCamera* cam, float glob_scale, float clip_thresh,
+                  int32_t degrees_to_use, const float background[3], float* out_img, void* stream) {
+    return guarded([&] {
+        check_inputs(g, cam, degrees_to_use);
+        if (!background) throw Error(MSPLAT_ERR_ARGUMENT, "null background");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        Workspace& w = workspace();
+        CameraDev cd = make_cam(cam);
+        stage_forward(w, g, cd, degrees_to_use, glob_scale, clip_thresh, background, true, 0, cd.tiles_y, s);
+        mark(w, -1, s);
+        if (out_img)
+            CK(cudaMemcpyAsync(out_img, w.out_img.p, (size_t)cd.width * cd.height * 3 * 4, cudaMemcpyDeviceToDevice, s));
+        CK(cudaGetLastError());
+    });
+}
+
+int msplat_train_step_2dgs(const MsplatGaussians* g, const MsplatCamera* cam, float glob_scale, float clip_thresh,
+                           int32_t degrees_to_use, const float background[3], const float* gt, float lambda_l1,
+                           float lambda_dist, float lambda_dssim, float* xys_grad_norm, float* vis_counts,
+                           float* max_2d_size, float inv_max_dim, float* loss, void* stream) {
+    return guarded([&] {
+        check_inputs(g, cam, degrees_to_use);
+        if (!background || !gt) throw Error(MSPLAT_ERR_ARGUMENT, "null background or gt");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        Workspace& w = workspace();
+        CameraDev cd = make_cam(cam);
+        const int n = g->num_points;
+        stage_forward(w, g, cd, degrees_to_use, glob_scale, clip_thresh, background, true, 0, cd.tiles_y, s);
+        stage_loss(w, cd, gt, lambda_l1, lambda_dist, lambda_dssim, 0, cd.height, true, s);
+        const size_t nn = (size_t)(n > 0 ? n : 1);
+        w.raster_grads.ensure(nn * kGradStride * 4);
+        CK(cudaMemsetAsync(w.raster_grads.p, 0, nn * kGradStride * 4, s));
+        stage_raster_backward(w, cd, background, lambda_dist, 0, cd.tiles_y, w.raster_grads.as<float>(), s);
+        const int K = sh_rest_bases(g->sh_degree);
+        w.dL_dmean3D.ensure(nn * 12); w.dL_dscale.ensure(nn * 8); w.dL_dquat.ensure(nn * 16);
+        w.dL_dmean2D.ensure(nn * 8); w.dL_dfeatures_dc.ensure(nn * 12);
+        w.dL_dfeatures_rest.ensure(nn * (size_t)(K > 0 ? K : 1) * 12); w.dL_dopacity.ensure(nn * 4);
+        w.dL_dtransMat.ensure(nn * 36); w.dL_dnormal3D.ensure(nn * 12); w.dL_dcolors.ensure(nn * 12);
+        ProjBwdArgs pb = make_proj_bwd(w, g, cd, degrees_to_use, glob_scale, w.raster_grads.as<float>(), 0, n);
+        pb.inv_max_dim = inv_max_dim;
+        pb.dL_dmean3D = w.dL_dmean3D.as<float>(); pb.dL_dscale = w.dL_dscale.as<float>();
+        pb.dL_dquat = w.dL_dquat.as<float>(); pb.dL_dmean2D = w.dL_dmean2D.as<float>();
+        pb.dL_dfeatures_dc = w.dL_dfeatures_dc.as<float>();
+        pb.dL_dfeatures_rest = K > 0 ? w.dL_dfeatures_rest.as<float>() : nullptr;
+        pb.dL_dopacity = w.dL_dopacity.as<float>();
+        pb.xys_grad_norm = xys_grad_norm; pb.vis_counts = vis_counts; pb.max_2d_size = max_2d_size;
+        if ((xys_grad_norm == nullptr) != (vis_counts == nullptr) || (vis_counts == nullptr) != (max_2d_size == nullptr))
+            throw Error(MSPLAT_ERR_ARGUMENT, "densify statistics must be all set or all null");
+        mark(w, kStProjectBwd, s);
+        launch_project_backward(pb, s);
+        mark(w, -1, s);
+        launch_unpack_raster_grads(n, w.raster_grads.as<float>(), w.dL_dtransMat.as<float>(),
+                                   w.dL_dnormal3D.as<float>(), w.dL_dcolors.as<float>(), nullptr, s);
+        w.have_grads = true;
+        float lf = 0.f;
+        CK(cudaMemcpyAsync(w.h_err, w.err.p, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+        CK(cudaMemcpyAsync(&lf, w.loss_f.p, sizeof(float), cudaMemcpyDeviceToHost, s));
+        CK(cudaStreamSynchronize(s));
+        CK(cudaGetLastError());
+        w.flags = *w.h_err;
+        w.flags_pending = false;
+        if (loss) *loss = lf;
+        if (w.flags & kErrCapacity) throw Error(MSPLAT_ERR_CAPACITY, "tile select kept a wrong count");
+        if (w.flags & kErrNonFinite) throw Error(MSPLAT_ERR_NONFINITE, "loss is not finite");
+    });
+}
+
+int msplat_fused_adam(float* params, const float* grads, float* exp_avg, float* exp_avg_sq, uint32_t n,
+                      float step_size, float beta1, float beta2, float bc2_sqrt, float eps, void* stream) {
+    return guarded([&] {
+        if (n > 0 && (!params || !grads || !exp_avg || !exp_avg_sq)) throw Error(MSPLAT_ERR_ARGUMENT, "null pointer");
+        launch_fused_adam(params, grads, exp_avg, exp_avg_sq, (int64_t)n, step_size, beta1, beta2, bc2_sqrt, eps,
+                          static_cast<cudaStream_t>(stream));
+        CK(cudaGetLastError());
+    });
+}
+
+int msplat_train_step_fused(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
+                            const float background[3], const float* gt, float lambda_l1, float lambda_dist,
+                            float lambda_dssim, const MsplatAdamState* adam, float* xys_grad_norm,
+                            float* vis_counts, float* max_2d_size, float* loss_dev, int32_t write_grads,
+                            void* stream) {
+    return guarded([&] {
+        check_inputs(g, cam, degrees_to_use);
+        if (!background || !gt) throw Error(MSPLAT_ERR_ARGUMENT, "null background or gt");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        Workspace& w = workspace();
+        CameraDev cd = make_cam(cam);
+        const int n = g->num_points;
+        stage_forward(w, g, cd, degrees_to_use, 1.0f, 0.01f, background, write_grads != 0, 0, cd.tiles_y, s);
+        stage_loss(w, cd, gt, lambda_l1, lambda_dist, lambda_dssim, 0, cd.height, true, s);
+        const size_t nn = (size_t)(n > 0 ? n : 1);
+        w.raster_grads.ensure(nn * kGradStride * 4);
+        CK(cudaMemsetAsync(w.raster_grads.p, 0, nn * kGradStride * 4, s));
+        stage_raster_backward(w, cd, background, lambda_dist, 0, cd.tiles_y, w.raster_grads.as<float>(), s);
+        ProjBwdArgs pb = make_proj_bwd(w, g, cd, degrees_to_use, 1.0f, w.raster_grads.as<float>(), 0, n);
+        set_adam(pb, adam);
+        pb.xys_grad_norm = xys_grad_norm; pb.vis_counts = vis_counts; pb.max_2d_size = max_2d_size;
+        if ((xys_grad_norm == nullptr) != (vis_counts == nullptr) || (vis_counts == nullptr) != (max_2d_size == nullptr))
+            throw Error(MSPLAT_ERR_ARGUMENT, "densify statistics must be all set or all null");
+        const int K = sh_rest_bases(g->sh_degree);
+        if (write_grads) {
+            w.dL_dmean3D.ensure(nn * 12); w.dL_dscale.ensure(nn * 8); w.dL_dquat.ensure(nn * 16);
+            w.dL_dmean2D.ensure(nn * 8); w.dL_dfeatures_dc.ensure(nn * 12);
+            w.dL_dfeatures_rest.ensure(nn * (size_t)(K > 0 ? K : 1) * 12); w.dL_dopacity.ensure(nn * 4);
+            pb.dL_dmean3D = w.dL_dmean3D.as<float>(); pb.dL_dscale = w.dL_dscale.as<float>();
+            pb.dL_dquat = w.dL_dquat.as<float>(); pb.dL_dmean2D = w.dL_dmean2D.as<float>();
+            pb.dL_dfeatures_dc = w.dL_dfeatures_dc.as<float>();
+            pb.dL_dfeatures_rest = K > 0 ? w.dL_dfeatures_rest.as<float>() : nullptr;
+            pb.dL_dopacity = w.dL_dopacity.as<float>();
+        }
+        mark(w, kStProjectBwd, s);
+        launch_project_backward(pb, s);
+        mark(w, -1, s);
+        if (write_grads) {
+            w.dL_dtransMat.ensure(nn * 36); w.dL_dnormal3D.ensure(nn * 12); w.dL_dcolors.ensure(nn * 12);
+            launch_unpack_raster_grads(n, w.raster_grads.as<float>(), w.dL_dtransMat.as<float>(),
+                                       w.dL_dnormal3D.as<float>(), w.dL_dcolors.as<float>(), nullptr, s);
+            w.have_grads = true;
+        }
+        if (loss_dev) CK(cudaMemcpyAsync(loss_dev, w.loss_f.p, sizeof(float), cudaMemcpyDeviceToDevice, s));
+        CK(cudaGetLastError());
+    });
+}
+
+int msplat_shard_forward_backward(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
+                                  const float background[3], const float* gt, float lambda_l1, float lambda_dist,
+                                  float lambda_dssim, int32_t tile_row_begin, int32_t tile_row_end,
+                                  float* raster_grads_out, double* loss_parts_dev, void* stream) {
+    return guarded([&] {
+        check_inputs(g, cam, degrees_to_use);
+        if (!background || !gt || !raster_grads_out) throw Error(MSPLAT_ERR_ARGUMENT, "null pointer");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        Workspace& w = workspace();
+        CameraDev cd = make_cam(cam);
+        if (tile_row_begin < 0 || tile_row_end > cd.tiles_y || tile_row_begin > tile_row_end)
+            throw Error(MSPLAT_ERR_ARGUMENT, "bad tile row range");
+        const int n = g->num_points;
+        const int r0 = std::max(0, tile_row_begin - 1), r1 = std::min(cd.tiles_y, tile_row_end + 1);
+        stage_forward(w, g, cd, degrees_to_use, 1.0f, 0.01f, background, false, r0, r1, s);
+        const int p0 = tile_row_begin * kTile, p1 = std::min(cd.height, tile_row_end * kTile);
+        stage_loss(w, cd, gt, lambda_l1, lambda_dist, lambda_dssim, p0, p1, false, s);
+        const size_t nn = (size_t)(n > 0 ? n : 1);
+        CK(cudaMemsetAsync(raster_grads_out, 0, nn * kGradStride * 4, s));
+        stage_raster_backward(w, cd, background, lambda_dist, tile_row_begin, tile_row_end, raster_grads_out, s);
+        if (loss_parts_dev) {
+            // Sum the block partials (l1, ssim, dist) without the DSSIM offset.
+            const int nb = loss_num_blocks(cd.width, p0, p1);
+            launch_loss_finalize(w.loss_partials.as<double>(), nb, 0.0f, 0.0f, w.loss_out.as<double>(),
+                                 nullptr, w.err.as<uint32_t>(), s);
+            // loss_out = {l1 + dist, ssim, l1, dist}: forward (l1, ssim, dist)
+            CK(cudaMemcpyAsync(loss_parts_dev, w.loss_out.as<double>() + 2, sizeof(double), cudaMemcpyDeviceToDevice, s));
+            CK(cudaMemcpyAsync(loss_parts_dev + 1, w.loss_out.as<double>() + 1, sizeof(double), cudaMemcpyDeviceToDevice, s));
+            CK(cudaMemcpyAsync(loss_parts_dev + 2, w.loss_out.as<double>() + 3, sizeof(double), cudaMemcpyDeviceToDevice, s));
+        }
+        CK(cudaGetLastError());
+    });
+}
+
+int msplat_shard_project_backward_adam(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
+                                       const float* raster_grads, int32_t g_begin, int32_t g_end,
+                                       const MsplatAdamState* adam, float* xys_grad_norm, float* vis_counts,
+                                       float* max_2d_size, void* stream) {
+    return guarded([&] {
+        check_inputs(g, cam, degrees_to_use);
+        if (!raster_grads) throw Error(MSPLAT_ERR_ARGUMENT, "null raster_grads");
+        if (g_begin < 0 || g_end > g->num_points || g_begin > g_end) throw Error(MSPLAT_ERR_ARGUMENT, "bad shard");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        Workspace& w = workspace();
+        CameraDev cd = make_cam(cam);
+        ProjBwdArgs pb = make_proj_bwd(w, g, cd, degrees_to_use, 1.0f, raster_grads, g_begin, g_end);
+        set_adam(pb, adam);
+        pb.xys_grad_norm = xys_grad_norm; pb.vis_counts = vis_counts; pb.max_2d_size = max_2d_size;
+        mark(w, kStProjectBwd, s);
+        launch_project_backward(pb, s);
+        mark(w, -1, s);
+        CK(cudaGetLastError());
+    });
+}
+
+int msplat_last_tensor(const char* name, MsplatTensorRef* out) {
+    return guarded([&] {
+        if (!name || !out) throw Error(MSPLAT_ERR_ARGUMENT, "null argument");
+        Workspace& w = workspace();
+        const std::string nm(name);
+        const int64_t n = w.n, H = w.H, W = w.W, T = (int64_t)w.tx * w.ty;
+        auto set = [&](const Buf& b, int dtype, std::initializer_list<int64_t> shape, bool ok) {
+            if (!ok || !b.p) throw Error(MSPLAT_ERR_ARGUMENT, "tensor '" + nm + "' not produced by the last call");
+            out->data = b.p;
+            out->dtype = dtype;
+            out->ndim = (int32_t)shape.size();
+            int k = 0;
+            for (int64_t d : shape) out->shape[k++] = d;
+            for (; k < 4; ++k) out->shape[k] = 0;
+        };
+        const bool px = w.have_pixels, rp = w.have_ref_proj, gr = w.have_grads;
+        if (nm == "out_img") set(w.out_img, 0, {H, W, 3}, px);
+        else if (nm == "out_depth") set(w.out_depth, 0, {H, W}, px);
+        else if (nm == "out_normal") set(w.out_normal, 0, {H, W, 3}, px);
+        else if (nm == "out_alpha") set(w.out_alpha, 0, {H, W}, px);
+        else if (nm == "out_median_depth") set(w.out_median, 0, {H, W}, px);
+        else if (nm == "out_distortion") set(w.out_dist, 0, {H, W}, px);
+        else if (nm == "final_Ts") set(w.final_Ts, 0, {H, W, 3}, px);
+        else if (nm == "final_idx") set(w.final_idx, 1, {H, W, 2}, px);
+        else if (nm == "dL_dout_img") set(w.dL_dout_img, 0, {H, W, 3}, w.have_dimg);
+        else if (nm == "radii") set(w.radii, 1, {n}, px);
+        else if (nm == "depths") set(w.depths, 0, {n}, px);
+        else if (nm == "tile_bins") set(w.tile_bins, 1, {T, 2}, px);
+        else if (nm == "raw_tile_counts") set(w.raw_counts, 1, {T}, px);
+        else if (nm == "gaussian_ids") set(w.gaussian_ids, 1, {w.kept}, px);
+        else if (nm == "xys") set(w.xys, 0, {n, 2}, rp);
+        else if (nm == "transMats") set(w.transmats, 0, {n, 9}, rp);
+        else if (nm == "normal_opacity") set(w.normal_opacity, 0, {n, 4}, rp);
+        else if (nm == "colors") set(w.colors, 0, {n, 3}, rp);
+        else if (nm == "num_tiles_hit") set(w.num_tiles_hit, 1, {n}, rp);
+        else if (nm == "dL_dmean3D") set(w.dL_dmean3D, 0, {n, 3}, gr);
+        else if (nm == "dL_dscale") set(w.dL_dscale, 0, {n, 2}, gr);
+        else if (nm == "dL_dquat") set(w.dL_dquat, 0, {n, 4}, gr);
+        else if (nm == "dL_dopacity") set(w.dL_dopacity, 0, {n, 1}, gr);
+        else if (nm == "dL_dfeatures_dc") set(w.dL_dfeatures_dc, 0, {n, 3}, gr);
+        else if (nm == "dL_dfeatures_rest") set(w.dL_dfeatures_rest, 0, {n, w.K, 3}, gr && w.K > 0);
+        else if (nm == "dL_dmean2D") set(w.dL_dmean2D, 0, {n, 2}, gr);
+        else if (nm == "dL_dtransMat") set(w.dL_dtransMat, 0, {n, 9}, gr);
+        else if (nm == "dL_dnormal3D") set(w.dL_dnormal3D, 0, {n, 3}, gr);
+        else if (nm == "dL_dcolors") set(w.dL_dcolors, 0, {n, 3}, gr);
+        else throw Error(MSPLAT_ERR_ARGUMENT, "unknown tensor name '" + nm + "'");
+    });
+}
+
+int64_t msplat_last_num_intersections(void) {
+    try {
+        return workspace().kept;
+    } catch (...) {
+        return -1;
+    }
+}
+
+uint32_t msplat_last_status_flags(void) {
+    try {
+        Workspace& w = workspace();
+        if (w.flags_pending) {
+            CK(cudaMemcpyAsync(w.h_err, w.err.p, sizeof(uint32_t), cudaMemcpyDeviceToHost, w.last_stream));
+            CK(cudaStreamSynchronize(w.last_stream));
+            w.flags = *w.h_err;
+            w.flags_pending = false;
+        }
+        return w.flags & MSPLAT_FLAG_TILE_OVERFLOW;
+    } catch (...) {
+        return 0;
+    }
+}
+
+int msplat_set_stage_timing(int32_t enable) {
+    return guarded([&] {
+        Workspace& w = workspace();
+        flush_timing(w);
+        g_timing = enable != 0;
+        for (int k = 0; k < kNumStages; ++k) {
+            g_stage_ms[k] = 0.0;
+            g_stage_n[k] = 0;
+        }
+    });
+}
+
+int32_t msplat_stage_times(double* total_ms, int64_t* counts, int32_t max_stages) {
+    try {
+        Workspace& w = workspace();
+        flush_timing(w);
+        const int k = max_stages < kNumStages ? max_stages : kNumStages;
+        for (int i = 0; i < k; ++i) {
+            if (total_ms) total_ms[i] = g_stage_ms[i];
+            if (counts) counts[i] = g_stage_n[i];
+        }
+        t_last_error.clear();
+        return kNumStages;
+    } catch (const std::exception& e) {
+        t_last_error = e.what();
+        return -1;
+    }
+}
+
+const char* msplat_stage_name(int32_t i) { return (i >= 0 && i < kNumStages) ? kStageNames[i] : ""; }
+
+int64_t msplat_launch_count(void) { return g_launches.load(); }
+
+const char* msplat_last_error(void) { return t_last_error.c_str(); }
+
+void msplat_commit(void) {}
+
+void msplat_gpu_sync(void) { cudaDeviceSynchronize(); }
+
+void msplat_backend_cleanup(void) {
+    std::lock_guard<std::mutex> lk(g_ws_mu);
+    for (Workspace* w : g_ws)
+        if (w) {
+            w->release_all();
+            delete w;
+        }
+    g_ws.clear();
+}
+
+}  // extern "C"

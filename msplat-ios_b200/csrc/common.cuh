@@ -1,0 +1,76 @@
+// common.cuh — device helpers shared by the msplat B200 kernels.
+//
+// The forward path (projection, binning keys, rasterisation) is evaluated with
+// a fixed sequence of IEEE-rounded operations so that tile counts, per-tile
+// order and the rendered image are reproducible bit for bit on any IEEE
+// implementation that follows the same sequence. The helpers below pin that
+// sequence: __fmul_rn/__fadd_rn/__fsub_rn are never contracted into an FMA by
+// the compiler, __fmaf_rn is always one fused operation.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace msplat {
+
+constexpr int kTile = 16;               // 16x16 pixel tiles (BLOCK_X/BLOCK_Y)
+constexpr int kTilePixels = kTile * kTile;
+constexpr int kMaxTileElems = 2048;     // per-tile intersection cap
+constexpr float kFilterSize = 0.707106f;
+constexpr float kFilterInvSq = 2.0f;
+constexpr float kNearN = 0.2f;
+constexpr float kFarN = 100.0f;
+
+// Per-Gaussian raster record written by the projection and gathered by the
+// rasterisers: 5 x float4 = 80 bytes.
+//   r0 = (Tu.x, Tu.y, Tu.z, Tv.x)
+//   r1 = (Tv.y, Tv.z, Tw.x, Tw.y)
+//   r2 = (Tw.z, xy.x, xy.y, sigmoid(opacity))
+//   r3 = (rgb.r, rgb.g, rgb.b, normal.x)   rgb = max(raw SH colour + 0.5, 0)
+//   r4 = (normal.y, normal.z, 0, 0)
+constexpr int kRecordF4 = 5;
+
+// Per-Gaussian raster-space gradient record accumulated by the backward
+// rasteriser: 16 floats = 4 x float4.
+//   [0..8]  dL/dT (rows Tu, Tv, Tw)   [9] dL/d(raw opacity)
+//   [10..12] dL/d(raw SH colour)      [13..15] dL/d(world normal)
+constexpr int kGradStride = 16;
+
+__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float ffma(float a, float b, float c) { return __fmaf_rn(a, b, c); }
+
+// Deterministic exponential: Cody-Waite reduction x = k*ln2 + r with ln2 split
+// into a 16-bit head (0.693145751953125) and a tail, degree-7 Taylor
+// polynomial for exp(r) on |r| <= ln2/2 evaluated by Horner with fused
+// multiply-adds, exact scaling by 2^k. Flushes to 0 below -86 and to +inf
+// above 88. Relative error is a few ulp; what matters here is that the CPU
+// checker evaluates the identical sequence.
+__device__ __forceinline__ float det_exp(float x) {
+    if (x != x) return x;
+    if (x > 88.0f) return __int_as_float(0x7f800000);
+    if (x < -86.0f) return 0.0f;
+    float kf = rintf(__fmul_rn(x, 1.44269502f));
+    float r = __fmaf_rn(-kf, 0.693145751953125f, x);
+    r = __fmaf_rn(-kf, 1.42860677e-06f, r);
+    float p = 1.98412698e-04f;
+    p = __fmaf_rn(p, r, 1.38888889e-03f);
+    p = __fmaf_rn(p, r, 8.33333377e-03f);
+    p = __fmaf_rn(p, r, 4.16666679e-02f);
+    p = __fmaf_rn(p, r, 1.66666672e-01f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    int k = (int)kf;
+    return __fmul_rn(p, __int_as_float((k + 127) << 23));
+}
+
+// Device-side error word: kernels OR bits into it instead of trapping; the
+// host reads it after the step.
+enum : uint32_t {
+    kErrTileOverflow = 1u << 0,   // a tile had more than 2048 intersections (informational)
+    kErrCapacity = 1u << 1,       // an intersection buffer was too small: step invalid
+    kErrNonFinite = 1u << 2,      // non-finite loss
+};
+
+}  // namespace msplat

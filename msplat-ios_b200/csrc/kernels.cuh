@@ -1,0 +1,130 @@
+// kernels.cuh — launch interfaces of the msplat B200 kernels (host side).
+//
+// Each kernel family lives in its own translation unit; backend.cu sequences
+// them on one CUDA stream. All pointers are device pointers. Layouts follow
+// the reference (core/metal/msplat_metal.mm:353-537) for every tensor that
+// crosses the public boundary; the raster record and the raster-gradient
+// record are internal (common.cuh).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace msplat {
+
+// Kernel-launch accounting (msplat_launch_count): every launcher records the
+// kernels it enqueues.
+void note_launches(int k);
+
+struct CameraDev {
+    float viewmat[16];
+    float projmat[16];
+    float fx, fy, cx, cy;
+    int width, height, tiles_x, tiles_y;
+    float cam_pos[3];
+};
+
+// ---- projection (project.cu) ------------------------------------------------
+struct ProjFwdArgs {
+    int n;
+    const float* means; const float* scales; const float* quats; const float* opacities;
+    const float* f_dc; const float* f_rest;
+    int rest_bases;          // K = num_sh_bases(degree) - 1
+    int degrees_to_use;
+    float glob_scale, clip_thresh;
+    CameraDev cam;
+    // product outputs
+    float4* records;         // [N, 5] float4
+    uint2* rects;            // [N] packed tile rect (x0 | y0 << 16, x1 | y1 << 16)
+    float* depths;           // [N] view-space depth (sort key)
+    int32_t* radii;          // [N]
+    int32_t* tile_diff;      // [(tiles_y+1) * (tiles_x+1)] 2-D difference array (+=)
+    // optional reference-shaped outputs (may be null)
+    float* xys; float* transmats; int32_t* num_tiles_hit; float* normal_opacity;
+    float* colors; float* aabb;
+};
+void launch_project_forward(const ProjFwdArgs& a, cudaStream_t s);
+
+struct ProjBwdArgs {
+    int g_begin, g_end;      // Gaussians handled by this launch (a shard)
+    float* means; float* scales; float* quats; float* f_dc; float* f_rest; float* opacities;
+    int rest_bases, degrees_to_use;
+    float glob_scale;
+    CameraDev cam;
+    const int32_t* radii;
+    const float* raster_grads;   // [N, 16]
+    // optional reference-shaped gradient outputs (null = not written)
+    float* dL_dmean3D; float* dL_dscale; float* dL_dquat; float* dL_dmean2D;
+    float* dL_dfeatures_dc; float* dL_dfeatures_rest; float* dL_dopacity;
+    // densify statistics (updated in place; may be null)
+    float* xys_grad_norm; float* vis_counts; float* max_2d_size; float inv_max_dim;
+    // Adam (applied when do_adam != 0); group order means, scales, quats,
+    // f_dc, f_rest, opacities
+    int do_adam;
+    float* exp_avg[6]; float* exp_avg_sq[6];
+    float step_size[6];
+    float beta1, beta2, bc2_sqrt, eps;
+};
+void launch_project_backward(const ProjBwdArgs& a, cudaStream_t s);
+
+// ---- binning (binning.cu) ---------------------------------------------------
+// Tile counts from the difference array, kept counts, exclusive scans and the
+// two totals. totals[0] = raw intersections (int64), totals[1] = kept.
+void launch_tile_counts(const int32_t* tile_diff, int tiles_x, int tiles_y, int32_t* raw_counts,
+                        int64_t* raw_start, int2* tile_bins, int64_t* totals, cudaStream_t s);
+void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x,
+                      const int64_t* raw_start, int32_t* fill, uint64_t* raw_keys, cudaStream_t s);
+void launch_tile_sort(int num_tiles, const int32_t* raw_counts, const int64_t* raw_start,
+                      const uint64_t* raw_keys, const int2* tile_bins, int32_t* gaussian_ids,
+                      uint32_t* err, cudaStream_t s);
+
+// ---- rasterisation (rasterize.cu) -------------------------------------------
+struct RasterFwdArgs {
+    int width, height, tiles_x, tiles_y;
+    int tile_row_begin, tile_row_end;   // tile rows rendered by this launch
+    const int2* tile_bins; const int32_t* gaussian_ids; const float4* records;
+    float bg[3];
+    float* final_Ts; int32_t* final_idx; float* out_img; float* out_depth; float* out_normal;
+    float* out_alpha; float* out_median_depth; float* out_distortion;
+};
+void launch_rasterize_forward(const RasterFwdArgs& a, cudaStream_t s);
+
+struct RasterBwdArgs {
+    int width, height, tiles_x, tiles_y;
+    int tile_row_begin, tile_row_end;
+    const int2* tile_bins; const int32_t* gaussian_ids; const float4* records;
+    float bg[3];
+    const float* final_Ts; const int32_t* final_idx;
+    const float* dL_dout_img;
+    // auxiliary upstream gradients; all null (and dist_grad == 0) selects the
+    // colour-only kernel used by training
+    const float* dL_dout_depth; const float* dL_dout_alpha; const float* dL_dout_normal;
+    const float* dL_dout_median_depth;
+    float dL_dout_distortion;            // uniform per-pixel distortion gradient
+    float* raster_grads;                 // [N, 16] (+=)
+};
+void launch_rasterize_backward(const RasterBwdArgs& a, cudaStream_t s);
+
+// ---- loss (ssim_loss.cu) ------------------------------------------------------
+struct LossArgs {
+    int width, height;
+    int row_begin, row_end;              // pixel rows owned by this launch
+    const float* out_img; const float* gt; const float* out_distortion;
+    float lambda_l1, lambda_dist, lambda_dssim;
+    float inv_num;                       // 1 / (3 * H * W) of the full image
+    float* dL_dout_img;                  // written for owned rows
+    double* partials;                    // [num_blocks * 3] (l1, ssim, dist) per block
+};
+int loss_num_blocks(int width, int row_begin, int row_end);
+void launch_loss_ssim(const LossArgs& a, cudaStream_t s);
+// Sums the block partials in a fixed order: out[0] = loss, out[1] = ssim sum,
+// out[2] = l1 term, out[3] = distortion term (all double), loss_f = float loss.
+void launch_loss_finalize(const double* partials, int num_blocks, float lambda_dssim, float inv_num,
+                          double* out, float* loss_f, uint32_t* err, cudaStream_t s);
+
+// ---- Adam (adam.cu) -----------------------------------------------------------
+void launch_fused_adam(float* params, const float* grads, float* exp_avg, float* exp_avg_sq, int64_t n,
+                       float step_size, float beta1, float beta2, float bc2_sqrt, float eps, cudaStream_t s);
+void launch_unpack_raster_grads(int n, const float* raster_grads, float* dL_dtransMat, float* dL_dnormal3D,
+                                float* dL_dcolors, float* dL_dopacity, cudaStream_t s);
+
+}  // namespace msplat

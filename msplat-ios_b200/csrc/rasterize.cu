@@ -1,0 +1,352 @@
+// rasterize.cu — 2DGS tile rasteriser, forward and backward.
+//
+// Forward follows nd_rasterize_forward_2dgs_kernel
+// (core/metal/msplat_metal.metal:553-754): per pixel, front-to-back over the
+// tile's depth-sorted surfels, ray/plane intersection through the surfel's
+// homography, min(rho3d, 2 * d^2) falloff, alpha = min(0.99, o * exp(-rho/2)),
+// skip below 1/255, stop when T would drop to 1e-4, plus depth, normal,
+// median-depth and distortion outputs.
+// Backward follows nd_rasterize_backward_2dgs_kernel (:1705-1979): reverse
+// traversal recovering T as T / (1 - alpha).
+//
+// B200 design: one 256-thread CTA per 16x16 tile (the reference runs four
+// 8x8 groups per tile, each re-reading the tile list); the tile's surfels are
+// streamed in batches of 256: ids are read coalesced, the 80-byte per-Gaussian
+// records (written once by the projection) are gathered into shared memory
+// structure-of-arrays, and every thread walks the batch. In the backward the
+// per-(pixel, surfel) gradients are summed across the warp with a recursive
+// halving exchange (16 values in 16 shuffles), across warps in shared memory,
+// and leave the CTA as four float4 atomics per surfel.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace msplat {
+namespace {
+
+constexpr int kThreads = 256;
+
+struct Pair {
+    float u, v, pz, rho3d, rho2d, depth, G, alpha;
+    float kx, ky, kz, lx, ly, lz;
+};
+
+// Per-(pixel, surfel) evaluation with a pinned IEEE operation sequence
+// (identical in the forward and the backward replay, and in the CPU checker).
+__device__ __forceinline__ bool eval_pair(float px, float py, float4 r0, float4 r1, float4 r2, Pair& e) {
+    // Tu = r0.xyz, Tv = (r0.w, r1.x, r1.y), Tw = (r1.z, r1.w, r2.x), xy = r2.yz, opacity = r2.w
+    const float kx = ffma(px, r1.z, -r0.x), ky = ffma(px, r1.w, -r0.y), kz = ffma(px, r2.x, -r0.z);
+    const float lx = ffma(py, r1.z, -r0.w), ly = ffma(py, r1.w, -r1.x), lz = ffma(py, r2.x, -r1.y);
+    const float p_x = ffma(ky, lz, -fmul(kz, ly));
+    const float p_y = ffma(kz, lx, -fmul(kx, lz));
+    const float p_z = ffma(kx, ly, -fmul(ky, lx));
+    if (p_z == 0.0f) return false;
+    const float inv_z = __frcp_rn(p_z);
+    const float u = fmul(p_x, inv_z), v = fmul(p_y, inv_z);
+    const float rho3d = ffma(u, u, fmul(v, v));
+    const float dx = fsub(r2.y, px), dy = fsub(r2.z, py);
+    const float rho2d = fmul(kFilterInvSq, ffma(dx, dx, fmul(dy, dy)));
+    const float rho = (rho2d < rho3d) ? rho2d : rho3d;
+    const float depth = ffma(u, r1.z, ffma(v, r1.w, r2.x));
+    if (depth < kNearN) return false;
+    const float power = fmul(-0.5f, rho);
+    if (power > 0.0f) return false;
+    const float G = det_exp(power);
+    const float og = fmul(r2.w, G);
+    const float alpha = (og < 0.99f) ? og : 0.99f;
+    if (alpha < 1.0f / 255.0f) return false;
+    e.u = u; e.v = v; e.pz = p_z; e.rho3d = rho3d; e.rho2d = rho2d; e.depth = depth; e.G = G; e.alpha = alpha;
+    e.kx = kx; e.ky = ky; e.kz = kz; e.lx = lx; e.ly = ly; e.lz = lz;
+    return true;
+}
+
+__global__ void __launch_bounds__(kThreads) k_raster_fwd(RasterFwdArgs a) {
+    __shared__ float4 srec[kRecordF4][kThreads];
+    const int tile = (a.tile_row_begin + blockIdx.y) * a.tiles_x + blockIdx.x;
+    const int lx = threadIdx.x & 15, ly = threadIdx.x >> 4;
+    const int j = blockIdx.x * kTile + lx;
+    const int i = (a.tile_row_begin + blockIdx.y) * kTile + ly;
+    const bool inside = (i < a.height) && (j < a.width);
+    const float px = (float)j, py = (float)i;
+    const int2 range = a.tile_bins[tile];
+    const float mscale = __fdiv_rn(kFarN, __fsub_rn(kFarN, kNearN));
+
+    float T = 1.f, cr = 0.f, cg = 0.f, cb = 0.f, nx = 0.f, ny = 0.f, nz = 0.f, pdepth = 0.f;
+    float M1 = 0.f, M2 = 0.f, dist = 0.f, median_depth = 0.f;
+    int median_c = -1, contributor = 0, last_c = 0;
+    bool done = !inside;
+
+    for (int b0 = range.x; b0 < range.y; b0 += kThreads) {
+        if (__syncthreads_count(done) == kThreads) break;
+        const int idx = b0 + threadIdx.x;
+        if (idx < range.y) {
+            const int g = a.gaussian_ids[idx];
+            const float4* r = a.records + (size_t)g * kRecordF4;
+#pragma unroll
+            for (int k = 0; k < kRecordF4; ++k) srec[k][threadIdx.x] = __ldg(r + k);
+        }
+        __syncthreads();
+        if (done) continue;
+        const int bs = min(kThreads, range.y - b0);
+        for (int s = 0; s < bs; ++s) {
+            contributor++;
+            Pair e;
+            const float4 r2 = srec[2][s];
+            if (!eval_pair(px, py, srec[0][s], srec[1][s], r2, e)) continue;
+            const float next_T = fmul(T, fsub(1.0f, e.alpha));
+            if (next_T <= 1e-4f) {
+                done = true;
+                break;
+            }
+            const float w = fmul(e.alpha, T);
+            const float A = fsub(1.f, T);
+            const float m = fmul(mscale, fsub(1.f, __fdiv_rn(kNearN, e.depth)));
+            const float mm = fmul(m, m);
+            dist = ffma(fsub(fadd(fmul(mm, A), M2), fmul(fmul(2.f, m), M1)), w, dist);
+            M1 = ffma(m, w, M1);
+            M2 = ffma(mm, w, M2);
+            if (T > 0.5f) {
+                median_depth = e.depth;
+                median_c = contributor;
+            }
+            const float4 r3 = srec[3][s], r4 = srec[4][s];
+            cr = ffma(r3.x, w, cr);
+            cg = ffma(r3.y, w, cg);
+            cb = ffma(r3.z, w, cb);
+            pdepth = ffma(e.depth, w, pdepth);
+            nx = ffma(r3.w, w, nx);
+            ny = ffma(r4.x, w, ny);
+            nz = ffma(r4.y, w, nz);
+            T = next_T;
+            last_c = contributor;
+        }
+    }
+    if (!inside) return;
+    const size_t pix = (size_t)i * a.width + j;
+    a.final_Ts[3 * pix + 0] = T;
+    a.final_Ts[3 * pix + 1] = M1;
+    a.final_Ts[3 * pix + 2] = M2;
+    a.final_idx[2 * pix + 0] = last_c;
+    a.final_idx[2 * pix + 1] = median_c;
+    a.out_img[3 * pix + 0] = ffma(a.bg[0], T, cr);
+    a.out_img[3 * pix + 1] = ffma(a.bg[1], T, cg);
+    a.out_img[3 * pix + 2] = ffma(a.bg[2], T, cb);
+    a.out_depth[pix] = pdepth;
+    a.out_normal[3 * pix + 0] = nx;
+    a.out_normal[3 * pix + 1] = ny;
+    a.out_normal[3 * pix + 2] = nz;
+    a.out_alpha[pix] = fsub(1.f, T);
+    a.out_median_depth[pix] = median_depth;
+    a.out_distortion[pix] = dist;
+}
+
+// Sums v[0..15] across the warp; afterwards lane L (L even) holds the total of
+// value index L >> 1 (odd lanes hold a copy).
+__device__ __forceinline__ float warp_halving_sum16(float (&v)[16], int lane) {
+    constexpr unsigned full = 0xffffffffu;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const bool up = lane & 16;
+        const float send = up ? v[k] : v[k + 8];
+        const float keep = up ? v[k + 8] : v[k];
+        v[k] = keep + __shfl_xor_sync(full, send, 16);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const bool up = lane & 8;
+        const float send = up ? v[k] : v[k + 4];
+        const float keep = up ? v[k + 4] : v[k];
+        v[k] = keep + __shfl_xor_sync(full, send, 8);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const bool up = lane & 4;
+        const float send = up ? v[k] : v[k + 2];
+        const float keep = up ? v[k + 2] : v[k];
+        v[k] = keep + __shfl_xor_sync(full, send, 4);
+    }
+    {
+        const bool up = lane & 2;
+        const float send = up ? v[0] : v[1];
+        const float keep = up ? v[1] : v[0];
+        v[0] = keep + __shfl_xor_sync(full, send, 2);
+    }
+    v[0] += __shfl_xor_sync(full, v[0], 1);
+    return v[0];
+}
+
+template <bool AUX>
+__global__ void __launch_bounds__(kThreads) k_raster_bwd(RasterBwdArgs a) {
+    __shared__ float4 srec[kRecordF4][kThreads];
+    __shared__ int sid[kThreads];
+    __shared__ float sacc[kThreads][kGradStride];
+    __shared__ int s_max_last;
+    const int lane = threadIdx.x & 31;
+    const int tile_row = a.tile_row_begin + blockIdx.y;
+    const int tile = tile_row * a.tiles_x + blockIdx.x;
+    const int j = blockIdx.x * kTile + (threadIdx.x & 15);
+    const int i = tile_row * kTile + (threadIdx.x >> 4);
+    const bool inside = (i < a.height) && (j < a.width);
+    const float px = (float)j, py = (float)i;
+    const int2 range = a.tile_bins[tile];
+    const size_t pix = inside ? (size_t)i * a.width + j : 0;
+    const float mscale = __fdiv_rn(kFarN, __fsub_rn(kFarN, kNearN));
+
+    float T_final = 0.f, final_D = 0.f, final_D2 = 0.f;
+    int last_c = 0, median_c = -1;
+    float dpix[3] = {0.f, 0.f, 0.f};
+    float dL_ddepth = 0.f, dL_daccum = 0.f, dL_dmed = 0.f, dnorm2[3] = {0.f, 0.f, 0.f};
+    const float dL_dreg = a.dL_dout_distortion;
+    if (inside) {
+        T_final = a.final_Ts[3 * pix];
+        final_D = a.final_Ts[3 * pix + 1];
+        final_D2 = a.final_Ts[3 * pix + 2];
+        last_c = a.final_idx[2 * pix];
+        median_c = a.final_idx[2 * pix + 1];
+        dpix[0] = a.dL_dout_img[3 * pix];
+        dpix[1] = a.dL_dout_img[3 * pix + 1];
+        dpix[2] = a.dL_dout_img[3 * pix + 2];
+        if (AUX) {
+            if (a.dL_dout_depth) dL_ddepth = a.dL_dout_depth[pix];
+            if (a.dL_dout_alpha) dL_daccum = a.dL_dout_alpha[pix];
+            if (a.dL_dout_median_depth) dL_dmed = a.dL_dout_median_depth[pix];
+            if (a.dL_dout_normal)
+                for (int c = 0; c < 3; ++c) dnorm2[c] = a.dL_dout_normal[3 * pix + c];
+        }
+    }
+    if (threadIdx.x == 0) s_max_last = 0;
+    __syncthreads();
+    if (last_c > 0) atomicMax(&s_max_last, last_c);
+    __syncthreads();
+    const int hi = range.x + s_max_last;  // surfels at or past this index never blended
+    const float final_A = 1.0f - T_final;
+    const float bg_dot = a.bg[0] * dpix[0] + a.bg[1] * dpix[1] + a.bg[2] * dpix[2];
+
+    float T = T_final;
+    float accum_rec[3] = {0.f, 0.f, 0.f}, last_color[3] = {0.f, 0.f, 0.f}, last_alpha = 0.f;
+    float accum_depth_rec = 0.f, last_depth = 0.f, accum_alpha_rec = 0.f, last_dL_dT = 0.f;
+    float accum_normal_rec[3] = {0.f, 0.f, 0.f}, last_normal[3] = {0.f, 0.f, 0.f};
+
+    for (int bend = hi; bend > range.x; bend -= kThreads) {
+        const int bs = min(kThreads, bend - range.x);
+        __syncthreads();
+        if ((int)threadIdx.x < bs) {
+            const int g = a.gaussian_ids[bend - 1 - threadIdx.x];
+            sid[threadIdx.x] = g;
+            const float4* r = a.records + (size_t)g * kRecordF4;
+#pragma unroll
+            for (int k = 0; k < kRecordF4; ++k) srec[k][threadIdx.x] = __ldg(r + k);
+        }
+#pragma unroll
+        for (int k = 0; k < kGradStride; ++k) sacc[threadIdx.x][k] = 0.f;
+        __syncthreads();
+        for (int s = 0; s < bs; ++s) {
+            const int rel = bend - 1 - s - range.x;
+            float g[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) g[k] = 0.f;
+            bool contrib = false;
+            Pair e;
+            const float4 r0 = srec[0][s], r1 = srec[1][s], r2 = srec[2][s];
+            if (rel < last_c && eval_pair(px, py, r0, r1, r2, e)) {
+                contrib = true;
+                const float4 r3 = srec[3][s], r4 = srec[4][s];
+                const float alpha = e.alpha, G = e.G, opa = r2.w;
+                T = T / (1.0f - alpha);
+                const float w = alpha * T;
+                float dL_dalpha = 0.f;
+                const float col[3] = {r3.x, r3.y, r3.z};
+#pragma unroll
+                for (int c = 0; c < 3; ++c) {
+                    accum_rec[c] = last_alpha * last_color[c] + (1.f - last_alpha) * accum_rec[c];
+                    last_color[c] = col[c];
+                    dL_dalpha += (col[c] - accum_rec[c]) * dpix[c];
+                    g[10 + c] = col[c] > 0.f ? w * dpix[c] : 0.f;
+                }
+                float dL_dz = 0.f;
+                if (AUX) {
+                    const float m_d = mscale * (1.0f - kNearN / e.depth);
+                    const float dmd_dd = (kFarN * kNearN) / ((kFarN - kNearN) * e.depth * e.depth);
+                    if (rel == median_c - 1) dL_dz += dL_dmed;
+                    const float dL_dweight = (final_D2 + m_d * m_d * final_A - 2.0f * m_d * final_D) * dL_dreg;
+                    dL_dalpha += dL_dweight - last_dL_dT;
+                    last_dL_dT = dL_dweight * alpha + (1.0f - alpha) * last_dL_dT;
+                    const float dL_dmd = 2.0f * (T * alpha) * (m_d * final_A - final_D) * dL_dreg;
+                    dL_dz += dL_dmd * dmd_dd;
+                    accum_depth_rec = last_alpha * last_depth + (1.f - last_alpha) * accum_depth_rec;
+                    last_depth = e.depth;
+                    dL_dalpha += (e.depth - accum_depth_rec) * dL_ddepth;
+                    accum_alpha_rec = last_alpha + (1.f - last_alpha) * accum_alpha_rec;
+                    dL_dalpha += (1.0f - accum_alpha_rec) * dL_daccum;
+                    const float nrm[3] = {r3.w, r4.x, r4.y};
+#pragma unroll
+                    for (int c = 0; c < 3; ++c) {
+                        accum_normal_rec[c] = last_alpha * last_normal[c] + (1.f - last_alpha) * accum_normal_rec[c];
+                        last_normal[c] = nrm[c];
+                        dL_dalpha += (nrm[c] - accum_normal_rec[c]) * dnorm2[c];
+                        g[13 + c] = w * dnorm2[c];
+                    }
+                }
+                dL_dalpha *= T;
+                last_alpha = alpha;
+                dL_dalpha += (-T_final / (1.f - alpha)) * bg_dot;
+                const float dL_dG = opa * dL_dalpha;
+                if (AUX) dL_dz += w * dL_ddepth;
+                if (e.rho3d <= e.rho2d) {
+                    const float dsx = -dL_dG * G * e.u + dL_dz * r1.z;
+                    const float dsy = -dL_dG * G * e.v + dL_dz * r1.w;
+                    const float dpx = dsx / e.pz, dpy = dsy / e.pz;
+                    const float dpz = -(dpx * e.u + dpy * e.v);
+                    // dk = cross(l, dp), dl = cross(dp, k)
+                    const float dkx = e.ly * dpz - e.lz * dpy, dky = e.lz * dpx - e.lx * dpz, dkz = e.lx * dpy - e.ly * dpx;
+                    const float dlx = dpy * e.kz - dpz * e.ky, dly = dpz * e.kx - dpx * e.kz, dlz = dpx * e.ky - dpy * e.kx;
+                    g[0] = -dkx; g[1] = -dky; g[2] = -dkz;
+                    g[3] = -dlx; g[4] = -dly; g[5] = -dlz;
+                    g[6] = px * dkx + py * dlx + dL_dz * e.u;
+                    g[7] = px * dky + py * dly + dL_dz * e.v;
+                    g[8] = px * dkz + py * dlz + dL_dz;
+                } else if (AUX) {
+                    g[6] = e.u * dL_dz;
+                    g[7] = e.v * dL_dz;
+                    g[8] = dL_dz;
+                }
+                g[9] = G * dL_dalpha * (opa * (1.0f - opa));
+            }
+            if (__any_sync(0xffffffffu, contrib)) {
+                const float tot = warp_halving_sum16(g, lane);
+                const int vi = lane >> 1;
+                if (!(lane & 1) && (AUX || vi < 13) && tot != 0.f) atomicAdd(&sacc[s][vi], tot);
+            }
+        }
+        __syncthreads();
+        for (int q = threadIdx.x; q < bs * 4; q += kThreads) {
+            const int s = q >> 2, part = q & 3;
+            const float4 v = make_float4(sacc[s][4 * part], sacc[s][4 * part + 1], sacc[s][4 * part + 2],
+                                         sacc[s][4 * part + 3]);
+            if (v.x != 0.f || v.y != 0.f || v.z != 0.f || v.w != 0.f)
+                atomicAdd(reinterpret_cast<float4*>(a.raster_grads + (size_t)sid[s] * kGradStride) + part, v);
+        }
+    }
+}
+
+}  // namespace
+
+void launch_rasterize_forward(const RasterFwdArgs& a, cudaStream_t s) {
+    const int rows = a.tile_row_end - a.tile_row_begin;
+    if (rows <= 0 || a.tiles_x <= 0) return;
+    note_launches(1);
+    k_raster_fwd<<<dim3(a.tiles_x, rows), kThreads, 0, s>>>(a);
+}
+
+void launch_rasterize_backward(const RasterBwdArgs& a, cudaStream_t s) {
+    const int rows = a.tile_row_end - a.tile_row_begin;
+    if (rows <= 0 || a.tiles_x <= 0) return;
+    const bool aux = a.dL_dout_depth || a.dL_dout_alpha || a.dL_dout_normal || a.dL_dout_median_depth ||
+                     a.dL_dout_distortion != 0.0f;
+    note_launches(1);
+    if (aux)
+        k_raster_bwd<true><<<dim3(a.tiles_x, rows), kThreads, 0, s>>>(a);
+    else
+        k_raster_bwd<false><<<dim3(a.tiles_x, rows), kThreads, 0, s>>>(a);
+}
+
+}  // namespace msplat

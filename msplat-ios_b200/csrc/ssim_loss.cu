@@ -1,0 +1,230 @@
+// ssim_loss.cu — fused L1 + DSSIM loss, forward and backward, in one pass.
+//
+// Replaces the reference's 21-dispatch chain (core/metal/msplat_metal.mm:
+// 1077-1212): ssim_prep_products_kernel, 5 x (ssim_blur_horiz_kernel +
+// ssim_blur_vert_kernel), ssim_compute_kernel, loss_l1_distortion_2dgs_kernel,
+// ssim_backward_compute_kernel, 3 x re-blur and ssim_backward_accumulate_kernel
+// (core/metal/msplat_metal.metal:2704-3085). Same mathematics: 11-tap
+// sigma-1.5 separable window with zero padding, C1 = 1e-4, C2 = 9e-4,
+// dL/dssim = -lambda_dssim / (3HW) uniform, dL/dimg = lambda_l1 * sign(r-g) /
+// (3HW) + blur(g_mu1) + 2 img blur(g_sigma1^2) + gt blur(g_sigma12).
+//
+// One CTA produces a 32x16 tile of dL/dimg for one channel at a time: it
+// stages the rendered and target images with a 10-pixel halo in shared
+// memory, blurs the five moment maps horizontally then vertically over a
+// 5-pixel halo, evaluates SSIM and its per-pixel partials there (zero outside
+// the image, as the adjoint of zero padding requires), and blurs the partials
+// back to the tile. The image and target are read once (plus halo) and
+// dL/dimg is written once; no [H,W,3] intermediate touches HBM. Loss partial
+// sums are reduced per CTA in double and summed in a fixed order afterwards.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace msplat {
+namespace {
+
+__constant__ float kW[11] = {0.001028380084f, 0.007598758135f, 0.036000772128f, 0.109360689510f,
+                             0.213005537711f, 0.266011724862f, 0.213005537711f, 0.109360689510f,
+                             0.036000772128f, 0.007598758135f, 0.001028380084f};
+
+constexpr int OW = 32, OH = 16, R = 5;
+constexpr int IW = OW + 4 * R, IH = OH + 4 * R;  // input region (halo 10)
+constexpr int PW = OW + 2 * R, PH = OH + 2 * R;  // partial region (halo 5)
+constexpr int kThreads = 256;
+constexpr int kSmemFloats = 2 * IH * IW + 5 * IH * PW + 3 * PH * PW + 3 * PH * OW;
+
+__global__ void __launch_bounds__(kThreads) k_loss_ssim(LossArgs a) {
+    extern __shared__ float sm[];
+    float* sI = sm;                     // [IH][IW]
+    float* sG = sI + IH * IW;           // [IH][IW]
+    float* hb = sG + IH * IW;           // [5][IH][PW]
+    float* pmap = hb + 5 * IH * PW;     // [3][PH][PW]
+    float* hp = pmap + 3 * PH * PW;     // [3][PH][OW]
+    const int W = a.width, H = a.height;
+    const int x0 = blockIdx.x * OW;
+    const int y0 = a.row_begin + blockIdx.y * OH;
+    const float C1 = 0.0001f, C2 = 0.0009f;
+    const float g = -a.lambda_dssim * a.inv_num;
+    double l1_sum = 0.0, ssim_sum = 0.0, dist_sum = 0.0;
+
+    for (int c = 0; c < 3; ++c) {
+        for (int q = threadIdx.x; q < IH * IW; q += kThreads) {
+            const int r = q / IW, cc = q - r * IW;
+            const int y = y0 - 2 * R + r, x = x0 - 2 * R + cc;
+            float vi = 0.f, vg = 0.f;
+            if (y >= 0 && y < H && x >= 0 && x < W) {
+                const size_t e = ((size_t)y * W + x) * 3 + c;
+                vi = a.out_img[e];
+                vg = a.gt[e];
+            }
+            sI[q] = vi;
+            sG[q] = vg;
+        }
+        __syncthreads();
+        // Horizontal blur of img, gt, img^2, gt^2, img*gt.
+        for (int q = threadIdx.x; q < IH * PW; q += kThreads) {
+            const int r = q / PW, cc = q - r * PW;
+            float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f, m4 = 0.f;
+            const float* pi = sI + r * IW + cc;
+            const float* pg = sG + r * IW + cc;
+#pragma unroll
+            for (int k = 0; k < 11; ++k) {
+                const float w = kW[k], x = pi[k], y = pg[k];
+                m0 += w * x;
+                m1 += w * y;
+                m2 += w * (x * x);
+                m3 += w * (y * y);
+                m4 += w * (x * y);
+            }
+            hb[0 * IH * PW + q] = m0;
+            hb[1 * IH * PW + q] = m1;
+            hb[2 * IH * PW + q] = m2;
+            hb[3 * IH * PW + q] = m3;
+            hb[4 * IH * PW + q] = m4;
+        }
+        __syncthreads();
+        // Vertical blur -> SSIM and its partials on the halo-5 region.
+        for (int q = threadIdx.x; q < PH * PW; q += kThreads) {
+            const int r = q / PW, cc = q - r * PW;
+            const int y = y0 - R + r, x = x0 - R + cc;
+            float mu1 = 0.f, mu2 = 0.f, b11 = 0.f, b22 = 0.f, b12 = 0.f;
+#pragma unroll
+            for (int k = 0; k < 11; ++k) {
+                const float w = kW[k];
+                const int o = (r + k) * PW + cc;
+                mu1 += w * hb[0 * IH * PW + o];
+                mu2 += w * hb[1 * IH * PW + o];
+                b11 += w * hb[2 * IH * PW + o];
+                b22 += w * hb[3 * IH * PW + o];
+                b12 += w * hb[4 * IH * PW + o];
+            }
+            float gm1 = 0.f, gs1 = 0.f, g12 = 0.f;
+            if (y >= 0 && y < H && x >= 0 && x < W) {
+                const float m1s = mu1 * mu1, m2s = mu2 * mu2, m1m2 = mu1 * mu2;
+                const float v1 = b11 - m1s, v2 = b22 - m2s, v12 = b12 - m1m2;
+                const float A = 2.0f * m1m2 + C1, B = 2.0f * v12 + C2;
+                const float Cd = m1s + m2s + C1, Dd = v1 + v2 + C2;
+                const float CD = Cd * Dd, AB = A * B;
+                const bool own = r >= R && r < R + OH && cc >= R && cc < R + OW && y < a.row_end;
+                if (own) ssim_sum += (double)(AB / CD);
+                const float inv_CD = 1.0f / CD, inv_Cd = 1.0f / Cd, inv_Dd = 1.0f / Dd;
+                const float d_mu1 = 2.0f * inv_CD * (mu2 * B - mu1 * AB * inv_Cd);
+                const float d_s12 = 2.0f * A * inv_CD;
+                const float d_s1 = -AB * inv_CD * inv_Dd;
+                gs1 = g * d_s1;
+                g12 = g * d_s12;
+                gm1 = g * d_mu1 + gs1 * (-2.0f * mu1) + g12 * (-mu2);
+            }
+            pmap[0 * PH * PW + q] = gm1;
+            pmap[1 * PH * PW + q] = gs1;
+            pmap[2 * PH * PW + q] = g12;
+        }
+        __syncthreads();
+        for (int q = threadIdx.x; q < PH * OW; q += kThreads) {
+            const int r = q / OW, cc = q - r * OW;
+            float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+#pragma unroll
+            for (int k = 0; k < 11; ++k) {
+                const float w = kW[k];
+                const int o = r * PW + cc + k;
+                s0 += w * pmap[0 * PH * PW + o];
+                s1 += w * pmap[1 * PH * PW + o];
+                s2 += w * pmap[2 * PH * PW + o];
+            }
+            hp[0 * PH * OW + q] = s0;
+            hp[1 * PH * OW + q] = s1;
+            hp[2 * PH * OW + q] = s2;
+        }
+        __syncthreads();
+        for (int q = threadIdx.x; q < OH * OW; q += kThreads) {
+            const int r = q / OW, cc = q - r * OW;
+            const int y = y0 + r, x = x0 + cc;
+            if (y >= a.row_end || y >= H || x >= W) continue;
+            float bm1 = 0.f, bs1 = 0.f, b12 = 0.f;
+#pragma unroll
+            for (int k = 0; k < 11; ++k) {
+                const float w = kW[k];
+                const int o = (r + k) * OW + cc;
+                bm1 += w * hp[0 * PH * OW + o];
+                bs1 += w * hp[1 * PH * OW + o];
+                b12 += w * hp[2 * PH * OW + o];
+            }
+            const float va = sI[(r + 2 * R) * IW + cc + 2 * R];
+            const float vb = sG[(r + 2 * R) * IW + cc + 2 * R];
+            const float diff = va - vb;
+            l1_sum += (double)(a.lambda_l1 * fabsf(diff) * a.inv_num);
+            const float sg = diff > 0.0f ? 1.0f : (diff < 0.0f ? -1.0f : 0.0f);
+            const float l1g = a.lambda_l1 * sg * a.inv_num;
+            const size_t pix = (size_t)y * W + x;
+            a.dL_dout_img[pix * 3 + c] = l1g + (bm1 + 2.0f * va * bs1 + vb * b12);
+            if (c == 0 && a.lambda_dist != 0.f) dist_sum += (double)(a.lambda_dist * a.out_distortion[pix] * (a.inv_num * 3.0f));
+        }
+        __syncthreads();
+    }
+    // Block reduction of the three partial sums in a fixed order.
+    __shared__ double red[3][kThreads];
+    red[0][threadIdx.x] = l1_sum;
+    red[1][threadIdx.x] = ssim_sum;
+    red[2][threadIdx.x] = dist_sum;
+    __syncthreads();
+    for (int off = kThreads / 2; off > 0; off >>= 1) {
+        if ((int)threadIdx.x < off)
+            for (int k = 0; k < 3; ++k) red[k][threadIdx.x] += red[k][threadIdx.x + off];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        const size_t b = (size_t)blockIdx.y * gridDim.x + blockIdx.x;
+        a.partials[3 * b + 0] = red[0][0];
+        a.partials[3 * b + 1] = red[1][0];
+        a.partials[3 * b + 2] = red[2][0];
+    }
+}
+
+__global__ void __launch_bounds__(1024) k_loss_finalize(const double* partials, int nb, float lambda_dssim,
+                                                        float inv_num, double* out, float* loss_f, uint32_t* err) {
+    __shared__ double red[3][1024];
+    double s[3] = {0.0, 0.0, 0.0};
+    for (int b = threadIdx.x; b < nb; b += blockDim.x)
+        for (int k = 0; k < 3; ++k) s[k] += partials[3 * b + k];
+    for (int k = 0; k < 3; ++k) red[k][threadIdx.x] = s[k];
+    __syncthreads();
+    for (int off = blockDim.x / 2; off > 0; off >>= 1) {
+        if ((int)threadIdx.x < off)
+            for (int k = 0; k < 3; ++k) red[k][threadIdx.x] += red[k][threadIdx.x + off];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        const double l1 = red[0][0], ss = red[1][0], dd = red[2][0];
+        const double loss = l1 + dd + (double)lambda_dssim * (1.0 - ss * (double)inv_num);
+        out[0] = loss;
+        out[1] = ss;
+        out[2] = l1;
+        out[3] = dd;
+        if (loss_f) *loss_f = (float)loss;
+        if (!(loss == loss) || loss > 1e300 || loss < -1e300) atomicOr(err, kErrNonFinite);
+    }
+}
+
+}  // namespace
+
+int loss_num_blocks(int width, int row_begin, int row_end) {
+    return ((width + OW - 1) / OW) * ((row_end - row_begin + OH - 1) / OH);
+}
+
+void launch_loss_ssim(const LossArgs& a, cudaStream_t s) {
+    const int rows = a.row_end - a.row_begin;
+    if (rows <= 0) return;
+    dim3 grid((a.width + OW - 1) / OW, (rows + OH - 1) / OH);
+    const size_t smem = sizeof(float) * kSmemFloats;
+    cudaFuncSetAttribute(k_loss_ssim, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    note_launches(1);
+    k_loss_ssim<<<grid, kThreads, smem, s>>>(a);
+}
+
+void launch_loss_finalize(const double* partials, int num_blocks, float lambda_dssim, float inv_num, double* out,
+                          float* loss_f, uint32_t* err, cudaStream_t s) {
+    note_launches(1);
+    k_loss_finalize<<<1, 1024, 0, s>>>(partials, num_blocks, lambda_dssim, inv_num, out, loss_f, err);
+}
+
+}  // namespace msplat

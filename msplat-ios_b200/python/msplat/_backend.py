@@ -1,0 +1,286 @@
+"""ctypes binding of include/msplat_backend.h (libmsplat_b200.so).
+
+Torch is used here only for device memory and streams: tensors are passed to
+the C ABI as raw device pointers. There is no CPU or PyTorch fallback: if the
+CUDA library is missing or a call fails, an exception is raised.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+_ROOT = os.path.dirname(os.path.dirname(_PKG))  # msplat-ios_b200/
+LIB_PATH = os.path.join(_ROOT, "lib", "libmsplat_b200.so")
+
+MSPLAT_OK = 0
+
+
+class MsplatError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"msplat error {code}: {msg}")
+        self.code = code
+
+
+class MsplatCamera(C.Structure):
+    _fields_ = [("viewmat", C.c_float * 16), ("projmat", C.c_float * 16), ("fx", C.c_float), ("fy", C.c_float),
+                ("cx", C.c_float), ("cy", C.c_float), ("width", C.c_int32), ("height", C.c_int32),
+                ("cam_pos", C.c_float * 3)]
+
+
+class MsplatGaussians(C.Structure):
+    _fields_ = [("num_points", C.c_int32), ("sh_degree", C.c_int32), ("means", C.c_void_p), ("scales", C.c_void_p),
+                ("quats", C.c_void_p), ("opacities", C.c_void_p), ("features_dc", C.c_void_p),
+                ("features_rest", C.c_void_p)]
+
+
+class MsplatAdamState(C.Structure):
+    _fields_ = [("exp_avg", C.c_void_p * 6), ("exp_avg_sq", C.c_void_p * 6), ("lr", C.c_float * 6),
+                ("step", C.c_int32), ("beta1", C.c_float), ("beta2", C.c_float), ("eps", C.c_float)]
+
+
+class MsplatTensorRef(C.Structure):
+    _fields_ = [("data", C.c_void_p), ("shape", C.c_int64 * 4), ("ndim", C.c_int32), ("dtype", C.c_int32)]
+
+
+_lib = None
+
+
+def lib_path() -> str:
+    return LIB_PATH
+
+
+def load():
+    """Load libmsplat_b200.so (raises if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with `python msplat-ios_b200/build.py`")
+    L = C.CDLL(LIB_PATH)
+    vp, f, i32, i64, u32 = C.c_void_p, C.c_float, C.c_int32, C.c_int64, C.c_uint32
+    fp3 = C.POINTER(C.c_float)
+    L.msplat_render.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), f, f, i32, fp3, vp, vp]
+    L.msplat_train_step_2dgs.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), f, f, i32, fp3, vp,
+                                         f, f, f, vp, vp, vp, f, C.POINTER(C.c_float), vp]
+    L.msplat_fused_adam.argtypes = [vp, vp, vp, vp, u32, f, f, f, f, f, vp]
+    L.msplat_train_step_fused.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, fp3, vp, f, f,
+                                          f, C.POINTER(MsplatAdamState), vp, vp, vp, vp, i32, vp]
+    L.msplat_shard_forward_backward.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, fp3, vp,
+                                                f, f, f, i32, i32, vp, vp, vp]
+    L.msplat_shard_project_backward_adam.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, vp,
+                                                     i32, i32, C.POINTER(MsplatAdamState), vp, vp, vp, vp]
+    L.msplat_last_tensor.argtypes = [C.c_char_p, C.POINTER(MsplatTensorRef)]
+    L.msplat_last_num_intersections.restype = i64
+    L.msplat_last_status_flags.restype = u32
+    L.msplat_launch_count.restype = i64
+    L.msplat_set_stage_timing.argtypes = [i32]
+    L.msplat_set_stage_timing.restype = C.c_int
+    L.msplat_stage_times.argtypes = [C.POINTER(C.c_double), C.POINTER(C.c_int64), i32]
+    L.msplat_stage_times.restype = i32
+    L.msplat_stage_name.argtypes = [i32]
+    L.msplat_stage_name.restype = C.c_char_p
+    L.msplat_last_error.restype = C.c_char_p
+    for name in ("msplat_render", "msplat_train_step_2dgs", "msplat_fused_adam", "msplat_train_step_fused",
+                 "msplat_shard_forward_backward", "msplat_shard_project_backward_adam", "msplat_last_tensor"):
+        getattr(L, name).restype = C.c_int
+    _lib = L
+    return L
+
+
+def _check(code: int):
+    if code != MSPLAT_OK:
+        raise MsplatError(code, load().msplat_last_error().decode())
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    import torch
+    assert isinstance(t, torch.Tensor) and t.is_cuda and t.is_contiguous() and t.dtype in (
+        torch.float32, torch.int32, torch.float64), (t.dtype, t.device)
+    return t.data_ptr()
+
+
+def _stream(stream=None):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def camera(viewmat, projmat, fx, fy, cx, cy, width, height, cam_pos) -> MsplatCamera:
+    c = MsplatCamera()
+    c.viewmat[:] = [float(x) for x in np.asarray(viewmat, np.float32).reshape(16)]
+    c.projmat[:] = [float(x) for x in np.asarray(projmat, np.float32).reshape(16)]
+    c.fx, c.fy, c.cx, c.cy = float(fx), float(fy), float(cx), float(cy)
+    c.width, c.height = int(width), int(height)
+    c.cam_pos[:] = [float(x) for x in np.asarray(cam_pos, np.float32).reshape(3)]
+    return c
+
+
+def camera_from_oracle(ocam) -> MsplatCamera:
+    """Copy of a camera struct with the same field layout (e.g. the checker's)."""
+    return camera(ocam.viewmat[:], ocam.projmat[:], ocam.fx, ocam.fy, ocam.cx, ocam.cy, ocam.width, ocam.height,
+                  ocam.cam_pos[:])
+
+
+class DeviceGaussians:
+    """Parameters as torch CUDA tensors in the reference layout."""
+
+    def __init__(self, means, scales, quats, opacities, f_dc, f_rest, sh_degree: int, device="cuda"):
+        import torch
+        t = lambda a: torch.as_tensor(np.ascontiguousarray(a, np.float32)).to(device).contiguous()
+        self.means, self.scales, self.quats = t(means), t(scales), t(quats)
+        self.opacities = t(np.asarray(opacities).reshape(-1, 1))
+        self.f_dc = t(f_dc)
+        self.f_rest = t(f_rest)
+        self.sh_degree = sh_degree
+
+    @property
+    def n(self):
+        return self.means.shape[0]
+
+    def groups(self):
+        return [self.means, self.scales, self.quats, self.f_dc, self.f_rest, self.opacities]
+
+    def struct(self) -> MsplatGaussians:
+        g = MsplatGaussians()
+        g.num_points, g.sh_degree = self.n, self.sh_degree
+        g.means, g.scales, g.quats = _ptr(self.means), _ptr(self.scales), _ptr(self.quats)
+        g.opacities, g.features_dc = _ptr(self.opacities), _ptr(self.f_dc)
+        g.features_rest = _ptr(self.f_rest) if self.f_rest.numel() else None
+        return g
+
+
+def _bg(background):
+    return (C.c_float * 3)(*[float(x) for x in np.asarray(background, np.float32).reshape(3)])
+
+
+def render(g: DeviceGaussians, cam: MsplatCamera, degrees_to_use: int, background, out_img=None, glob_scale=1.0,
+           clip_thresh=0.01, stream=None):
+    gs = g.struct()
+    _check(load().msplat_render(C.byref(gs), C.byref(cam), glob_scale, clip_thresh, degrees_to_use, _bg(background),
+                                _ptr(out_img), _stream(stream)))
+
+
+def train_step_2dgs(g: DeviceGaussians, cam: MsplatCamera, degrees_to_use: int, background, gt, lambda_l1,
+                    lambda_dist, lambda_dssim, stats=None, glob_scale=1.0, clip_thresh=0.01, stream=None) -> float:
+    gs = g.struct()
+    loss = C.c_float()
+    sp = [None, None, None] if stats is None else [_ptr(s) for s in stats]
+    inv_max_dim = 1.0 / max(cam.width, cam.height)
+    _check(load().msplat_train_step_2dgs(C.byref(gs), C.byref(cam), glob_scale, clip_thresh, degrees_to_use,
+                                         _bg(background), _ptr(gt), lambda_l1, lambda_dist, lambda_dssim, sp[0], sp[1],
+                                         sp[2], inv_max_dim, C.byref(loss), _stream(stream)))
+    return loss.value
+
+
+def fused_adam(params, grads, m, v, step_size, beta1, beta2, bc2_sqrt, eps, stream=None):
+    _check(load().msplat_fused_adam(_ptr(params), _ptr(grads), _ptr(m), _ptr(v), params.numel(), step_size, beta1,
+                                    beta2, bc2_sqrt, eps, _stream(stream)))
+
+
+class AdamState:
+    LR_INIT = (0.00016, 0.005, 0.001, 0.0025, 0.000125, 0.05)  # model.cpp:142
+
+    def __init__(self, g: DeviceGaussians):
+        import torch
+        self.m = [torch.zeros_like(p) for p in g.groups()]
+        self.v = [torch.zeros_like(p) for p in g.groups()]
+        self.lr = list(self.LR_INIT)
+        self.step = 0
+        self.beta1, self.beta2, self.eps = 0.9, 0.999, 1e-8
+
+    def struct(self) -> MsplatAdamState:
+        a = MsplatAdamState()
+        for k in range(6):
+            a.exp_avg[k] = _ptr(self.m[k]) if self.m[k].numel() else None
+            a.exp_avg_sq[k] = _ptr(self.v[k]) if self.v[k].numel() else None
+            a.lr[k] = self.lr[k]
+        a.step, a.beta1, a.beta2, a.eps = self.step, self.beta1, self.beta2, self.eps
+        return a
+
+
+def train_step_fused(g: DeviceGaussians, cam: MsplatCamera, degrees_to_use: int, background, gt, lambda_l1,
+                     lambda_dist, lambda_dssim, adam: AdamState, stats=None, loss_dev=None, write_grads=False,
+                     stream=None):
+    gs = g.struct()
+    adam.step += 1
+    st = adam.struct()
+    sp = [None, None, None] if stats is None else [_ptr(s) for s in stats]
+    _check(load().msplat_train_step_fused(C.byref(gs), C.byref(cam), degrees_to_use, _bg(background), _ptr(gt),
+                                          lambda_l1, lambda_dist, lambda_dssim, C.byref(st), sp[0], sp[1], sp[2],
+                                          _ptr(loss_dev), 1 if write_grads else 0, _stream(stream)))
+
+
+def shard_forward_backward(g, cam, degrees_to_use, background, gt, lambda_l1, lambda_dist, lambda_dssim, row0, row1,
+                           raster_grads, loss_parts, stream=None):
+    gs = g.struct()
+    _check(load().msplat_shard_forward_backward(C.byref(gs), C.byref(cam), degrees_to_use, _bg(background), _ptr(gt),
+                                                lambda_l1, lambda_dist, lambda_dssim, row0, row1, _ptr(raster_grads),
+                                                _ptr(loss_parts), _stream(stream)))
+
+
+def shard_project_backward_adam(g, cam, degrees_to_use, raster_grads, g0, g1, adam: AdamState, stats=None,
+                                stream=None):
+    gs = g.struct()
+    st = adam.struct()
+    sp = [None, None, None] if stats is None else [_ptr(s) for s in stats]
+    _check(load().msplat_shard_project_backward_adam(C.byref(gs), C.byref(cam), degrees_to_use, _ptr(raster_grads),
+                                                     g0, g1, C.byref(st), sp[0], sp[1], sp[2], _stream(stream)))
+
+
+_DT = {0: "float32", 1: "int32", 2: "int64"}
+
+
+def last_tensor(name: str):
+    """A torch view of a workspace tensor of the last call (aliases device memory)."""
+    import torch
+    ref = MsplatTensorRef()
+    _check(load().msplat_last_tensor(name.encode(), C.byref(ref)))
+    shape = tuple(ref.shape[k] for k in range(ref.ndim))
+    dtype = {0: torch.float32, 1: torch.int32, 2: torch.int64}[ref.dtype]
+    numel = int(np.prod(shape)) if shape else 1
+    if numel == 0:
+        return torch.empty(shape, dtype=dtype, device="cuda")
+    # Wrap the raw pointer without copying via the CUDA array interface.
+    itemsize = torch.empty((), dtype=dtype).element_size()
+
+    class _Holder:
+        __cuda_array_interface__ = {"shape": shape, "typestr": {torch.float32: "<f4", torch.int32: "<i4",
+                                                                 torch.int64: "<i8"}[dtype],
+                                    "data": (ref.data, False), "version": 2,
+                                    "strides": None}
+
+    t = torch.as_tensor(_Holder(), device="cuda")
+    assert t.element_size() == itemsize
+    return t
+
+
+def last_num_intersections() -> int:
+    return load().msplat_last_num_intersections()
+
+
+def last_status_flags() -> int:
+    return load().msplat_last_status_flags()
+
+
+def launch_count() -> int:
+    return load().msplat_launch_count()
+
+
+def set_stage_timing(enable: bool):
+    _check(load().msplat_set_stage_timing(1 if enable else 0))
+
+
+def stage_times() -> dict:
+    """{stage name: (total ms, samples)} accumulated since set_stage_timing(True)."""
+    L = load()
+    ms = (C.c_double * 16)()
+    cnt = (C.c_int64 * 16)()
+    k = L.msplat_stage_times(ms, cnt, 16)
+    if k < 0:
+        raise MsplatError(2, L.msplat_last_error().decode())
+    return {L.msplat_stage_name(i).decode(): (ms[i], cnt[i]) for i in range(k)}
