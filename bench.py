@@ -1,0 +1,357 @@
+"""Benchmark of the 2DGS training step (BASELINE.json metric: train iters/s and
+fwd+bwd Mpix/s at 3M Gaussians, 4946x3286, SH degree 3 = config 3).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
+
+One step = one full training iteration (projection, binning, sort, rasterise,
+SSIM+L1 loss, backward, Adam on all six groups) for one ring camera, cycling
+through the cameras. Inputs are seeded synthetic scenes with the shapes and
+distributions of the configuration (no dataset is available here).
+
+value: iters/s with parameters, Adam state and target images resident in HBM
+       (inputs are larger than L2), timed with CUDA events on the launch stream,
+       max over ranks.
+e2e:   the same metric through the C ABI with the step's target image copied
+       host->device from pinned memory and the loss read back every step.
+
+N > 1 (torchrun, one process per GPU): image tile rows are sharded across
+ranks (strong scaling: the image and the Gaussian set are fixed), per-Gaussian
+raster gradients are reduce-scattered with NCCL, each rank runs the
+projection VJP + Adam on its slice of Gaussians, and the updated parameters
+are all-gathered.
+
+--impl reference: the CPU oracle (a restatement of the reference's Metal
+kernels; the Metal code cannot run here) timed on the host cores on a bounded
+sample of every step (see oracle.h: orc_time_step_sample).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+sys.path.insert(0, os.path.join(REPO, "msplat-ios_b200", "python"))
+
+import numpy as np  # noqa: E402
+
+METRIC = "train iters/sec (3M Gaussians, 4946x3286, SH3)"
+SSIM_WEIGHT = 0.2
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"msplat_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- scene
+def build_scene(cfg_id: int):
+    from msplat import synthetic as S
+    cfg = S.CONFIGS[cfg_id]
+    scene = S.make_scene(cfg, seed=0)
+    return S, cfg, scene
+
+
+def cameras(B, S, cfg, scene):
+    from msplat import camera_setup
+    fx, fy, cx, cy = scene.intrinsics
+    return [camera_setup.prepare_cam(B, scene.cam_to_world[k], fx, fy, cx, cy, cfg.width, cfg.height)
+            for k in range(len(scene.cam_to_world))]
+
+
+# ---------------------------------------------------------------- byte model
+def raster_bwd_bytes(kept: int, n_vis: int, pixels: int) -> int:
+    """Algorithmic HBM bytes of one rasterize_backward launch in this design:
+    4 B per kept intersection (sorted id), 80 B per visible Gaussian (raster
+    record, read once), 32 B per pixel (final T/M1/M2, last/median index,
+    dL/dimg), 64 B read + 64 B written per visible Gaussian (gradient record)."""
+    return 4 * kept + 80 * n_vis + 32 * pixels + 128 * n_vis
+
+
+def raster_fwd_bytes(kept: int, n_vis: int, pixels: int) -> int:
+    """4 B per kept intersection, 80 B per visible Gaussian, 60 B per pixel of
+    outputs (image, T/M1/M2, indices, depth, normal, alpha, median, distortion)."""
+    return 4 * kept + 80 * n_vis + 60 * pixels
+
+
+def run_ours(args, ws, rank, local):
+    import torch
+    import torch.distributed as dist
+    from msplat import _backend as B
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B.load()
+    S, cfg, scene = build_scene(args.config)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=300))
+    cams = cameras(B, S, cfg, scene)
+    C = len(cams)
+    n = cfg.n
+    bg = S.BACKGROUND
+    # targets: render of the jittered scene for every camera (setup, untimed)
+    tgt = B.DeviceGaussians(*scene.jittered().params(), sh_degree=cfg.degree)
+    gts = []
+    for c in cams:
+        img = torch.empty(cfg.height, cfg.width, 3, device=dev)
+        B.render(tgt, c, cfg.degree, bg, out_img=img)
+        gts.append(img)
+    torch.cuda.synchronize()
+    del tgt
+    g = B.DeviceGaussians(*scene.params(), sh_degree=cfg.degree)
+    adam = B.AdamState(g)
+    stats = [torch.zeros(n, device=dev) for _ in range(3)]
+    loss_dev = torch.zeros(1, device=dev)
+    l1, ld = 1.0 - SSIM_WEIGHT, 0.0
+    stream = torch.cuda.current_stream()
+
+    if ws == 1:
+        def step(k):
+            B.train_step_fused(g, cams[k % C], cfg.degree, bg, gts[k % C], l1, ld, SSIM_WEIGHT, adam, stats=stats,
+                               loss_dev=loss_dev)
+    else:
+        from msplat import sharding
+        plan = sharding.ShardPlan(n, (cfg.height + 15) // 16, ws, rank)
+        sharding.pad_gaussians(g, plan.padded)
+        rg = torch.zeros(plan.padded, 16, device=dev)
+        rg_shard = torch.zeros(plan.chunk, 16, device=dev)
+        parts = torch.zeros(3, dtype=torch.float64, device=dev)
+
+        def step(k):
+            sharding.sharded_step(B, dist, g, cams[k % C], cfg.degree, bg, gts[k % C], l1, ld, SSIM_WEIGHT, adam,
+                                  stats, plan, rg, rg_shard, parts)
+
+    for k in range(args.warmup):
+        step(k)
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    launches0 = B.launch_count()
+    B.set_stage_timing(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for k in range(args.steps):
+        step(args.warmup + k)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    launches = B.launch_count() - launches0
+    stage = B.stage_times()
+    B.set_stage_timing(False)
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    if ws > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = 1000.0 / ms
+    pixels = cfg.width * cfg.height
+
+    # roofline of the dominant kernel over the timed region
+    kept = B.last_num_intersections()
+    n_vis = int((B.last_tensor("radii") > 0).sum().item())
+    per_stage = {k: (v[0] / max(v[1], 1)) for k, v in stage.items()}
+    dom = max(per_stage, key=per_stage.get)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    byte_models = {"rasterize_backward": raster_bwd_bytes(kept, n_vis, pixels),
+                   "rasterize_forward": raster_fwd_bytes(kept, n_vis, pixels)}
+    traffic = None
+    try:
+        tr = json.load(open(os.path.join(REPO, "profiles", "traffic.json")))
+        if tr.get("kernel") == dom and tr.get("config") == args.config:
+            traffic = tr.get("bytes_per_launch")
+    except (OSError, ValueError):
+        pass
+    alg = byte_models.get(dom)
+    roof = None
+    if alg is not None:
+        ach = alg / (per_stage[dom] * 1e-3) / 1e9
+        roof = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 2), "peak": hbm_peak, "peak_source": peak_src,
+                "unit": "GB/s", "frac": round(ach / hbm_peak, 5), "traffic": traffic,
+                "algorithmic_bytes": alg, "ms_per_launch": round(per_stage[dom], 4),
+                "pairs_upper_bound_per_s": round(kept * 256 / (per_stage[dom] * 1e-3), 1)}
+
+    # e2e through the C ABI with host buffers
+    e2e = None
+    e2e_steps = args.e2e_steps if args.e2e_steps is not None else min(args.steps, 10)
+    if ws == 1 and e2e_steps > 0:
+        host_gt = [gts[k].cpu().pin_memory() for k in range(min(C, e2e_steps + 1))]
+        dev_gt = torch.empty_like(gts[0])
+        loss_host = torch.zeros(1).pin_memory()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for k in range(e2e_steps):
+            dev_gt.copy_(host_gt[k % len(host_gt)], non_blocking=True)
+            B.train_step_fused(g, cams[k % C], cfg.degree, bg, dev_gt, l1, ld, SSIM_WEIGHT, adam, stats=stats,
+                               loss_dev=loss_dev)
+            loss_host.copy_(loss_dev, non_blocking=True)
+            stream.synchronize()
+        e2e_s = (time.perf_counter() - t0) / e2e_steps
+        e2e = {"value": round(1.0 / e2e_s, 3), "unit": "iters/s", "h2d_bytes_per_step": int(gts[0].numel() * 4),
+               "d2h_bytes_per_step": 4, "steps": e2e_steps,
+               "path": "msplat_train_step_fused (C ABI), target image H2D from pinned memory, loss D2H"}
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(S, cfg, scene, gts[0].cpu().numpy(), steps=1)
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 3), "unit": "iters/s", "n_gpus": ws, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+                "scaling": "strong" if ws > 1 else "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded; shapes/distributions of BASELINE config %d)" % args.config,
+                "config": {"workload": f"config {args.config}: {cfg.n} Gaussians SH{cfg.degree}, "
+                                       f"{cfg.width}x{cfg.height}, {cfg.num_cameras} ring cameras",
+                           "gaussians": cfg.n, "image": [cfg.width, cfg.height], "sh_degree": cfg.degree,
+                           "parallelism": f"tile-row sharding x{ws}" if ws > 1 else "single GPU",
+                           "l2": "inputs larger than L2 (params+Adam state %.1f GB)" % (n * 58 * 12 / 1e9)},
+                "mpix_per_s": round(pixels * value / 1e6, 2),
+                "e2e": e2e, "gpu_launches": int(launches), "clocks": clk, "roofline": roof,
+                "stage_ms": {k: round(v, 4) for k, v in per_stage.items()},
+                "intersections": kept, "visible_gaussians": n_vis, "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_baseline(S, cfg, scene, gt_np, steps=1, warmup=0):
+    """Times the CPU oracle (restatement of the reference kernels) on a bounded
+    sample of one step of the same workload; returns the cpu_baseline dict."""
+    from oracle import oracle as O
+    threads = O.set_threads(0)
+    stride = {0: 1, 1: 1, 2: 4}.get(cfg_id(cfg), 16)
+    fx, fy, cx, cy = scene.intrinsics
+    ocam = O.prepare_cam(scene.cam_to_world[0], fx, fy, cx, cy, cfg.width, cfg.height)
+    tr = O.OracleTrainer(scene.params(), cfg.degree)
+    for _ in range(warmup):
+        tr.time_sample(ocam, gt_np, S.BACKGROUND, stride)
+    ests = []
+    stages = None
+    for _ in range(steps):
+        est, stages = tr.time_sample(ocam, gt_np, S.BACKGROUND, stride)
+        ests.append(est)
+    est = sum(ests) / len(ests)
+    return {"value": round(1.0 / est, 5), "unit": "iters/s", "cores": threads, "kind": "port",
+            "sample": (f"oracle step on config workload: per-Gaussian stages on all {cfg.n} Gaussians, binning "
+                       f"of all tiles, rasteriser fwd/bwd on every {stride}th tile row and SSIM on "
+                       f"{cfg.height // stride} pixel rows, both scaled x{stride}"),
+            "stage_s": [round(x, 3) for x in stages], "est_s_per_step": round(est, 3)}
+
+
+def cfg_id(cfg):
+    from msplat import synthetic as S
+    for k, v in S.CONFIGS.items():
+        if v == cfg:
+            return k
+    return -1
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return
+    import torch  # noqa: F401  (only for parity of the environment)
+    S, cfg, scene = build_scene(args.config)
+    from oracle import oracle as O
+    fx, fy, cx, cy = scene.intrinsics
+    ocam = O.prepare_cam(scene.cam_to_world[0], fx, fy, cx, cy, cfg.width, cfg.height)
+    gt = O.render(scene.jittered().params(), cfg.degree, cfg.degree, S.BACKGROUND, ocam) if cfg.n <= 200_000 \
+        else np.zeros((cfg.height, cfg.width, 3), np.float32) + 0.5
+    cb = cpu_baseline(S, cfg, scene, gt, steps=args.steps, warmup=args.warmup)
+    v = cb["value"]
+    line = {"metric": METRIC, "value": v, "unit": "iters/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(1000.0 / v, 3), "higher_is_better": True,
+            "scaling": "strong" if ws > 1 else "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded; shapes/distributions of BASELINE config %d)" % args.config,
+            "config": {"workload": f"config {args.config}: {cfg.n} Gaussians SH{cfg.degree}, "
+                                   f"{cfg.width}x{cfg.height}", "parallelism": "CPU host cores"},
+            "impl": "reference", "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": "iters/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    ws, rank, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, ws, rank)
+        return
+    run_ours(args, ws, rank, local)
+
+
+if __name__ == "__main__":
+    main()

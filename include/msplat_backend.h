@@ -73,13 +73,24 @@ typedef struct MsplatAdamState {
 } MsplatAdamState;
 
 /* Reference-shaped tensor view returned by msplat_last_tensor. dtype: 0 f32,
- * 1 i32, 2 i64 (metal_tensor.hpp:18-24 numbering). */
+ * 1 i32, 2 i64, 3 f64. */
 typedef struct MsplatTensorRef {
     void* data;
     int64_t shape[4];
     int32_t ndim;
     int32_t dtype;
 } MsplatTensorRef;
+
+/* Model::prepareCam (core/src/model.cpp:500-544) for downscale factor 1: view
+ * matrix from an OpenGL camToWorld (row-major 4x4) with the y/z flip,
+ * perspective with znear 0.001 / zfar 1000 from the intrinsics, camera
+ * position. Host-only; returns MSPLAT_ERR_ARGUMENT on bad input. */
+int msplat_prepare_camera(const float camToWorld[16], float fx, float fy, float cx, float cy, int32_t width,
+                          int32_t height, MsplatCamera* out);
+
+/* Model::schedulersStep (core/src/model.cpp:183-186): log-linear means
+ * learning rate at `step` of `max_steps`. */
+float msplat_means_lr(int32_t step, int32_t max_steps, float lr_init, float lr_final);
 
 /* Replaces msplat_render (core/metal/bindings.h:139-148, impl
  * msplat_metal.mm:545-772): projection, binning, sort and forward
@@ -144,8 +155,10 @@ int msplat_shard_project_backward_adam(const MsplatGaussians* g, const MsplatCam
  * family, core/metal/bindings.h:36-43, 107-131). Names: out_img, out_depth,
  * out_normal, out_alpha, out_median_depth, out_distortion, final_Ts,
  * final_idx, dL_dout_img, radii, depths, xys, transMats, normal_opacity,
- * colors, num_tiles_hit, tile_bins, gaussian_ids, raw_tile_counts and the
- * dL_d* gradients listed above. Returns MSPLAT_ERR_ARGUMENT for an unknown
+ * colors, num_tiles_hit, tile_bins, gaussian_ids, raw_tile_counts, the
+ * dL_d* gradients listed above, loss_partials (f64 [blocks,3]: l1, ssim,
+ * distortion sums per loss block) and loss_terms (f64 [4]: loss, ssim sum,
+ * l1 term, distortion term). Returns MSPLAT_ERR_ARGUMENT for an unknown
  * name or a tensor the last call did not produce. */
 int msplat_last_tensor(const char* name, MsplatTensorRef* out);
 

@@ -82,6 +82,7 @@ struct Workspace {
     // shape bookkeeping of the last call
     int n = 0, K = 0, W = 0, H = 0, tx = 0, ty = 0;
     int64_t kept = 0;
+    int64_t loss_blocks = 0;
     uint32_t flags = 0;
     bool flags_pending = false;       // err word not yet read back
     cudaStream_t last_stream = nullptr;
@@ -266,8 +267,8 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     mark(w, kStProject, s);
     launch_project_forward(pa, s);
     mark(w, kStCounts, s);
-    launch_tile_counts(w.tile_diff.as<int32_t>(), tx, ty, w.raw_counts.as<int32_t>(), w.raw_start.as<int64_t>(),
-                       w.tile_bins.as<int2>(), w.totals.as<int64_t>(), s);
+    launch_tile_counts(w.tile_diff.as<int32_t>(), tx, ty, row0, row1, w.raw_counts.as<int32_t>(),
+                       w.raw_start.as<int64_t>(), w.tile_bins.as<int2>(), w.totals.as<int64_t>(), s);
     // The one host read of the step: buffer sizes for the intersections.
     CK(cudaMemcpyAsync(w.h_totals, w.totals.p, 2 * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
@@ -277,10 +278,10 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     w.raw_keys.ensure((size_t)(raw_total > 0 ? raw_total : 1) * sizeof(uint64_t));
     w.gaussian_ids.ensure((size_t)(kept > 0 ? kept : 1) * sizeof(int32_t));
     mark(w, kStEmit, s);
-    launch_emit_keys(n, w.rects.as<uint2>(), w.depths.as<float>(), tx, w.raw_start.as<int64_t>(),
+    launch_emit_keys(n, w.rects.as<uint2>(), w.depths.as<float>(), tx, row0, row1, w.raw_start.as<int64_t>(),
                      w.fill.as<int32_t>(), w.raw_keys.as<uint64_t>(), s);
     mark(w, kStSort, s);
-    launch_tile_sort(T, w.raw_counts.as<int32_t>(), w.raw_start.as<int64_t>(), w.raw_keys.as<uint64_t>(),
+    launch_tile_sort(row0 * tx, (row1 - row0) * tx, w.raw_counts.as<int32_t>(), w.raw_start.as<int64_t>(), w.raw_keys.as<uint64_t>(),
                      w.tile_bins.as<int2>(), w.gaussian_ids.as<int32_t>(), w.err.as<uint32_t>(), s);
     RasterFwdArgs ra{};
     ra.width = cam.width; ra.height = cam.height; ra.tiles_x = tx; ra.tiles_y = ty;
@@ -306,6 +307,7 @@ void stage_loss(Workspace& w, const CameraDev& cam, const float* gt, float l1, f
     const size_t P = (size_t)cam.width * cam.height;
     w.dL_dout_img.ensure(P * 3 * 4);
     const int nb = loss_num_blocks(cam.width, prow0, prow1);
+    w.loss_blocks = nb;
     w.loss_partials.ensure((size_t)(nb > 0 ? nb : 1) * 3 * sizeof(double));
     w.loss_out.ensure(4 * sizeof(double));
     w.loss_f.ensure(sizeof(float));
@@ -617,6 +619,8 @@ int msplat_last_tensor(const char* name, MsplatTensorRef* out) {
         else if (nm == "dL_dtransMat") set(w.dL_dtransMat, 0, {n, 9}, gr);
         else if (nm == "dL_dnormal3D") set(w.dL_dnormal3D, 0, {n, 3}, gr);
         else if (nm == "dL_dcolors") set(w.dL_dcolors, 0, {n, 3}, gr);
+        else if (nm == "loss_partials") set(w.loss_partials, 3, {w.loss_blocks, 3}, w.have_dimg);
+        else if (nm == "loss_terms") set(w.loss_out, 3, {4}, w.have_dimg);
         else throw Error(MSPLAT_ERR_ARGUMENT, "unknown tensor name '" + nm + "'");
     });
 }

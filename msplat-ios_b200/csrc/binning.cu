@@ -26,7 +26,7 @@ namespace {
 constexpr int kCountThreads = 1024;
 
 __global__ void __launch_bounds__(kCountThreads)
-k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int32_t* __restrict__ raw_counts,
+k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int row0, int row1, int32_t* __restrict__ raw_counts,
               int64_t* __restrict__ raw_start, int2* __restrict__ tile_bins, int64_t* __restrict__ totals) {
     const int dw = tx + 1;
     // Column prefix over y (one thread per tile column).
@@ -38,13 +38,15 @@ k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int32_t* __restr
         }
     }
     __syncthreads();
-    // Row prefix over x (one thread per tile row).
+    // Row prefix over x (one thread per tile row); rows outside the band
+    // [row0, row1) get zero counts so that nothing is emitted for them.
     for (int y = threadIdx.x; y < ty; y += blockDim.x) {
         int run = 0;
         int32_t* row = raw_counts + (size_t)y * tx;
+        const bool in_band = y >= row0 && y < row1;
         for (int x = 0; x < tx; ++x) {
             run += row[x];
-            row[x] = run;
+            row[x] = in_band ? run : 0;
         }
     }
     __syncthreads();
@@ -91,12 +93,13 @@ k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int32_t* __restr
 }
 
 __global__ void __launch_bounds__(256)
-k_emit_keys(int n, const uint2* __restrict__ rects, const float* __restrict__ depths, int tx,
+k_emit_keys(int n, const uint2* __restrict__ rects, const float* __restrict__ depths, int tx, int row0, int row1,
             const int64_t* __restrict__ raw_start, int32_t* __restrict__ fill, uint64_t* __restrict__ keys) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const uint2 r = rects[i];
-    const int x0 = r.x & 0xFFFF, y0 = r.x >> 16, x1 = r.y & 0xFFFF, y1 = r.y >> 16;
+    const int x0 = r.x & 0xFFFF, x1 = r.y & 0xFFFF;
+    const int y0 = max((int)(r.x >> 16), row0), y1 = min((int)(r.y >> 16), row1);
     if (x1 <= x0 || y1 <= y0) return;
     const uint64_t key = ((uint64_t)__float_as_uint(depths[i]) << 32) | (uint64_t)(uint32_t)i;
     for (int y = y0; y < y1; ++y)
@@ -130,12 +133,12 @@ __device__ __forceinline__ void bitonic_sort(uint64_t* data, int n) {
 __global__ void __launch_bounds__(kSortThreads)
 k_tile_sort(const int32_t* __restrict__ raw_counts, const int64_t* __restrict__ raw_start,
             const uint64_t* __restrict__ keys, const int2* __restrict__ tile_bins,
-            int32_t* __restrict__ gaussian_ids, uint32_t* err) {
+            int32_t* __restrict__ gaussian_ids, int tile0, uint32_t* err) {
     __shared__ uint64_t data[kMaxTileElems];
     __shared__ int hist[256];
     __shared__ uint32_t s_prefix;
     __shared__ int s_need, s_count;
-    const int t = blockIdx.x;
+    const int t = tile0 + blockIdx.x;
     const int count = raw_counts[t];
     if (count <= 0) return;
     const uint64_t* src = keys + raw_start[t];
@@ -195,26 +198,26 @@ k_tile_sort(const int32_t* __restrict__ raw_counts, const int64_t* __restrict__ 
 
 }  // namespace
 
-void launch_tile_counts(const int32_t* tile_diff, int tiles_x, int tiles_y, int32_t* raw_counts,
-                        int64_t* raw_start, int2* tile_bins, int64_t* totals, cudaStream_t s) {
+void launch_tile_counts(const int32_t* tile_diff, int tiles_x, int tiles_y, int row0, int row1,
+                        int32_t* raw_counts, int64_t* raw_start, int2* tile_bins, int64_t* totals, cudaStream_t s) {
     note_launches(1);
-    k_tile_counts<<<1, kCountThreads, 0, s>>>(tile_diff, tiles_x, tiles_y, raw_counts, raw_start, tile_bins,
-                                              totals);
+    k_tile_counts<<<1, kCountThreads, 0, s>>>(tile_diff, tiles_x, tiles_y, row0, row1, raw_counts, raw_start,
+                                              tile_bins, totals);
 }
 
-void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x, const int64_t* raw_start,
-                      int32_t* fill, uint64_t* raw_keys, cudaStream_t s) {
+void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x, int row0, int row1,
+                      const int64_t* raw_start, int32_t* fill, uint64_t* raw_keys, cudaStream_t s) {
     if (n <= 0) return;
     note_launches(1);
-    k_emit_keys<<<(n + 255) / 256, 256, 0, s>>>(n, rects, depths, tiles_x, raw_start, fill, raw_keys);
+    k_emit_keys<<<(n + 255) / 256, 256, 0, s>>>(n, rects, depths, tiles_x, row0, row1, raw_start, fill, raw_keys);
 }
 
-void launch_tile_sort(int num_tiles, const int32_t* raw_counts, const int64_t* raw_start,
+void launch_tile_sort(int tile0, int num_tiles, const int32_t* raw_counts, const int64_t* raw_start,
                       const uint64_t* raw_keys, const int2* tile_bins, int32_t* gaussian_ids, uint32_t* err,
                       cudaStream_t s) {
     if (num_tiles <= 0) return;
     note_launches(1);
-    k_tile_sort<<<num_tiles, kSortThreads, 0, s>>>(raw_counts, raw_start, raw_keys, tile_bins, gaussian_ids,
+    k_tile_sort<<<num_tiles, kSortThreads, 0, s>>>(raw_counts, raw_start, raw_keys, tile_bins, gaussian_ids, tile0,
                                                     err);
 }
 

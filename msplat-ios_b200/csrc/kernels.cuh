@@ -68,12 +68,13 @@ void launch_project_backward(const ProjBwdArgs& a, cudaStream_t s);
 
 // ---- binning (binning.cu) ---------------------------------------------------
 // Tile counts from the difference array, kept counts, exclusive scans and the
-// two totals. totals[0] = raw intersections (int64), totals[1] = kept.
-void launch_tile_counts(const int32_t* tile_diff, int tiles_x, int tiles_y, int32_t* raw_counts,
-                        int64_t* raw_start, int2* tile_bins, int64_t* totals, cudaStream_t s);
-void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x,
+// two totals. totals[0] = raw intersections (int64), totals[1] = kept. Only
+// tile rows [row0, row1) are binned; the other rows get empty ranges.
+void launch_tile_counts(const int32_t* tile_diff, int tiles_x, int tiles_y, int row0, int row1,
+                        int32_t* raw_counts, int64_t* raw_start, int2* tile_bins, int64_t* totals, cudaStream_t s);
+void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x, int row0, int row1,
                       const int64_t* raw_start, int32_t* fill, uint64_t* raw_keys, cudaStream_t s);
-void launch_tile_sort(int num_tiles, const int32_t* raw_counts, const int64_t* raw_start,
+void launch_tile_sort(int tile0, int num_tiles, const int32_t* raw_counts, const int64_t* raw_start,
                       const uint64_t* raw_keys, const int2* tile_bins, int32_t* gaussian_ids,
                       uint32_t* err, cudaStream_t s);
 

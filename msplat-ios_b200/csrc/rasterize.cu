@@ -30,21 +30,32 @@ struct Pair {
     float kx, ky, kz, lx, ly, lz;
 };
 
+// Rho above which a surfel of opacity o is certainly skipped by the 1/255
+// alpha cut: o * exp(-rho/2) < 1/255 for rho > 2 ln(255 o); the +0.01 margin
+// covers the rounding of det_exp and of this bound. Negative for o < 1/255.
+__device__ __forceinline__ float reject_rho(float opac) {
+    return opac > 0.f ? 2.0f * logf(255.0f * opac) + 0.01f : -1.0f;
+}
+
 // Per-(pixel, surfel) evaluation with a pinned IEEE operation sequence
 // (identical in the forward and the backward replay, and in the CPU checker).
-__device__ __forceinline__ bool eval_pair(float px, float py, float4 r0, float4 r1, float4 r2, Pair& e) {
+// Before the exact sequence, a pair whose 2-D and 3-D falloff both exceed
+// rmax is rejected without the division and the exponential; such a pair
+// would fail the alpha >= 1/255 test anyway, so results are unchanged.
+__device__ __forceinline__ bool eval_pair(float px, float py, float4 r0, float4 r1, float4 r2, float rmax, Pair& e) {
     // Tu = r0.xyz, Tv = (r0.w, r1.x, r1.y), Tw = (r1.z, r1.w, r2.x), xy = r2.yz, opacity = r2.w
+    const float dx = fsub(r2.y, px), dy = fsub(r2.z, py);
+    const float rho2d = fmul(kFilterInvSq, ffma(dx, dx, fmul(dy, dy)));
     const float kx = ffma(px, r1.z, -r0.x), ky = ffma(px, r1.w, -r0.y), kz = ffma(px, r2.x, -r0.z);
     const float lx = ffma(py, r1.z, -r0.w), ly = ffma(py, r1.w, -r1.x), lz = ffma(py, r2.x, -r1.y);
     const float p_x = ffma(ky, lz, -fmul(kz, ly));
     const float p_y = ffma(kz, lx, -fmul(kx, lz));
     const float p_z = ffma(kx, ly, -fmul(ky, lx));
+    if (rho2d > rmax && p_x * p_x + p_y * p_y > (rmax * 1.0001f) * (p_z * p_z)) return false;
     if (p_z == 0.0f) return false;
     const float inv_z = __frcp_rn(p_z);
     const float u = fmul(p_x, inv_z), v = fmul(p_y, inv_z);
     const float rho3d = ffma(u, u, fmul(v, v));
-    const float dx = fsub(r2.y, px), dy = fsub(r2.z, py);
-    const float rho2d = fmul(kFilterInvSq, ffma(dx, dx, fmul(dy, dy)));
     const float rho = (rho2d < rho3d) ? rho2d : rho3d;
     const float depth = ffma(u, r1.z, ffma(v, r1.w, r2.x));
     if (depth < kNearN) return false;
@@ -59,10 +70,16 @@ __device__ __forceinline__ bool eval_pair(float px, float py, float4 r0, float4 
     return true;
 }
 
+// Pixel of thread t inside its 16x16 tile: each warp covers an 8x4 block, so
+// a small surfel tends to be rejected by whole warps.
+__device__ __forceinline__ int tile_lx(int t) { return ((t >> 5) & 1) * 8 + (t & 7); }
+__device__ __forceinline__ int tile_ly(int t) { return (t >> 6) * 4 + ((t >> 3) & 3); }
+
 __global__ void __launch_bounds__(kThreads) k_raster_fwd(RasterFwdArgs a) {
     __shared__ float4 srec[kRecordF4][kThreads];
+    __shared__ float srmax[kThreads];
     const int tile = (a.tile_row_begin + blockIdx.y) * a.tiles_x + blockIdx.x;
-    const int lx = threadIdx.x & 15, ly = threadIdx.x >> 4;
+    const int lx = tile_lx(threadIdx.x), ly = tile_ly(threadIdx.x);
     const int j = blockIdx.x * kTile + lx;
     const int i = (a.tile_row_begin + blockIdx.y) * kTile + ly;
     const bool inside = (i < a.height) && (j < a.width);
@@ -83,6 +100,7 @@ __global__ void __launch_bounds__(kThreads) k_raster_fwd(RasterFwdArgs a) {
             const float4* r = a.records + (size_t)g * kRecordF4;
 #pragma unroll
             for (int k = 0; k < kRecordF4; ++k) srec[k][threadIdx.x] = __ldg(r + k);
+            srmax[threadIdx.x] = reject_rho(srec[2][threadIdx.x].w);
         }
         __syncthreads();
         if (done) continue;
@@ -91,7 +109,7 @@ __global__ void __launch_bounds__(kThreads) k_raster_fwd(RasterFwdArgs a) {
             contributor++;
             Pair e;
             const float4 r2 = srec[2][s];
-            if (!eval_pair(px, py, srec[0][s], srec[1][s], r2, e)) continue;
+            if (!eval_pair(px, py, srec[0][s], srec[1][s], r2, srmax[s], e)) continue;
             const float next_T = fmul(T, fsub(1.0f, e.alpha));
             if (next_T <= 1e-4f) {
                 done = true;
@@ -177,14 +195,15 @@ __device__ __forceinline__ float warp_halving_sum16(float (&v)[16], int lane) {
 template <bool AUX>
 __global__ void __launch_bounds__(kThreads) k_raster_bwd(RasterBwdArgs a) {
     __shared__ float4 srec[kRecordF4][kThreads];
+    __shared__ float srmax[kThreads];
     __shared__ int sid[kThreads];
     __shared__ float sacc[kThreads][kGradStride];
     __shared__ int s_max_last;
     const int lane = threadIdx.x & 31;
     const int tile_row = a.tile_row_begin + blockIdx.y;
     const int tile = tile_row * a.tiles_x + blockIdx.x;
-    const int j = blockIdx.x * kTile + (threadIdx.x & 15);
-    const int i = tile_row * kTile + (threadIdx.x >> 4);
+    const int j = blockIdx.x * kTile + tile_lx(threadIdx.x);
+    const int i = tile_row * kTile + tile_ly(threadIdx.x);
     const bool inside = (i < a.height) && (j < a.width);
     const float px = (float)j, py = (float)i;
     const int2 range = a.tile_bins[tile];
@@ -235,6 +254,7 @@ __global__ void __launch_bounds__(kThreads) k_raster_bwd(RasterBwdArgs a) {
             const float4* r = a.records + (size_t)g * kRecordF4;
 #pragma unroll
             for (int k = 0; k < kRecordF4; ++k) srec[k][threadIdx.x] = __ldg(r + k);
+            srmax[threadIdx.x] = reject_rho(srec[2][threadIdx.x].w);
         }
 #pragma unroll
         for (int k = 0; k < kGradStride; ++k) sacc[threadIdx.x][k] = 0.f;
@@ -247,7 +267,7 @@ __global__ void __launch_bounds__(kThreads) k_raster_bwd(RasterBwdArgs a) {
             bool contrib = false;
             Pair e;
             const float4 r0 = srec[0][s], r1 = srec[1][s], r2 = srec[2][s];
-            if (rel < last_c && eval_pair(px, py, r0, r1, r2, e)) {
+            if (rel < last_c && eval_pair(px, py, r0, r1, r2, srmax[s], e)) {
                 contrib = true;
                 const float4 r3 = srec[3][s], r4 = srec[4][s];
                 const float alpha = e.alpha, G = e.G, opa = r2.w;

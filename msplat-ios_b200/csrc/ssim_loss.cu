@@ -100,11 +100,14 @@ __global__ void __launch_bounds__(kThreads) k_loss_ssim(LossArgs a) {
             }
             float gm1 = 0.f, gs1 = 0.f, g12 = 0.f;
             if (y >= 0 && y < H && x >= 0 && x < W) {
-                const float m1s = mu1 * mu1, m2s = mu2 * mu2, m1m2 = mu1 * mu2;
-                const float v1 = b11 - m1s, v2 = b22 - m2s, v12 = b12 - m1m2;
-                const float A = 2.0f * m1m2 + C1, B = 2.0f * v12 + C2;
-                const float Cd = m1s + m2s + C1, Dd = v1 + v2 + C2;
-                const float CD = Cd * Dd, AB = A * B;
+                // Separately rounded operations: sigma1^2, sigma2^2 and sigma12
+                // must round identically where img == gt (flat background),
+                // where the reference's SSIM is exactly 1.
+                const float m1s = fmul(mu1, mu1), m2s = fmul(mu2, mu2), m1m2 = fmul(mu1, mu2);
+                const float v1 = fsub(b11, m1s), v2 = fsub(b22, m2s), v12 = fsub(b12, m1m2);
+                const float A = fadd(fmul(2.0f, m1m2), C1), B = fadd(fmul(2.0f, v12), C2);
+                const float Cd = fadd(fadd(m1s, m2s), C1), Dd = fadd(fadd(v1, v2), C2);
+                const float CD = fmul(Cd, Dd), AB = fmul(A, B);
                 const bool own = r >= R && r < R + OH && cc >= R && cc < R + OW && y < a.row_end;
                 if (own) ssim_sum += (double)(AB / CD);
                 const float inv_CD = 1.0f / CD, inv_Cd = 1.0f / Cd, inv_Dd = 1.0f / Dd;

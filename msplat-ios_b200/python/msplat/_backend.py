@@ -98,6 +98,8 @@ def _check(code: int):
 def _ptr(t):
     if t is None:
         return None
+    if isinstance(t, int):
+        return t
     import torch
     assert isinstance(t, torch.Tensor) and t.is_cuda and t.is_contiguous() and t.dtype in (
         torch.float32, torch.int32, torch.float64), (t.dtype, t.device)
@@ -224,7 +226,11 @@ def shard_forward_backward(g, cam, degrees_to_use, background, gt, lambda_l1, la
 
 
 def shard_project_backward_adam(g, cam, degrees_to_use, raster_grads, g0, g1, adam: AdamState, stats=None,
-                                stream=None):
+                                stream=None, count_step=True):
+    """raster_grads: a [N, 16] tensor, or an int device address such that row i
+    of the gradient record is at address + 64 * i for i in [g0, g1)."""
+    if count_step:
+        adam.step += 1
     gs = g.struct()
     st = adam.struct()
     sp = [None, None, None] if stats is None else [_ptr(s) for s in stats]
@@ -241,7 +247,7 @@ def last_tensor(name: str):
     ref = MsplatTensorRef()
     _check(load().msplat_last_tensor(name.encode(), C.byref(ref)))
     shape = tuple(ref.shape[k] for k in range(ref.ndim))
-    dtype = {0: torch.float32, 1: torch.int32, 2: torch.int64}[ref.dtype]
+    dtype = {0: torch.float32, 1: torch.int32, 2: torch.int64, 3: torch.float64}[ref.dtype]
     numel = int(np.prod(shape)) if shape else 1
     if numel == 0:
         return torch.empty(shape, dtype=dtype, device="cuda")
@@ -250,7 +256,7 @@ def last_tensor(name: str):
 
     class _Holder:
         __cuda_array_interface__ = {"shape": shape, "typestr": {torch.float32: "<f4", torch.int32: "<i4",
-                                                                 torch.int64: "<i8"}[dtype],
+                                                                 torch.int64: "<i8", torch.float64: "<f8"}[dtype],
                                     "data": (ref.data, False), "version": 2,
                                     "strides": None}
 

@@ -10,6 +10,7 @@
 #include "oracle.h"
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -375,26 +376,48 @@ int64_t orc_bin_and_sort(int n, const float* xys, const float* depths, const int
                          const float* aabb, int tiles_x, int tiles_y, int64_t* raw_counts,
                          int32_t* tile_bins, int32_t* gaussian_ids, int64_t capacity) {
     const int T = tiles_x * tiles_y;
-    // Per-tile lists in increasing Gaussian-id order (the scatter of
-    // metal:1557-1591, serialised by id).
-    std::vector<std::vector<uint64_t>> lists(T);
+    // Per-tile candidate lists (the scatter of metal:1557-1591). Filled in
+    // parallel; each list is then put into id order, so the result does not
+    // depend on the fill order.
+    std::vector<int64_t> cnt(T, 0);
+    std::vector<int> rect(4 * (size_t)n, 0);
+#pragma omp parallel for schedule(static)
     for (int i = 0; i < n; ++i) {
         if (radii[i] <= 0) continue;
-        int x0, y0, x1, y1;
-        tile_bbox(xys[2 * i], xys[2 * i + 1], aabb[2 * i], tiles_x, tiles_y, &x0, &y0, &x1, &y1);
+        int* r = &rect[4 * (size_t)i];
+        tile_bbox(xys[2 * i], xys[2 * i + 1], aabb[2 * i], tiles_x, tiles_y, &r[0], &r[1], &r[2], &r[3]);
+        for (int y = r[1]; y < r[3]; ++y)
+            for (int x = r[0]; x < r[2]; ++x) {
+#pragma omp atomic
+                cnt[y * tiles_x + x] += 1;
+            }
+    }
+    std::vector<int64_t> off(T + 1, 0);
+    for (int t = 0; t < T; ++t) off[t + 1] = off[t] + cnt[t];
+    std::vector<uint64_t> keys((size_t)off[T] + 1);
+    std::vector<int64_t> fill(T, 0);
+#pragma omp parallel for schedule(static)
+    for (int i = 0; i < n; ++i) {
+        if (radii[i] <= 0) continue;
+        const int* r = &rect[4 * (size_t)i];
         uint32_t db;
         std::memcpy(&db, &depths[i], 4);
-        uint64_t key = ((uint64_t)db << 32) | (uint64_t)(uint32_t)i;
-        for (int y = y0; y < y1; ++y)
-            for (int x = x0; x < x1; ++x) lists[y * tiles_x + x].push_back(key);
+        const uint64_t key = ((uint64_t)db << 32) | (uint64_t)(uint32_t)i;
+        for (int y = r[1]; y < r[3]; ++y)
+            for (int x = r[0]; x < r[2]; ++x) {
+                const int t = y * tiles_x + x;
+                int64_t slot;
+#pragma omp atomic capture
+                slot = fill[t]++;
+                keys[off[t] + slot] = key;
+            }
     }
     // prefix_sum_kernel over min(count, 2048) (metal:3093-3145); tile_bins
     // (start, end) as written by the sort kernel (metal:1628-1635).
     int64_t running = 0;
     for (int t = 0; t < T; ++t) {
-        int64_t raw = (int64_t)lists[t].size();
-        raw_counts[t] = raw;
-        int64_t kept = std::min<int64_t>(raw, kMaxTileElems);
+        raw_counts[t] = cnt[t];
+        int64_t kept = std::min<int64_t>(cnt[t], kMaxTileElems);
         tile_bins[2 * t] = (int32_t)running;
         running += kept;
         tile_bins[2 * t + 1] = (int32_t)running;
@@ -402,12 +425,18 @@ int64_t orc_bin_and_sort(int n, const float* xys, const float* depths, const int
     if (running > capacity) return -1;
 #pragma omp parallel for schedule(dynamic, 16)
     for (int t = 0; t < T; ++t) {
-        auto& L = lists[t];
-        // Overflow policy: lists are in id order, keep the lowest 2048 ids.
-        if ((int64_t)L.size() > kMaxTileElems) L.resize(kMaxTileElems);
-        std::sort(L.begin(), L.end());  // ascending (depth_bits, id), metal:1649-1664
+        uint64_t* L = keys.data() + off[t];
+        int64_t c = cnt[t];
+        if (c > kMaxTileElems) {
+            // Overflow policy: keep the 2048 lowest Gaussian ids.
+            std::nth_element(L, L + kMaxTileElems, L + c, [](uint64_t a, uint64_t b) {
+                return (uint32_t)a < (uint32_t)b;
+            });
+            c = kMaxTileElems;
+        }
+        std::sort(L, L + c);  // ascending (depth_bits, id), metal:1649-1664
         int32_t start = tile_bins[2 * t];
-        for (size_t k = 0; k < L.size(); ++k) gaussian_ids[start + k] = (int32_t)(L[k] & 0xFFFFFFFFu);
+        for (int64_t k = 0; k < c; ++k) gaussian_ids[start + k] = (int32_t)(L[k] & 0xFFFFFFFFu);
     }
     return running;
 }
@@ -459,6 +488,12 @@ inline bool eval_pair(float px, float py, const float* xy, const float* tm, floa
 }
 }  // namespace
 
+namespace {
+// Tile-row sampling used only by orc_time_step_sample: rows of tiles whose
+// index is not a multiple of g_row_stride are skipped.
+thread_local int g_row_stride = 1;
+}  // namespace
+
 void orc_rasterize_forward(int width, int height, int tiles_x, const int32_t* tile_bins,
                            const float* packed_xy, const float* packed_normal_opac,
                            const float* packed_transmat, const float* packed_rgb,
@@ -466,9 +501,11 @@ void orc_rasterize_forward(int width, int height, int tiles_x, const int32_t* ti
                            float* out_img, float* out_depth, float* out_normal, float* out_alpha,
                            float* out_median_depth, float* out_distortion) {
     const float mscale = kFarN / (kFarN - kNearN);
+    const int row_stride = g_row_stride;
 #pragma omp parallel for schedule(dynamic, 64)
     for (int64_t pix = 0; pix < (int64_t)width * height; ++pix) {
         int i = (int)(pix / width), j = (int)(pix % width);
+        if ((i / kTile) % row_stride != 0) continue;
         int tile = (i / kTile) * tiles_x + (j / kTile);
         float px = (float)j, py = (float)i;
         int start = tile_bins[2 * tile], end = tile_bins[2 * tile + 1];
@@ -621,9 +658,11 @@ void orc_rasterize_backward(int n, int width, int height, int tiles_x, const int
         gO((size_t)n, 0.0), gC((size_t)n * 3, 0.0);
     const float mscale = kFarN / (kFarN - kNearN);
     const int64_t P = (int64_t)width * height;
+    const int row_stride = g_row_stride;
 #pragma omp parallel for schedule(dynamic, 64)
     for (int64_t pix = 0; pix < P; ++pix) {
         int i = (int)(pix / width), j = (int)(pix % width);
+        if ((i / kTile) % row_stride != 0) continue;
         int tile = (i / kTile) * tiles_x + (j / kTile);
         float px = (float)j, py = (float)i;
         int start = tile_bins[2 * tile], end = tile_bins[2 * tile + 1];
@@ -918,6 +957,87 @@ float orc_train_step(const OrcStepArgs* a, const OrcCamera* cam, float* grads_ou
                        a->lr[gi] / bc1, b1, b2, bc2_sqrt, eps);
     }
     return (float)loss;
+}
+
+double orc_time_step_sample(const OrcStepArgs* a, const OrcCamera* cam, int tile_row_stride,
+                            double* stage_seconds) {
+    // Bounded CPU sample of one training step (see oracle.h).
+    using clk = std::chrono::steady_clock;
+    auto secs = [](clk::time_point t0) { return std::chrono::duration<double>(clk::now() - t0).count(); };
+    const int S = tile_row_stride < 1 ? 1 : tile_row_stride;
+    const int n = a->n;
+    const int K = num_sh_bases(a->degree) - 1;
+    const int W = cam->width, H = cam->height, tx = (W + kTile - 1) / kTile, ty = (H + kTile - 1) / kTile;
+    const int64_t P = (int64_t)W * H;
+    double st[7] = {0, 0, 0, 0, 0, 0, 0};
+    Forward F;
+    auto t0 = clk::now();
+    F.xys.resize(2 * (size_t)n); F.depths.resize(n); F.radii.resize(n); F.transmats.resize(9 * (size_t)n);
+    F.tiles_hit.resize(n); F.normal_opacity.resize(4 * (size_t)n); F.colors.resize(3 * (size_t)n);
+    F.aabb.resize(2 * (size_t)n);
+    orc_project_forward(n, a->means, a->scales, 1.0f, a->quats, a->opacities, a->f_dc, a->f_rest, a->degree,
+                        a->degrees_to_use, cam, 0.01f, F.xys.data(), F.depths.data(), F.radii.data(),
+                        F.transmats.data(), F.tiles_hit.data(), F.normal_opacity.data(), F.colors.data(),
+                        F.aabb.data());
+    st[0] = secs(t0);
+    t0 = clk::now();
+    int64_t cap = (int64_t)tx * ty * kMaxTileElems;
+    F.raw.resize((size_t)tx * ty); F.tile_bins.resize(2 * (size_t)tx * ty); F.ids.resize(cap);
+    F.kept = orc_bin_and_sort(n, F.xys.data(), F.depths.data(), F.radii.data(), F.aabb.data(), tx, ty,
+                              F.raw.data(), F.tile_bins.data(), F.ids.data(), cap);
+    int64_t k = std::max<int64_t>(F.kept, 1);
+    F.pxy.resize(2 * k); F.ptm.resize(9 * k); F.pno.resize(4 * k); F.prgb.resize(3 * k);
+    orc_pack(F.kept, F.ids.data(), F.xys.data(), F.transmats.data(), F.normal_opacity.data(), F.colors.data(),
+             F.pxy.data(), F.ptm.data(), F.pno.data(), F.prgb.data());
+    st[1] = secs(t0);
+    F.final_Ts.resize(3 * P); F.final_idx.resize(2 * P); F.out_img.resize(3 * P); F.out_depth.resize(P);
+    F.out_normal.resize(3 * P); F.out_alpha.resize(P); F.out_median.resize(P); F.out_dist.resize(P);
+    g_row_stride = S;
+    t0 = clk::now();
+    orc_rasterize_forward(W, H, tx, F.tile_bins.data(), F.pxy.data(), F.pno.data(), F.ptm.data(), F.prgb.data(),
+                          a->background, F.final_Ts.data(), F.final_idx.data(), F.out_img.data(), F.out_depth.data(),
+                          F.out_normal.data(), F.out_alpha.data(), F.out_median.data(), F.out_dist.data());
+    st[2] = secs(t0) * S;
+    // loss on a band of H/S rows (same per-pixel work), scaled by S
+    const int hb = std::max(1, H / S);
+    std::vector<float> dimg(3 * P, 0.f), ddist(P, 0.f);
+    double loss = 0, ssum = 0;
+    t0 = clk::now();
+    orc_loss_ssim(W, hb, F.out_img.data(), a->gt, F.out_dist.data(), a->lambda_l1, a->lambda_dist, a->lambda_dssim,
+                  dimg.data(), ddist.data(), &loss, &ssum);
+    st[3] = secs(t0) * ((double)H / hb);
+    std::vector<float> zeros1(P, 0.f), zeros3(3 * P, 0.f);
+    std::vector<float> dT(9 * (size_t)n), dM2(2 * (size_t)n), dN(3 * (size_t)n), dO(n), dC(3 * (size_t)n);
+    t0 = clk::now();
+    orc_rasterize_backward(n, W, H, tx, F.tile_bins.data(), F.ids.data(), F.pxy.data(), F.pno.data(), F.ptm.data(),
+                           F.prgb.data(), F.final_Ts.data(), F.final_idx.data(), a->background, dimg.data(),
+                           zeros1.data(), zeros1.data(), zeros3.data(), zeros1.data(), ddist.data(), dT.data(),
+                           dM2.data(), dN.data(), dO.data(), dC.data());
+    st[4] = secs(t0) * S;
+    g_row_stride = 1;
+    std::vector<float> gmean(3 * (size_t)n), gscale(2 * (size_t)n), gquat(4 * (size_t)n), gdc(3 * (size_t)n),
+        grest((size_t)3 * K * n + 1);
+    t0 = clk::now();
+    orc_project_backward(n, a->means, a->scales, 1.0f, a->quats, cam, F.radii.data(), dT.data(), dN.data(), dC.data(),
+                         a->degree, a->degrees_to_use, a->f_rest, gmean.data(), gscale.data(), gquat.data(),
+                         dM2.data(), gdc.data(), grest.data(), a->xys_grad_norm, a->vis_counts, a->max_2d_size,
+                         1.0f / (float)std::max(W, H));
+    st[5] = secs(t0);
+    t0 = clk::now();
+    float* params[6] = {a->means, a->scales, a->quats, a->f_dc, a->f_rest, a->opacities};
+    const float* grads[6] = {gmean.data(), gscale.data(), gquat.data(), gdc.data(), grest.data(), dO.data()};
+    int64_t counts[6] = {3LL * n, 2LL * n, 4LL * n, 3LL * n, 3LL * K * n, (int64_t)n};
+    for (int gi = 0; gi < 6; ++gi)
+        if (counts[gi])
+            orc_fused_adam(params[gi], grads[gi], a->exp_avg[gi], a->exp_avg_sq[gi], counts[gi], a->lr[gi] / 0.1f,
+                           0.9f, 0.999f, 0.0447f, 1e-8f);
+    st[6] = secs(t0);
+    double total = 0;
+    for (int q = 0; q < 7; ++q) {
+        total += st[q];
+        if (stage_seconds) stage_seconds[q] = st[q];
+    }
+    return total;
 }
 
 }  // extern "C"

@@ -159,6 +159,16 @@ void orc_render(int n, const float* means, const float* scales, const float* qua
                 int degree, int degrees_to_use, const float* background,
                 const OrcCamera* cam, float* out_img);
 
+/* Times one training step on a bounded sample of the workload, for the CPU
+ * baseline: projection, binning, projection VJP and Adam on all N Gaussians;
+ * rasterisation forward/backward on every tile_row_stride-th row of tiles and
+ * the loss on a band of H / tile_row_stride pixel rows, both scaled back by
+ * the stride. Parameters are updated in place (values are not checked).
+ * Returns the estimated seconds of one full step; stage_seconds[7] receives
+ * project, bin+sort+pack, raster fwd, loss, raster bwd, projection VJP, Adam. */
+double orc_time_step_sample(const OrcStepArgs* a, const OrcCamera* cam, int tile_row_stride,
+                            double* stage_seconds);
+
 /* Threads the oracle may use (OpenMP); <= 0 means all. Returns the count. */
 int orc_set_threads(int n);
 

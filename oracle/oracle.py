@@ -86,6 +86,9 @@ def lib():
                                      C.POINTER(C.c_int64)]
         L.orc_render.argtypes = [C.c_int, f32p, f32p, f32p, f32p, f32p, f32p, C.c_int, C.c_int, f32p,
                                  C.POINTER(OrcCamera), f32p]
+        L.orc_time_step_sample.restype = C.c_double
+        L.orc_time_step_sample.argtypes = [C.POINTER(OrcStepArgs), C.POINTER(OrcCamera), C.c_int,
+                                           C.POINTER(C.c_double)]
         _lib = L
     return _lib
 
@@ -260,9 +263,7 @@ class OracleTrainer:
     def params(self):
         return (self.means, self.scales, self.quats, self.opac, self.f_dc, self.f_rest)
 
-    def step(self, cam, gt, background, degrees_to_use=None, ssim_weight=0.2, lambda_dist=0.0,
-             want_grads=False, lr=None):
-        self.adam_step += 1
+    def _args(self, cam, gt, background, degrees_to_use, ssim_weight, lambda_dist, lr):
         a = OrcStepArgs()
         a.n, a.degree = self.n, self.degree
         a.degrees_to_use = self.degree if degrees_to_use is None else degrees_to_use
@@ -283,11 +284,26 @@ class OracleTrainer:
             a.lr[g] = (lr or self.lr)[g]
         a.adam_step = self.adam_step
         a.lambda_l1, a.lambda_dist, a.lambda_dssim = 1.0 - ssim_weight, lambda_dist, ssim_weight
+        return a, (bufs, dummy, bg, gt_c)
+
+    def time_sample(self, cam, gt, background, row_stride, degrees_to_use=None):
+        """orc_time_step_sample: (estimated seconds per full step, per-stage seconds)."""
+        self.adam_step += 1
+        a, keep = self._args(cam, gt, background, degrees_to_use, 0.2, 0.0, None)
+        st = (C.c_double * 7)()
+        est = lib().orc_time_step_sample(C.byref(a), C.byref(cam), row_stride, st)
+        del keep
+        return est, list(st)
+
+    def step(self, cam, gt, background, degrees_to_use=None, ssim_weight=0.2, lambda_dist=0.0,
+             want_grads=False, lr=None):
+        self.adam_step += 1
+        a, keep = self._args(cam, gt, background, degrees_to_use, ssim_weight, lambda_dist, lr)
         K = (self.degree + 1) ** 2 - 1
         grads = np.zeros(13 * self.n + 3 * K * self.n, np.float32) if want_grads else None
         img = np.zeros((cam.height, cam.width, 3), np.float32)
         kept = C.c_int64()
         loss = lib().orc_train_step(C.byref(a), C.byref(cam), None if grads is None else grads.ctypes.data,
                                     img.ctypes.data, C.byref(kept))
-        del bufs
+        del keep
         return dict(loss=loss, grads=grads, out_img=img, kept=kept.value)
