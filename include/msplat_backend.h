@@ -151,6 +151,25 @@ int msplat_shard_project_backward_adam(const MsplatGaussians* g, const MsplatCam
                                        const MsplatAdamState* adam, float* xys_grad_norm, float* vis_counts,
                                        float* max_2d_size, void* stream);
 
+/* Allocation-free L1 + DSSIM (+ distortion) loss, forward and backward. No
+ * counterpart in the reference. For callers that may not allocate device
+ * memory at run time (hosts whose GPU memory all comes from their own pool
+ * allocator, or that fix their memory budget at start-up): it calls no
+ * cudaMalloc/cudaFree and no allocating library routine. Its scratch lives in
+ * fixed arrays inside the library's device image, about 1.5 MiB held by every
+ * GPU that loads the library until the process exits, which limits images to
+ * 65,536 blocks of 32x16 pixels (e.g. 8192 x 4096); larger sizes are rejected
+ * with MSPLAT_ERR_ARGUMENT. Inputs and outputs are caller-owned device
+ * memory: out_img and gt [H,W,3], out_distortion [H,W] (may be NULL when
+ * lambda_dist == 0), dL_dout_img [H,W,3] (written), loss_out one float
+ * (written, may be NULL). The first call on a device looks up the scratch
+ * addresses; make that first call before any stream capture. All calls share
+ * the scratch, so calls that overlap on the GPU (other streams, other host
+ * threads) race; serialise them. Asynchronous on `stream`. */
+int msplat_loss_ssim_noalloc(const float* out_img, const float* gt, const float* out_distortion, int32_t width,
+                             int32_t height, float lambda_l1, float lambda_dist, float lambda_dssim,
+                             float* dL_dout_img, float* loss_out, void* stream);
+
 /* Accessor for the workspace tensors of the last call (the msplat_last_*
  * family, core/metal/bindings.h:36-43, 107-131). Names: out_img, out_depth,
  * out_normal, out_alpha, out_median_depth, out_distortion, final_Ts,

@@ -67,7 +67,8 @@ def build(verbose: bool = False, clean: bool = False) -> str:
             continue
         cmd = [nv] + ARCH + COMMON + PER_FILE.get(f, []) + ["-c", src, "-o", obj]
         if f.endswith(".cpp"):
-            cmd = [nv] + COMMON + ["-Xcompiler", "-ffp-contract=off", "-x", "c++", "-c", src, "-o", obj]
+            cmd = ["g++", "-O3", "-std=c++17", "-fPIC", "-ffp-contract=off", "-fno-fast-math",
+                   "-I", os.path.join(REPO, "include"), "-c", src, "-o", obj]
         if verbose:
             print(" ".join(cmd))
         subprocess.run(cmd, check=True)

@@ -625,6 +625,16 @@ int msplat_last_tensor(const char* name, MsplatTensorRef* out) {
     });
 }
 
+int msplat_loss_ssim_noalloc(const float* out_img, const float* gt, const float* out_distortion, int32_t width,
+                             int32_t height, float lambda_l1, float lambda_dist, float lambda_dssim,
+                             float* dL_dout_img, float* loss_out, void* stream) {
+    std::string msg;
+    const int rc = loss_ssim_noalloc(out_img, gt, out_distortion, width, height, lambda_l1, lambda_dist, lambda_dssim,
+                                     dL_dout_img, loss_out, static_cast<cudaStream_t>(stream), &msg);
+    t_last_error = rc == MSPLAT_OK ? std::string() : msg;
+    return rc;
+}
+
 int64_t msplat_last_num_intersections(void) {
     try {
         return workspace().kept;

@@ -7,6 +7,7 @@
 // record are internal (common.cuh).
 #pragma once
 #include <cstdint>
+#include <string>
 #include <cuda_runtime.h>
 
 namespace msplat {
@@ -121,6 +122,12 @@ void launch_loss_ssim(const LossArgs& a, cudaStream_t s);
 // out[2] = l1 term, out[3] = distortion term (all double), loss_f = float loss.
 void launch_loss_finalize(const double* partials, int num_blocks, float lambda_dssim, float inv_num,
                           double* out, float* loss_f, uint32_t* err, cudaStream_t s);
+
+// Allocation-free loss forward/backward (scratch in fixed device arrays of
+// ssim_loss.cu). Returns an MSPLAT_* code and fills *msg on failure.
+int loss_ssim_noalloc(const float* out_img, const float* gt, const float* out_distortion, int width, int height,
+                      float lambda_l1, float lambda_dist, float lambda_dssim, float* dL_dout_img, float* loss_out,
+                      cudaStream_t s, std::string* msg);
 
 // ---- Adam (adam.cu) -----------------------------------------------------------
 void launch_fused_adam(float* params, const float* grads, float* exp_avg, float* exp_avg_sq, int64_t n,

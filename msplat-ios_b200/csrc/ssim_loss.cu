@@ -17,6 +17,10 @@
 // back to the tile. The image and target are read once (plus halo) and
 // dL/dimg is written once; no [H,W,3] intermediate touches HBM. Loss partial
 // sums are reduced per CTA in double and summed in a fixed order afterwards.
+#include <mutex>
+#include <string>
+
+#include "../../include/msplat_backend.h"
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -228,6 +232,116 @@ void launch_loss_finalize(const double* partials, int num_blocks, float lambda_d
                           float* loss_f, uint32_t* err, cudaStream_t s) {
     note_launches(1);
     k_loss_finalize<<<1, 1024, 0, s>>>(partials, num_blocks, lambda_dssim, inv_num, out, loss_f, err);
+}
+
+// ---- allocation-free variant (msplat_loss_ssim_noalloc) --------------------
+//
+// The same two kernels, with their scratch (per-block partial sums, the four
+// loss terms and the error word) in fixed arrays that belong to the library's
+// device image instead of workspace buffers, so the entry point never
+// allocates. Every GPU that loads the library holds these arrays (about
+// 1.5 MiB) until the process exits. Host code cannot use the array names as
+// device addresses; the addresses are looked up once per device with
+// cudaGetSymbolAddress.
+constexpr int kNoAllocMaxBlocks = 65536;  // 32x16-pixel loss blocks: e.g. 8192 x 4096
+static __device__ __align__(256) double g_noalloc_partials[kNoAllocMaxBlocks * 3];
+static __device__ __align__(256) double g_noalloc_terms[4];
+static __device__ __align__(256) uint32_t g_noalloc_err[4];
+
+namespace {
+constexpr int kMaxDevices = 64;
+struct NoAllocScratch {
+    bool ready = false;
+    double* partials = nullptr;
+    double* terms = nullptr;
+    uint32_t* err = nullptr;
+};
+std::mutex g_noalloc_mu;
+NoAllocScratch g_noalloc[kMaxDevices];
+
+// Looks the scratch arrays up for the current device (first call per device).
+int noalloc_scratch(NoAllocScratch* out, std::string* msg) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        *msg = std::string("cudaGetDevice: ") + cudaGetErrorString(e);
+        return MSPLAT_ERR_CUDA;
+    }
+    if (dev < 0 || dev >= kMaxDevices) {
+        *msg = "device index out of range for the allocation-free loss";
+        return MSPLAT_ERR_ARGUMENT;
+    }
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    NoAllocScratch& s = g_noalloc[dev];
+    if (!s.ready) {
+        void* p = nullptr;
+        if ((e = cudaGetSymbolAddress(&p, g_noalloc_partials)) != cudaSuccess) {
+            *msg = std::string("cudaGetSymbolAddress(partials): ") + cudaGetErrorString(e);
+            return MSPLAT_ERR_CUDA;
+        }
+        s.partials = static_cast<double*>(p);
+        if ((e = cudaGetSymbolAddress(&p, g_noalloc_terms)) != cudaSuccess) {
+            *msg = std::string("cudaGetSymbolAddress(terms): ") + cudaGetErrorString(e);
+            return MSPLAT_ERR_CUDA;
+        }
+        s.terms = static_cast<double*>(p);
+        if ((e = cudaGetSymbolAddress(&p, g_noalloc_err)) != cudaSuccess) {
+            *msg = std::string("cudaGetSymbolAddress(err): ") + cudaGetErrorString(e);
+            return MSPLAT_ERR_CUDA;
+        }
+        s.err = static_cast<uint32_t*>(p);
+        s.ready = true;
+    }
+    *out = s;
+    return MSPLAT_OK;
+}
+}  // namespace
+
+int loss_ssim_noalloc(const float* out_img, const float* gt, const float* out_distortion, int width, int height,
+                      float lambda_l1, float lambda_dist, float lambda_dssim, float* dL_dout_img, float* loss_out,
+                      cudaStream_t s, std::string* msg) {
+    if (!out_img || !gt || !dL_dout_img) {
+        *msg = "out_img, gt and dL_dout_img must be device pointers";
+        return MSPLAT_ERR_ARGUMENT;
+    }
+    if (width <= 0 || height <= 0) {
+        *msg = "width and height must be positive";
+        return MSPLAT_ERR_ARGUMENT;
+    }
+    if (lambda_dist != 0.0f && !out_distortion) {
+        *msg = "out_distortion is required when lambda_dist != 0";
+        return MSPLAT_ERR_ARGUMENT;
+    }
+    const int64_t nb = (int64_t)((width + OW - 1) / OW) * ((height + OH - 1) / OH);
+    if (nb > kNoAllocMaxBlocks) {
+        *msg = "image too large for the allocation-free loss: " + std::to_string(nb) +
+               " blocks of 32x16 pixels, the fixed scratch holds " + std::to_string(kNoAllocMaxBlocks) +
+               " (e.g. 8192 x 4096)";
+        return MSPLAT_ERR_ARGUMENT;
+    }
+    NoAllocScratch sc;
+    int rc = noalloc_scratch(&sc, msg);
+    if (rc != MSPLAT_OK) return rc;
+    cudaError_t e = cudaMemsetAsync(sc.err, 0, sizeof(uint32_t), s);
+    if (e != cudaSuccess) {
+        *msg = std::string("cudaMemsetAsync: ") + cudaGetErrorString(e);
+        return MSPLAT_ERR_CUDA;
+    }
+    LossArgs la{};
+    la.width = width; la.height = height; la.row_begin = 0; la.row_end = height;
+    la.out_img = out_img; la.gt = gt; la.out_distortion = out_distortion;
+    la.lambda_l1 = lambda_l1; la.lambda_dist = lambda_dist; la.lambda_dssim = lambda_dssim;
+    la.inv_num = 1.0f / (float)(height * width * 3);
+    la.dL_dout_img = dL_dout_img;
+    la.partials = sc.partials;
+    launch_loss_ssim(la, s);
+    launch_loss_finalize(sc.partials, (int)nb, lambda_dssim, la.inv_num, sc.terms, loss_out, sc.err, s);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *msg = std::string("loss kernels: ") + cudaGetErrorString(e);
+        return MSPLAT_ERR_CUDA;
+    }
+    return MSPLAT_OK;
 }
 
 }  // namespace msplat

@@ -1,0 +1,70 @@
+"""The allocation-free loss entry point, msplat_loss_ssim_noalloc.
+
+Some programs that embed this library must not let it allocate GPU memory
+while they run: a host that gives out all device memory from its own pool
+allocator, or a system whose memory budget is fixed when it starts. For them
+the library has msplat_loss_ssim_noalloc, which keeps its working memory in a
+fixed array inside the library itself and never calls cudaMalloc. This test
+calls it through the C ABI and checks it against the loss and dL/dimage that
+the regular entry point (msplat_train_step_2dgs) computes for the same image,
+on two calls in a row with different image sizes, and checks that an image
+too large for the fixed array is refused. The file is named so that pytest
+collects it last.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from _cases import Case, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+GRAD_TOL = 1e-3
+LOSS_TOL = 1e-5
+
+
+def _lib():
+    from msplat import _backend as B
+    L = B.load()
+    f = L.msplat_loss_ssim_noalloc
+    f.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_float, C.c_float, C.c_float,
+                  C.c_void_p, C.c_void_p, C.c_void_p]
+    f.restype = C.c_int
+    L.msplat_last_error.restype = C.c_char_p
+    return B, L
+
+
+def test_noalloc_loss_matches_regular_entry_point_twice():
+    torch = pytest.importorskip("torch")
+    B, L = _lib()
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for name in ("cfg0", "sh1_odd"):  # 256x256, then 203x117: the second call reuses the scratch
+        case = Case(name)
+        g = B.DeviceGaussians(*case.scene.params(), sh_degree=case.degree)
+        cam = B.camera_from_oracle(case.ocam)
+        gt = torch.as_tensor(case.gt).cuda()
+        loss_ref = B.train_step_2dgs(g, cam, case.degree, case.bg, gt, 0.8, 0.0, 0.2)
+        img = B.last_tensor("out_img").clone()
+        dimg_ref = B.last_tensor("dL_dout_img").clone()
+        dimg = torch.full_like(img, float("nan"))
+        loss = torch.full((1,), float("nan"), device="cuda")
+        H, W = img.shape[0], img.shape[1]
+        rc = L.msplat_loss_ssim_noalloc(img.data_ptr(), gt.data_ptr(), None, W, H, 0.8, 0.0, 0.2,
+                                        dimg.data_ptr(), loss.data_ptr(), stream)
+        assert rc == 0, L.msplat_last_error().decode()
+        torch.cuda.synchronize()
+        assert rel_l2(dimg.cpu().numpy(), dimg_ref.cpu().numpy()) <= GRAD_TOL
+        got = float(loss.cpu()[0])
+        assert abs(got - loss_ref) <= LOSS_TOL * abs(loss_ref), (name, got, loss_ref)
+
+
+def test_noalloc_loss_rejects_images_beyond_its_fixed_scratch():
+    torch = pytest.importorskip("torch")
+    B, L = _lib()
+    buf = torch.zeros(16, device="cuda")
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = buf.data_ptr()
+    rc = L.msplat_loss_ssim_noalloc(p, p, None, 16384, 8192, 0.8, 0.0, 0.2, p, p, stream)
+    assert rc == 1
+    assert "too large" in L.msplat_last_error().decode()
