@@ -179,8 +179,10 @@ def run_ours(args, ws, rank, local):
         parts = torch.zeros(3, dtype=torch.float64, device=dev)
 
         def step(k):
-            sharding.sharded_step(B, dist, g, cams[k % C], cfg.degree, bg, gts[k % C], l1, ld, SSIM_WEIGHT, adam,
-                                  stats, plan, rg, rg_shard, parts)
+            adam.step += 1
+            fb, pa = sharding.gpu_step_fns(B, g, cams[k % C], cfg.degree, bg, gts[k % C], l1, ld, SSIM_WEIGHT,
+                                           adam, stats)
+            sharding.sharded_step(dist, plan, fb, pa, rg, rg_shard, g.full, parts)
 
     for k in range(args.warmup):
         step(k)

@@ -17,7 +17,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/msplat_backend.h"
+#include "msplat_backend.h"
 #include "common.cuh"
 #include "kernels.cuh"
 

@@ -8,7 +8,7 @@
 #include <cmath>
 #include <cstring>
 
-#include "../../include/msplat_backend.h"
+#include "msplat_backend.h"
 
 extern "C" {
 

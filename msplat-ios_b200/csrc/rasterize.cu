@@ -75,11 +75,51 @@ __device__ __forceinline__ bool eval_pair(float px, float py, float4 r0, float4 
 __device__ __forceinline__ int tile_lx(int t) { return ((t >> 5) & 1) * 8 + (t & 7); }
 __device__ __forceinline__ int tile_ly(int t) { return (t >> 6) * 4 + ((t >> 3) & 3); }
 
-__global__ void __launch_bounds__(kThreads) k_raster_fwd(RasterFwdArgs a) {
+__device__ __forceinline__ int to_pix(float v) {
+    return (int)fminf(fmaxf(v, -1.0e9f), 1.0e9f);
+}
+
+// Conservative inclusive pixel box (x0, y0, x1, y1) outside which the surfel
+// cannot reach alpha >= 1/255: the union of the 2-D filter disc
+// 2 d^2 <= rmax around the centre and the screen bounds of the projected disc
+// u^2 + v^2 <= rmax. The latter is the axis-aligned box of a conic computed
+// from its dual (T diag(rmax, rmax, -1) T^T), valid when the disc lies wholly
+// in front of the camera (d < 0); otherwise the box is unbounded. A 2-pixel
+// margin covers the rounding of this float computation. Empty (x0 > x1) when
+// the surfel can never reach 1/255.
+__device__ __forceinline__ int4 surfel_box(float4 r0, float4 r1, float4 r2, float rmax) {
+    const int4 everything = make_int4(-1000000000, -1000000000, 1000000000, 1000000000);
+    if (!(rmax > 0.f)) return (rmax == rmax) ? make_int4(1, 1, 0, 0) : everything;
+    const float r2d = sqrtf(0.5f * rmax) + 2.0f;
+    float x0 = r2.y - r2d, x1 = r2.y + r2d, y0 = r2.z - r2d, y1 = r2.z + r2d;
+    const float t0x = r0.x, t0y = r0.y, t0z = r0.z;   // row Tu
+    const float t1x = r0.w, t1y = r1.x, t1z = r1.y;   // row Tv
+    const float t2x = r1.z, t2y = r1.w, t2z = r2.x;   // row Tw
+    const float d = rmax * (t2x * t2x + t2y * t2y) - t2z * t2z;
+    if (!(d < 0.f)) return everything;
+    const float fa = rmax / d, fc = -1.0f / d;
+    const float cx = fa * (t0x * t2x + t0y * t2y) + fc * (t0z * t2z);
+    const float cy = fa * (t1x * t2x + t1y * t2y) + fc * (t1z * t2z);
+    const float hx = sqrtf(fmaxf(0.f, cx * cx - (fa * (t0x * t0x + t0y * t0y) + fc * (t0z * t0z))));
+    const float hy = sqrtf(fmaxf(0.f, cy * cy - (fa * (t1x * t1x + t1y * t1y) + fc * (t1z * t1z))));
+    const float mx = 2.0f + 1e-3f * (fabsf(cx) + hx), my = 2.0f + 1e-3f * (fabsf(cy) + hy);
+    x0 = fminf(x0, cx - hx - mx);
+    x1 = fmaxf(x1, cx + hx + mx);
+    y0 = fminf(y0, cy - hy - my);
+    y1 = fmaxf(y1, cy + hy + my);
+    if (!(x0 <= x1) || !(y0 <= y1)) return everything;
+    return make_int4(to_pix(floorf(x0)), to_pix(floorf(y0)), to_pix(ceilf(x1)), to_pix(ceilf(y1)));
+}
+
+__global__ void __launch_bounds__(kThreads, 5) k_raster_fwd(RasterFwdArgs a) {
     __shared__ float4 srec[kRecordF4][kThreads];
     __shared__ float srmax[kThreads];
+    __shared__ int4 sbox[kThreads];
     const int tile = (a.tile_row_begin + blockIdx.y) * a.tiles_x + blockIdx.x;
     const int lx = tile_lx(threadIdx.x), ly = tile_ly(threadIdx.x);
+    // this warp's 8x4 pixel block
+    const int wx0 = blockIdx.x * kTile + ((threadIdx.x >> 5) & 1) * 8, wx1 = wx0 + 7;
+    const int wy0 = (a.tile_row_begin + blockIdx.y) * kTile + (threadIdx.x >> 6) * 4, wy1 = wy0 + 3;
     const int j = blockIdx.x * kTile + lx;
     const int i = (a.tile_row_begin + blockIdx.y) * kTile + ly;
     const bool inside = (i < a.height) && (j < a.width);
@@ -88,6 +128,8 @@ __global__ void __launch_bounds__(kThreads) k_raster_fwd(RasterFwdArgs a) {
     const float mscale = __fdiv_rn(kFarN, __fsub_rn(kFarN, kNearN));
 
     float T = 1.f, cr = 0.f, cg = 0.f, cb = 0.f, nx = 0.f, ny = 0.f, nz = 0.f, pdepth = 0.f;
+    // contributor: 1-based position in the tile list of the surfel being
+    // blended (the reference's per-pixel counter, metal:612-650)
     float M1 = 0.f, M2 = 0.f, dist = 0.f, median_depth = 0.f;
     int median_c = -1, contributor = 0, last_c = 0;
     bool done = !inside;
@@ -98,18 +140,25 @@ __global__ void __launch_bounds__(kThreads) k_raster_fwd(RasterFwdArgs a) {
         if (idx < range.y) {
             const int g = a.gaussian_ids[idx];
             const float4* r = a.records + (size_t)g * kRecordF4;
+            float4 q[kRecordF4];
 #pragma unroll
-            for (int k = 0; k < kRecordF4; ++k) srec[k][threadIdx.x] = __ldg(r + k);
-            srmax[threadIdx.x] = reject_rho(srec[2][threadIdx.x].w);
+            for (int k = 0; k < kRecordF4; ++k) srec[k][threadIdx.x] = q[k] = __ldg(r + k);
+            const float rm = reject_rho(q[2].w);
+            srmax[threadIdx.x] = rm;
+            sbox[threadIdx.x] = surfel_box(q[0], q[1], q[2], rm);
         }
         __syncthreads();
         if (done) continue;
         const int bs = min(kThreads, range.y - b0);
+        const int base = b0 - range.x + 1;  // 1-based position of surfel 0 of this batch in the tile list
         for (int s = 0; s < bs; ++s) {
-            contributor++;
+            const int4 box = sbox[s];
+            if (box.x > wx1 || box.z < wx0 || box.y > wy1 || box.w < wy0) continue;  // whole warp
+            if (j < box.x || j > box.z || i < box.y || i > box.w) continue;
             Pair e;
             const float4 r2 = srec[2][s];
             if (!eval_pair(px, py, srec[0][s], srec[1][s], r2, srmax[s], e)) continue;
+            contributor = base + s;
             const float next_T = fmul(T, fsub(1.0f, e.alpha));
             if (next_T <= 1e-4f) {
                 done = true;
@@ -193,9 +242,10 @@ __device__ __forceinline__ float warp_halving_sum16(float (&v)[16], int lane) {
 }
 
 template <bool AUX>
-__global__ void __launch_bounds__(kThreads) k_raster_bwd(RasterBwdArgs a) {
+__global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
     __shared__ float4 srec[kRecordF4][kThreads];
     __shared__ float srmax[kThreads];
+    __shared__ int4 sbox[kThreads];
     __shared__ int sid[kThreads];
     __shared__ float sacc[kThreads][kGradStride];
     __shared__ int s_max_last;
@@ -204,6 +254,8 @@ __global__ void __launch_bounds__(kThreads) k_raster_bwd(RasterBwdArgs a) {
     const int tile = tile_row * a.tiles_x + blockIdx.x;
     const int j = blockIdx.x * kTile + tile_lx(threadIdx.x);
     const int i = tile_row * kTile + tile_ly(threadIdx.x);
+    const int wx0 = blockIdx.x * kTile + ((threadIdx.x >> 5) & 1) * 8, wx1 = wx0 + 7;
+    const int wy0 = tile_row * kTile + (threadIdx.x >> 6) * 4, wy1 = wy0 + 3;
     const bool inside = (i < a.height) && (j < a.width);
     const float px = (float)j, py = (float)i;
     const int2 range = a.tile_bins[tile];
@@ -252,22 +304,28 @@ __global__ void __launch_bounds__(kThreads) k_raster_bwd(RasterBwdArgs a) {
             const int g = a.gaussian_ids[bend - 1 - threadIdx.x];
             sid[threadIdx.x] = g;
             const float4* r = a.records + (size_t)g * kRecordF4;
+            float4 q[kRecordF4];
 #pragma unroll
-            for (int k = 0; k < kRecordF4; ++k) srec[k][threadIdx.x] = __ldg(r + k);
-            srmax[threadIdx.x] = reject_rho(srec[2][threadIdx.x].w);
+            for (int k = 0; k < kRecordF4; ++k) srec[k][threadIdx.x] = q[k] = __ldg(r + k);
+            const float rm = reject_rho(q[2].w);
+            srmax[threadIdx.x] = rm;
+            sbox[threadIdx.x] = surfel_box(q[0], q[1], q[2], rm);
         }
 #pragma unroll
         for (int k = 0; k < kGradStride; ++k) sacc[threadIdx.x][k] = 0.f;
         __syncthreads();
         for (int s = 0; s < bs; ++s) {
+            const int4 box = sbox[s];
+            if (box.x > wx1 || box.z < wx0 || box.y > wy1 || box.w < wy0) continue;  // whole warp
             const int rel = bend - 1 - s - range.x;
+            const bool in_box = j >= box.x && j <= box.z && i >= box.y && i <= box.w;
             float g[16];
 #pragma unroll
             for (int k = 0; k < 16; ++k) g[k] = 0.f;
             bool contrib = false;
             Pair e;
             const float4 r0 = srec[0][s], r1 = srec[1][s], r2 = srec[2][s];
-            if (rel < last_c && eval_pair(px, py, r0, r1, r2, srmax[s], e)) {
+            if (in_box && rel < last_c && eval_pair(px, py, r0, r1, r2, srmax[s], e)) {
                 contrib = true;
                 const float4 r3 = srec[3][s], r4 = srec[4][s];
                 const float alpha = e.alpha, G = e.G, opa = r2.w;

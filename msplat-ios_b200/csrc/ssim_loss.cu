@@ -20,7 +20,7 @@
 #include <mutex>
 #include <string>
 
-#include "../../include/msplat_backend.h"
+#include "msplat_backend.h"
 #include "common.cuh"
 #include "kernels.cuh"
 

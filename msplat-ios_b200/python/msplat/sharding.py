@@ -2,39 +2,60 @@
 
 Every rank holds the full parameter set and projects all Gaussians; rank r
 bins, sorts and rasterises the tile rows [row0, row1) (plus a one-tile-row
-halo that the 11x11 SSIM window needs), evaluates the loss and the backward on
-its own rows, and leaves per-Gaussian raster-space gradients [N, 16]. Those are
-summed across ranks with an NCCL reduce-scatter so that rank r receives the
+halo that the 11x11 SSIM window needs: 16 px >= the 10 px forward+backward
+reach), evaluates the loss and the backward on its own rows, and leaves
+per-Gaussian raster-space gradient records [N, 16]. Those are summed across
+ranks with one reduce-scatter, so that rank r receives the records of the
 Gaussian slice [g_begin, g_end); it runs the projection VJP and Adam on that
 slice, and the six parameter groups are all-gathered in place. Adam moments
-stay sharded (each rank only touches its slice).
+stay sharded (each rank only touches its slice). The three loss partial sums
+(l1, ssim, distortion) are all-reduced for reporting.
+
+The exchange is written once (`sharded_step`) over two callables, so the same
+collective sequence runs with NCCL on GPUs (the C ABI does the compute) and
+with gloo on CPU in the tests (the oracle does the compute).
 """
 from __future__ import annotations
 
 import dataclasses
 
+GRAD_STRIDE = 16  # floats per Gaussian in the raster-gradient record
+
 
 @dataclasses.dataclass
 class ShardPlan:
+    """Tile rows and the Gaussian slice owned by `rank` of `world` ranks.
+
+    Tile rows are split into equal contiguous bands. The Gaussian index range
+    is padded to world * chunk (chunk a multiple of 256) so that the
+    reduce-scatter and all-gather move equal-sized pieces.
+    """
     n: int
     tiles_y: int
     world: int
     rank: int
 
     def __post_init__(self):
+        if not (0 <= self.rank < self.world):
+            raise ValueError("rank out of range")
         rows = -(-self.tiles_y // self.world)
         self.row0 = min(self.rank * rows, self.tiles_y)
         self.row1 = min((self.rank + 1) * rows, self.tiles_y)
-        self.chunk = -(-self.n // self.world)
-        self.chunk = -(-self.chunk // 256) * 256
+        chunk = -(-self.n // self.world)
+        self.chunk = -(-chunk // 256) * 256
         self.padded = self.chunk * self.world
         self.g_begin = min(self.rank * self.chunk, self.n)
         self.g_end = min((self.rank + 1) * self.chunk, self.n)
 
+    def slice_rows(self):
+        """Rows of a [padded, ...] buffer that this rank contributes to all-gathers."""
+        return slice(self.rank * self.chunk, (self.rank + 1) * self.chunk)
+
 
 def pad_gaussians(g, padded: int):
-    """Re-home each parameter group in a [padded, ...] buffer (rows >= n stay
-    zero) so that all-gathers can run in place; g keeps contiguous [n] views."""
+    """Re-home each parameter group of a DeviceGaussians in a [padded, ...]
+    buffer (rows >= n stay zero) so that all-gathers can run in place; g keeps
+    contiguous [n] views for the compute."""
     import torch
     n = g.n
     g.full = []
@@ -47,14 +68,42 @@ def pad_gaussians(g, padded: int):
     return g
 
 
-def sharded_step(B, dist, g, cam, degree, bg, gt, l1, ld, lssim, adam, stats, plan, rg, rg_shard, parts):
-    B.shard_forward_backward(g, cam, degree, bg, gt, l1, ld, lssim, plan.row0, plan.row1, rg, parts)
+def sharded_step(dist, plan: ShardPlan, forward_backward, project_adam, rg, rg_shard, param_fulls, parts):
+    """One training step across ranks.
+
+    forward_backward(row0, row1, rg, parts): fills rg [padded, 16] with this
+        rank's raster gradients (rows >= n zero) and parts [3] with its loss sums.
+    project_adam(g_begin, g_end, rg_shard): projection VJP + Adam on the slice,
+        rg_shard [chunk, 16] holding the summed records of Gaussians
+        g_begin .. g_end - 1 in its first rows.
+    param_fulls: the [padded, ...] parameter buffers to all-gather in place.
+    """
+    forward_backward(plan.row0, plan.row1, rg, parts)
     dist.reduce_scatter_tensor(rg_shard, rg, op=dist.ReduceOp.SUM)
-    adam.step += 1
-    B.shard_project_backward_adam(g, cam, degree, rg_shard.data_ptr() - plan.g_begin * 64, plan.g_begin,
-                                  plan.g_end, adam, stats=stats, count_step=False)
-    for full in g.full:
+    project_adam(plan.g_begin, plan.g_end, rg_shard)
+    rows = plan.slice_rows()
+    for full in param_fulls:
         if full.numel() == 0:
             continue
-        dist.all_gather_into_tensor(full, full[plan.rank * plan.chunk:(plan.rank + 1) * plan.chunk])
+        dist.all_gather_into_tensor(full, full[rows])
     dist.all_reduce(parts)
+
+
+def loss_from_parts(parts, lambda_dssim: float, width: int, height: int) -> float:
+    """Loss of the whole image from the all-reduced (l1, ssim, distortion) sums."""
+    l1, ssim, dist_term = (float(x) for x in parts)
+    inv_num = 1.0 / (3.0 * width * height)
+    return l1 + dist_term + lambda_dssim * (1.0 - ssim * inv_num)
+
+
+def gpu_step_fns(B, g, cam, degree, bg, gt, lambda_l1, lambda_dist, lambda_dssim, adam, stats):
+    """The two callables of sharded_step bound to the C ABI (msplat_shard_*)."""
+    def forward_backward(row0, row1, rg, parts):
+        B.shard_forward_backward(g, cam, degree, bg, gt, lambda_l1, lambda_dist, lambda_dssim, row0, row1, rg, parts)
+
+    def project_adam(g0, g1, rg_shard):
+        # the kernel indexes records by global Gaussian id: offset the base
+        B.shard_project_backward_adam(g, cam, degree, rg_shard.data_ptr() - g0 * GRAD_STRIDE * 4, g0, g1, adam,
+                                      stats=stats, count_step=False)
+
+    return forward_backward, project_adam

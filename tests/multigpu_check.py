@@ -1,0 +1,77 @@
+"""Launched by tests/test_multigpu.py under torchrun (one process per GPU).
+
+Each rank runs two sharded training steps (msplat/sharding.py over NCCL) on a
+small scene; rank 0 also runs the same two steps with the single-GPU fused
+step on a private copy and compares the parameters. Prints "MULTIGPU OK" on
+success (rank 0) and exits non-zero otherwise.
+"""
+import datetime
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+for p in (REPO, os.path.join(REPO, "msplat-ios_b200", "python"), HERE):
+    sys.path.insert(0, p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+from _cases import Case  # noqa: E402
+from msplat import _backend as B  # noqa: E402
+from msplat import sharding  # noqa: E402
+
+
+def main():
+    rank, ws, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    B.load()
+    case = Case("sh3_small")
+    cfg, n = case.cfg, case.cfg.n
+    cam = B.camera_from_oracle(case.ocam)
+    gt = torch.as_tensor(case.gt).to(dev)
+    g = B.DeviceGaussians(*case.scene.params(), sh_degree=case.degree, device=dev)
+    adam = B.AdamState(g)
+    plan = sharding.ShardPlan(n, (cfg.height + 15) // 16, ws, rank)
+    sharding.pad_gaussians(g, plan.padded)
+    rg = torch.zeros(plan.padded, 16, device=dev)
+    rg_shard = torch.zeros(plan.chunk, 16, device=dev)
+    parts = torch.zeros(3, dtype=torch.float64, device=dev)
+    for _ in range(2):
+        adam.step += 1
+        fb, pa = sharding.gpu_step_fns(B, g, cam, case.degree, case.bg, gt, 0.8, 0.0, 0.2, adam, None)
+        sharding.sharded_step(dist, plan, fb, pa, rg, rg_shard, g.full, parts)
+    torch.cuda.synchronize()
+    loss_sh = sharding.loss_from_parts(parts.cpu().numpy(), 0.2, cfg.width, cfg.height)
+    got = [t.cpu().numpy() for t in g.groups()]
+    ok = True
+    if rank == 0:
+        g1 = B.DeviceGaussians(*case.scene.params(), sh_degree=case.degree, device=dev)
+        a1 = B.AdamState(g1)
+        loss_dev = torch.zeros(1, device=dev)
+        losses = []
+        for _ in range(2):
+            B.train_step_fused(g1, cam, case.degree, case.bg, gt, 0.8, 0.0, 0.2, a1, loss_dev=loss_dev)
+            losses.append(float(loss_dev.cpu()[0]))
+        ref = [t.cpu().numpy() for t in g1.groups()]
+        for k in range(6):
+            if ref[k].size == 0:
+                continue
+            frac = np.isclose(got[k], ref[k], rtol=1e-5, atol=1e-7).mean()
+            print(f"group {k}: {frac:.6f} of elements within 1e-5", flush=True)
+            ok &= frac > 0.999
+        print(f"loss sharded {loss_sh:.7f} single {losses[-1]:.7f}", flush=True)
+        ok &= abs(loss_sh - losses[-1]) <= 1e-4 * abs(losses[-1])
+    flag = torch.tensor([1 if ok else 0], device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    dist.destroy_process_group()
+    if rank == 0:
+        print("MULTIGPU OK" if flag.item() == 1 else "MULTIGPU FAIL", flush=True)
+    sys.exit(0 if flag.item() == 1 else 1)
+
+
+if __name__ == "__main__":
+    main()
