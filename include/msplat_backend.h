@@ -134,17 +134,22 @@ int msplat_train_step_fused(const MsplatGaussians* g, const MsplatCamera* cam, i
                             void* stream);
 
 /* Tile-sharded pieces of the step for multi-GPU runs (one process per GPU).
- * Part 1 projects all N Gaussians, bins and rasterises the tile rows
- * [tile_row_begin, tile_row_end) plus a one-tile-row halo, evaluates the
- * loss on the owned rows and rasterises the backward there; it leaves the
- * raster-space gradients [N,16] in raster_grads_out (device, zeroed by the
- * call) and the three loss partial sums (l1, ssim, distortion) in
- * loss_parts_dev (device double[3]). After the caller sums raster_grads across
- * ranks (reduce-scatter), part 2 runs the projection VJP and Adam on
- * Gaussians [g_begin, g_end). */
+ * Part 1 projects all N Gaussians, bins and rasterises a band of tile rows
+ * plus a one-tile-row halo (the SSIM window's reach), evaluates the loss on
+ * the band's own rows and rasterises the backward there. With world > 0 the
+ * band is chosen by the library: band `rank` of `world` contiguous bands of
+ * about equal work (kept tile intersections), identical on every rank because
+ * every rank projects the same Gaussians; the chosen [begin, end) is written
+ * to tile_rows. With world <= 0, tile_rows[0..1] gives the band. It leaves the
+ * raster-space gradient records [N,16] in raster_grads_out (device, zeroed by
+ * the call) and the three loss partial sums (l1, ssim, distortion) in
+ * loss_parts_dev (device double[3], may be NULL). After the caller sums the
+ * records across ranks (reduce-scatter), part 2 runs the projection VJP and
+ * Adam on Gaussians [g_begin, g_end); raster_grads must address the record of
+ * Gaussian i at raster_grads + 16 * i for i in that range. */
 int msplat_shard_forward_backward(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
                                   const float background[3], const float* gt, float lambda_l1, float lambda_dist,
-                                  float lambda_dssim, int32_t tile_row_begin, int32_t tile_row_end,
+                                  float lambda_dssim, int32_t world, int32_t rank, int32_t* tile_rows,
                                   float* raster_grads_out, double* loss_parts_dev, void* stream);
 int msplat_shard_project_backward_adam(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
                                        const float* raster_grads, int32_t g_begin, int32_t g_end,

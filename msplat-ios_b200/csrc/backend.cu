@@ -76,7 +76,8 @@ struct Workspace {
     // per pixel
     Buf final_Ts, final_idx, out_img, out_depth, out_normal, out_alpha, out_median, out_dist, dL_dout_img;
     // scalars
-    Buf loss_partials, loss_out, loss_f, err, totals;
+    Buf loss_partials, loss_out, loss_f, err, totals, row_work;
+    std::vector<int64_t> h_row_work;
     int64_t* h_totals = nullptr;  // pinned [2]
     uint32_t* h_err = nullptr;    // pinned [1]
     // shape bookkeeping of the last call
@@ -98,7 +99,7 @@ struct Workspace {
                       &dL_dfeatures_dc, &dL_dfeatures_rest, &dL_dopacity, &dL_dtransMat, &dL_dnormal3D,
                       &dL_dcolors, &tile_diff, &raw_counts, &raw_start, &tile_bins, &fill, &raw_keys,
                       &gaussian_ids, &final_Ts, &final_idx, &out_img, &out_depth, &out_normal, &out_alpha,
-                      &out_median, &out_dist, &dL_dout_img, &loss_partials, &loss_out, &loss_f, &err, &totals};
+                      &out_median, &out_dist, &dL_dout_img, &loss_partials, &loss_out, &loss_f, &err, &totals, &row_work};
         for (Buf* b : all) b->release();
         for (auto& set : ev_pending)
             for (auto& m : set) cudaEventDestroy(m.second);
@@ -214,9 +215,33 @@ CameraDev make_cam(const MsplatCamera* c) {
 
 // Projection, binning, sort and forward rasterisation of tile rows
 // [row0, row1). Fills the workspace; returns nothing.
+// Splits tile rows into `world` contiguous bands of about equal work; returns
+// band `rank` as [*b0, *b1).
+void balanced_band(const std::vector<int64_t>& work, int world, int rank, int* b0, int* b1) {
+    const int ty = (int)work.size();
+    long double total = 0;
+    for (int64_t v : work) total += (long double)v;
+    auto cut = [&](int r) {  // first row of band r
+        if (r <= 0) return 0;
+        if (r >= world) return ty;
+        const long double target = total * r / world;
+        long double run = 0;
+        int y = 0;
+        while (y < ty && run + (long double)work[y] / 2 < target) run += (long double)work[y++];
+        return y;
+    };
+    *b0 = cut(rank);
+    *b1 = cut(rank + 1);
+}
+
+// Projection, binning, sort and forward rasterisation of tile rows
+// [row0, row1). When balance_world > 0 the rows are chosen here instead:
+// band balance_rank of balance_world work-balanced bands, returned in
+// *owned0/*owned1, rendered with a one-tile-row halo.
 void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam, int degrees_to_use,
                    float glob_scale, float clip, const float bg[3], bool ref_outputs, int row0, int row1,
-                   cudaStream_t s) {
+                   cudaStream_t s, int balance_world = 0, int balance_rank = 0, int* owned0 = nullptr,
+                   int* owned1 = nullptr) {
     const int n = g->num_points;
     const int K = sh_rest_bases(g->sh_degree);
     const int tx = cam.tiles_x, ty = cam.tiles_y, T = tx * ty;
@@ -267,8 +292,24 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     mark(w, kStProject, s);
     launch_project_forward(pa, s);
     mark(w, kStCounts, s);
+    if (balance_world > 0) {
+        // counts over all rows -> per-row work -> this rank's band (+ halo)
+        w.row_work.ensure((size_t)ty * sizeof(int64_t));
+        launch_tile_counts(w.tile_diff.as<int32_t>(), tx, ty, 0, ty, w.raw_counts.as<int32_t>(),
+                           w.raw_start.as<int64_t>(), w.tile_bins.as<int2>(), w.totals.as<int64_t>(),
+                           w.row_work.as<int64_t>(), s);
+        w.h_row_work.resize(ty);
+        CK(cudaMemcpyAsync(w.h_row_work.data(), w.row_work.p, (size_t)ty * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+        CK(cudaStreamSynchronize(s));
+        int o0 = 0, o1 = 0;
+        balanced_band(w.h_row_work, balance_world, balance_rank, &o0, &o1);
+        if (owned0) *owned0 = o0;
+        if (owned1) *owned1 = o1;
+        row0 = o1 > o0 ? std::max(0, o0 - 1) : 0;
+        row1 = o1 > o0 ? std::min(ty, o1 + 1) : 0;
+    }
     launch_tile_counts(w.tile_diff.as<int32_t>(), tx, ty, row0, row1, w.raw_counts.as<int32_t>(),
-                       w.raw_start.as<int64_t>(), w.tile_bins.as<int2>(), w.totals.as<int64_t>(), s);
+                       w.raw_start.as<int64_t>(), w.tile_bins.as<int2>(), w.totals.as<int64_t>(), nullptr, s);
     // The one host read of the step: buffer sizes for the intersections.
     CK(cudaMemcpyAsync(w.h_totals, w.totals.p, 2 * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
@@ -521,33 +562,45 @@ int msplat_train_step_fused(const MsplatGaussians* g, const MsplatCamera* cam, i
 
 int msplat_shard_forward_backward(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
                                   const float background[3], const float* gt, float lambda_l1, float lambda_dist,
-                                  float lambda_dssim, int32_t tile_row_begin, int32_t tile_row_end,
+                                  float lambda_dssim, int32_t world, int32_t rank, int32_t* tile_rows,
                                   float* raster_grads_out, double* loss_parts_dev, void* stream) {
     return guarded([&] {
         check_inputs(g, cam, degrees_to_use);
-        if (!background || !gt || !raster_grads_out) throw Error(MSPLAT_ERR_ARGUMENT, "null pointer");
+        if (!background || !gt || !raster_grads_out || !tile_rows) throw Error(MSPLAT_ERR_ARGUMENT, "null pointer");
         cudaStream_t s = static_cast<cudaStream_t>(stream);
         Workspace& w = workspace();
         CameraDev cd = make_cam(cam);
-        if (tile_row_begin < 0 || tile_row_end > cd.tiles_y || tile_row_begin > tile_row_end)
+        int o0 = tile_rows[0], o1 = tile_rows[1];
+        if (world > 0) {
+            if (rank < 0 || rank >= world) throw Error(MSPLAT_ERR_ARGUMENT, "rank out of range");
+        } else if (o0 < 0 || o1 > cd.tiles_y || o0 > o1) {
             throw Error(MSPLAT_ERR_ARGUMENT, "bad tile row range");
+        }
         const int n = g->num_points;
-        const int r0 = std::max(0, tile_row_begin - 1), r1 = std::min(cd.tiles_y, tile_row_end + 1);
-        stage_forward(w, g, cd, degrees_to_use, 1.0f, 0.01f, background, false, r0, r1, s);
-        const int p0 = tile_row_begin * kTile, p1 = std::min(cd.height, tile_row_end * kTile);
-        stage_loss(w, cd, gt, lambda_l1, lambda_dist, lambda_dssim, p0, p1, false, s);
+        const int r0 = std::max(0, o0 - 1), r1 = std::min(cd.tiles_y, o1 + 1);
+        stage_forward(w, g, cd, degrees_to_use, 1.0f, 0.01f, background, false, r0, r1, s, world, rank, &o0, &o1);
+        tile_rows[0] = o0;
+        tile_rows[1] = o1;
+        const int p0 = std::min(cd.height, o0 * kTile), p1 = std::min(cd.height, o1 * kTile);
         const size_t nn = (size_t)(n > 0 ? n : 1);
         CK(cudaMemsetAsync(raster_grads_out, 0, nn * kGradStride * 4, s));
-        stage_raster_backward(w, cd, background, lambda_dist, tile_row_begin, tile_row_end, raster_grads_out, s);
+        if (p1 > p0) {
+            stage_loss(w, cd, gt, lambda_l1, lambda_dist, lambda_dssim, p0, p1, false, s);
+            stage_raster_backward(w, cd, background, lambda_dist, o0, o1, raster_grads_out, s);
+        }
         if (loss_parts_dev) {
-            // Sum the block partials (l1, ssim, dist) without the DSSIM offset.
-            const int nb = loss_num_blocks(cd.width, p0, p1);
-            launch_loss_finalize(w.loss_partials.as<double>(), nb, 0.0f, 0.0f, w.loss_out.as<double>(),
-                                 nullptr, w.err.as<uint32_t>(), s);
-            // loss_out = {l1 + dist, ssim, l1, dist}: forward (l1, ssim, dist)
-            CK(cudaMemcpyAsync(loss_parts_dev, w.loss_out.as<double>() + 2, sizeof(double), cudaMemcpyDeviceToDevice, s));
-            CK(cudaMemcpyAsync(loss_parts_dev + 1, w.loss_out.as<double>() + 1, sizeof(double), cudaMemcpyDeviceToDevice, s));
-            CK(cudaMemcpyAsync(loss_parts_dev + 2, w.loss_out.as<double>() + 3, sizeof(double), cudaMemcpyDeviceToDevice, s));
+            if (p1 > p0) {
+                // Sum the block partials (l1, ssim, dist) without the DSSIM offset.
+                const int nb = loss_num_blocks(cd.width, p0, p1);
+                launch_loss_finalize(w.loss_partials.as<double>(), nb, 0.0f, 0.0f, w.loss_out.as<double>(),
+                                     nullptr, w.err.as<uint32_t>(), s);
+                // loss_out = {l1 + dist, ssim, l1, dist} -> parts (l1, ssim, dist)
+                CK(cudaMemcpyAsync(loss_parts_dev, w.loss_out.as<double>() + 2, sizeof(double), cudaMemcpyDeviceToDevice, s));
+                CK(cudaMemcpyAsync(loss_parts_dev + 1, w.loss_out.as<double>() + 1, sizeof(double), cudaMemcpyDeviceToDevice, s));
+                CK(cudaMemcpyAsync(loss_parts_dev + 2, w.loss_out.as<double>() + 3, sizeof(double), cudaMemcpyDeviceToDevice, s));
+            } else {
+                CK(cudaMemsetAsync(loss_parts_dev, 0, 3 * sizeof(double), s));
+            }
         }
         CK(cudaGetLastError());
     });

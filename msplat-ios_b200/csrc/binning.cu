@@ -24,10 +24,14 @@ namespace msplat {
 namespace {
 
 constexpr int kCountThreads = 1024;
+// Work estimate of a tile row for band balancing: kept intersections plus a
+// fixed per-tile cost (launch, id loads, per-pixel outputs).
+constexpr int kRowWorkPerTile = 64;
 
 __global__ void __launch_bounds__(kCountThreads)
 k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int row0, int row1, int32_t* __restrict__ raw_counts,
-              int64_t* __restrict__ raw_start, int2* __restrict__ tile_bins, int64_t* __restrict__ totals) {
+              int64_t* __restrict__ raw_start, int2* __restrict__ tile_bins, int64_t* __restrict__ totals,
+              int64_t* __restrict__ row_work) {
     const int dw = tx + 1;
     // Column prefix over y (one thread per tile column).
     for (int x = threadIdx.x; x < tx; x += blockDim.x) {
@@ -42,12 +46,15 @@ k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int row0, int ro
     // [row0, row1) get zero counts so that nothing is emitted for them.
     for (int y = threadIdx.x; y < ty; y += blockDim.x) {
         int run = 0;
+        int64_t work = 0;
         int32_t* row = raw_counts + (size_t)y * tx;
         const bool in_band = y >= row0 && y < row1;
         for (int x = 0; x < tx; ++x) {
             run += row[x];
             row[x] = in_band ? run : 0;
+            work += min(run, kMaxTileElems) + kRowWorkPerTile;
         }
+        if (row_work) row_work[y] = work;
     }
     __syncthreads();
     // Exclusive scans of raw (int64) and kept = min(raw, 2048) (int32).
@@ -199,10 +206,11 @@ k_tile_sort(const int32_t* __restrict__ raw_counts, const int64_t* __restrict__ 
 }  // namespace
 
 void launch_tile_counts(const int32_t* tile_diff, int tiles_x, int tiles_y, int row0, int row1,
-                        int32_t* raw_counts, int64_t* raw_start, int2* tile_bins, int64_t* totals, cudaStream_t s) {
+                        int32_t* raw_counts, int64_t* raw_start, int2* tile_bins, int64_t* totals,
+                        int64_t* row_work, cudaStream_t s) {
     note_launches(1);
     k_tile_counts<<<1, kCountThreads, 0, s>>>(tile_diff, tiles_x, tiles_y, row0, row1, raw_counts, raw_start,
-                                              tile_bins, totals);
+                                              tile_bins, totals, row_work);
 }
 
 void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x, int row0, int row1,

@@ -69,7 +69,7 @@ def load():
     L.msplat_train_step_fused.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, fp3, vp, f, f,
                                           f, C.POINTER(MsplatAdamState), vp, vp, vp, vp, i32, vp]
     L.msplat_shard_forward_backward.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, fp3, vp,
-                                                f, f, f, i32, i32, vp, vp, vp]
+                                                f, f, f, i32, i32, C.POINTER(C.c_int32), vp, vp, vp]
     L.msplat_shard_project_backward_adam.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, vp,
                                                      i32, i32, C.POINTER(MsplatAdamState), vp, vp, vp, vp]
     L.msplat_last_tensor.argtypes = [C.c_char_p, C.POINTER(MsplatTensorRef)]
@@ -217,12 +217,16 @@ def train_step_fused(g: DeviceGaussians, cam: MsplatCamera, degrees_to_use: int,
                                           _ptr(loss_dev), 1 if write_grads else 0, _stream(stream)))
 
 
-def shard_forward_backward(g, cam, degrees_to_use, background, gt, lambda_l1, lambda_dist, lambda_dssim, row0, row1,
-                           raster_grads, loss_parts, stream=None):
+def shard_forward_backward(g, cam, degrees_to_use, background, gt, lambda_l1, lambda_dist, lambda_dssim, raster_grads,
+                           loss_parts, world=0, rank=0, rows=(0, 0), stream=None):
+    """Part 1 of the sharded step. With world > 0 the library picks a
+    work-balanced band for `rank`; returns the (begin, end) tile rows used."""
     gs = g.struct()
+    tr = (C.c_int32 * 2)(int(rows[0]), int(rows[1]))
     _check(load().msplat_shard_forward_backward(C.byref(gs), C.byref(cam), degrees_to_use, _bg(background), _ptr(gt),
-                                                lambda_l1, lambda_dist, lambda_dssim, row0, row1, _ptr(raster_grads),
-                                                _ptr(loss_parts), _stream(stream)))
+                                                lambda_l1, lambda_dist, lambda_dssim, world, rank, tr,
+                                                _ptr(raster_grads), _ptr(loss_parts), _stream(stream)))
+    return tr[0], tr[1]
 
 
 def shard_project_backward_adam(g, cam, degrees_to_use, raster_grads, g0, g1, adam: AdamState, stats=None,

@@ -71,14 +71,15 @@ def pad_gaussians(g, padded: int):
 def sharded_step(dist, plan: ShardPlan, forward_backward, project_adam, rg, rg_shard, param_fulls, parts):
     """One training step across ranks.
 
-    forward_backward(row0, row1, rg, parts): fills rg [padded, 16] with this
-        rank's raster gradients (rows >= n zero) and parts [3] with its loss sums.
+    forward_backward(plan, rg, parts): fills rg [padded, 16] with this rank's
+        raster gradients (rows >= n zero) and parts [3] with its loss sums; it
+        may rebalance plan.row0/plan.row1.
     project_adam(g_begin, g_end, rg_shard): projection VJP + Adam on the slice,
         rg_shard [chunk, 16] holding the summed records of Gaussians
         g_begin .. g_end - 1 in its first rows.
     param_fulls: the [padded, ...] parameter buffers to all-gather in place.
     """
-    forward_backward(plan.row0, plan.row1, rg, parts)
+    forward_backward(plan, rg, parts)
     dist.reduce_scatter_tensor(rg_shard, rg, op=dist.ReduceOp.SUM)
     project_adam(plan.g_begin, plan.g_end, rg_shard)
     rows = plan.slice_rows()
@@ -96,10 +97,16 @@ def loss_from_parts(parts, lambda_dssim: float, width: int, height: int) -> floa
     return l1 + dist_term + lambda_dssim * (1.0 - ssim * inv_num)
 
 
-def gpu_step_fns(B, g, cam, degree, bg, gt, lambda_l1, lambda_dist, lambda_dssim, adam, stats):
-    """The two callables of sharded_step bound to the C ABI (msplat_shard_*)."""
-    def forward_backward(row0, row1, rg, parts):
-        B.shard_forward_backward(g, cam, degree, bg, gt, lambda_l1, lambda_dist, lambda_dssim, row0, row1, rg, parts)
+def gpu_step_fns(B, g, cam, degree, bg, gt, lambda_l1, lambda_dist, lambda_dssim, adam, stats, balance=True):
+    """The two callables of sharded_step bound to the C ABI (msplat_shard_*).
+    With balance the library picks work-balanced tile-row bands each step."""
+    def forward_backward(plan, rg, parts):
+        if balance:
+            plan.row0, plan.row1 = B.shard_forward_backward(g, cam, degree, bg, gt, lambda_l1, lambda_dist,
+                                                            lambda_dssim, rg, parts, world=plan.world, rank=plan.rank)
+        else:
+            B.shard_forward_backward(g, cam, degree, bg, gt, lambda_l1, lambda_dist, lambda_dssim, rg, parts,
+                                     rows=(plan.row0, plan.row1))
 
     def project_adam(g0, g1, rg_shard):
         # the kernel indexes records by global Gaussian id: offset the base

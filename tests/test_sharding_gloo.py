@@ -59,7 +59,8 @@ def _rank_main(rank, ws, port, out_path):
     m = [np.zeros_like(a) for a in params]
     v = [np.zeros_like(a) for a in params]
 
-    def forward_backward(row0, row1, rg, parts):
+    def forward_backward(plan_, rg, parts):
+        row0, row1 = plan_.row0, plan_.row1
         dimg = ls["dL_dout_img"].copy()
         dimg[: row0 * 16] = 0.0
         dimg[row1 * 16:] = 0.0
