@@ -247,25 +247,49 @@ def run_ours(args, ws, rank, local):
                 "algorithmic_bytes": alg, "ms_per_launch": round(per_stage[dom], 4),
                 "pairs_upper_bound_per_s": round(kept * 256 / (per_stage[dom] * 1e-3), 1)}
 
-    # e2e through the C ABI with host buffers
+    # e2e through the public trainer API (msplat_trainer_step): every step
+    # copies its target image host->device from pinned memory and reads the
+    # loss back, as a user of msplat_c_api.h does.
     e2e = None
     e2e_steps = args.e2e_steps if args.e2e_steps is not None else min(args.steps, 10)
-    if ws == 1 and e2e_steps > 0:
-        host_gt = [gts[k].cpu().pin_memory() for k in range(min(C, e2e_steps + 1))]
+    if e2e_steps > 0 and ws == 1:
+        import msplat
+        E = min(C, 4)
+        host_imgs = np.stack([gts[k].cpu().numpy() for k in range(E)])
+        fx, fy, cx, cy = scene.intrinsics
+        ds = msplat.Dataset.from_memory(scene.cam_to_world[:E], np.tile([fx, fy, cx, cy], (E, 1)), cfg.width,
+                                        cfg.height, host_imgs)
+        tcfg = msplat.TrainingConfig(iterations=10 ** 9, sh_degree=cfg.degree, sh_degree_interval=1,
+                                     num_downscales=0, ssim_weight=SSIM_WEIGHT)
+        trainer = msplat.GaussianTrainer(ds, tcfg, params=scene.params())
+        for _ in range(max(args.warmup, cfg.degree)):  # degrees_to_use ramps to sh_degree by step 3
+            trainer.step()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            trainer.step()
+        e2e_s = (time.perf_counter() - t0) / e2e_steps
+        e2e = {"value": round(1.0 / e2e_s, 3), "unit": "iters/s", "h2d_bytes_per_step": int(host_imgs[0].nbytes),
+               "d2h_bytes_per_step": 4, "steps": e2e_steps,
+               "path": "msplat_trainer_step (public C API): target image H2D from pinned memory, loss D2H, sync"}
+        del trainer, ds
+    elif e2e_steps > 0:
+        host_gt = [gts[k].cpu().pin_memory() for k in range(min(C, 4))]
         dev_gt = torch.empty_like(gts[0])
-        loss_host = torch.zeros(1).pin_memory()
-        torch.cuda.synchronize()
+        parts_host = torch.zeros(3, dtype=torch.float64).pin_memory()
+        dist.barrier()
         t0 = time.perf_counter()
         for k in range(e2e_steps):
             dev_gt.copy_(host_gt[k % len(host_gt)], non_blocking=True)
-            B.train_step_fused(g, cams[k % C], cfg.degree, bg, dev_gt, l1, ld, SSIM_WEIGHT, adam, stats=stats,
-                               loss_dev=loss_dev)
-            loss_host.copy_(loss_dev, non_blocking=True)
+            adam.step += 1
+            fb, pa = sharding.gpu_step_fns(B, g, cams[k % C], cfg.degree, bg, dev_gt, l1, ld, SSIM_WEIGHT, adam, stats)
+            sharding.sharded_step(dist, plan, fb, pa, rg, rg_shard, g.full, parts)
+            parts_host.copy_(parts, non_blocking=True)
             stream.synchronize()
-        e2e_s = (time.perf_counter() - t0) / e2e_steps
-        e2e = {"value": round(1.0 / e2e_s, 3), "unit": "iters/s", "h2d_bytes_per_step": int(gts[0].numel() * 4),
-               "d2h_bytes_per_step": 4, "steps": e2e_steps,
-               "path": "msplat_train_step_fused (C ABI), target image H2D from pinned memory, loss D2H"}
+        e2e_s = torch.tensor([(time.perf_counter() - t0) / e2e_steps], device=dev, dtype=torch.float64)
+        dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(1.0 / float(e2e_s.item()), 3), "unit": "iters/s",
+               "h2d_bytes_per_step": int(gts[0].numel() * 4), "d2h_bytes_per_step": 24, "steps": e2e_steps,
+               "path": "msplat_shard_* C ABI + NCCL per rank: target image H2D from pinned memory, loss sums D2H"}
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:

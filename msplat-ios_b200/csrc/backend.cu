@@ -27,8 +27,12 @@ static std::atomic<int64_t> g_launches{0};
 void note_launches(int k) { g_launches.fetch_add(k, std::memory_order_relaxed); }
 
 namespace {
-
 thread_local std::string t_last_error;
+}  // namespace
+
+void set_last_error(const std::string& msg) { t_last_error = msg; }
+
+namespace {
 
 struct Error : std::runtime_error {
     int code;
@@ -219,15 +223,15 @@ CameraDev make_cam(const MsplatCamera* c) {
 // band `rank` as [*b0, *b1).
 void balanced_band(const std::vector<int64_t>& work, int world, int rank, int* b0, int* b1) {
     const int ty = (int)work.size();
-    long double total = 0;
-    for (int64_t v : work) total += (long double)v;
+    double total = 0;
+    for (int64_t v : work) total += (double)v;
     auto cut = [&](int r) {  // first row of band r
         if (r <= 0) return 0;
         if (r >= world) return ty;
-        const long double target = total * r / world;
-        long double run = 0;
+        const double target = total * r / world;
+        double run = 0;
         int y = 0;
-        while (y < ty && run + (long double)work[y] / 2 < target) run += (long double)work[y++];
+        while (y < ty && run + (double)work[y] / 2 < target) run += (double)work[y++];
         return y;
     };
     *b0 = cut(rank);

@@ -15,6 +15,8 @@ namespace msplat {
 // Kernel-launch accounting (msplat_launch_count): every launcher records the
 // kernels it enqueues.
 void note_launches(int k);
+// Sets the calling thread's msplat_last_error() text ("" clears it).
+void set_last_error(const std::string& msg);
 
 struct CameraDev {
     float viewmat[16];
@@ -131,6 +133,10 @@ void launch_loss_finalize(const double* partials, int num_blocks, float lambda_d
 int loss_ssim_noalloc(const float* out_img, const float* gt, const float* out_distortion, int width, int height,
                       float lambda_l1, float lambda_dist, float lambda_dssim, float* dL_dout_img, float* loss_out,
                       cudaStream_t s, std::string* msg);
+
+// ---- image helpers of the trainer API (image_ops.cu) --------------------------
+void launch_resize_area(const float* src, int sw, int sh, float* dst, int dw, int dh, cudaStream_t s);
+void launch_rgba8(const float* src, uint8_t* dst, int64_t n, cudaStream_t s);
 
 // ---- Adam (adam.cu) -----------------------------------------------------------
 void launch_fused_adam(float* params, const float* grads, float* exp_avg, float* exp_avg_sq, int64_t n,

@@ -1,0 +1,646 @@
+// trainer.cu — the trainer-level C API of include/msplat_c_api.h: in-memory
+// datasets, Model initialisation, the training step loop with its camera
+// shuffle and learning-rate schedule, rendering and evaluation. Host code over
+// the backend C ABI (include/msplat_backend.h) and the CUDA runtime.
+//
+// Follows core/src/msplat_api.mm (Dataset/Trainer, :20-280; C API :282-407)
+// and core/src/model.cpp (Model ctor :43-121, setupOptimizers :123-168,
+// schedulersStep :183-186, getDownscaleFactor :235-238, prepareCam :500-544,
+// fullIteration :762-829).
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <numeric>
+#include <random>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "kernels.cuh"
+#include "msplat_backend.h"
+#include "msplat_c_api.h"
+
+namespace msplat {
+namespace {
+
+struct ApiError : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+
+#define CKT(call)                                                                                     \
+    do {                                                                                              \
+        cudaError_t e_ = (call);                                                                      \
+        if (e_ != cudaSuccess) throw ApiError(std::string(#call) + ": " + cudaGetErrorString(e_));    \
+    } while (0)
+
+void check_rc(int rc) {
+    if (rc != MSPLAT_OK) throw ApiError(msplat_last_error());
+}
+
+struct Camera {
+    float c2w[16];
+    float fx, fy, cx, cy;
+    int width, height;
+    float* image = nullptr;  // pinned host [h][w][3] or null
+};
+
+struct Dataset {
+    std::vector<Camera> train, test;
+    std::vector<float> xyz;
+    std::vector<uint8_t> rgb;
+    std::vector<float*> pinned;
+    ~Dataset() {
+        for (float* p : pinned) cudaFreeHost(p);
+    }
+};
+
+template <typename T>
+struct DevArray {
+    T* p = nullptr;
+    size_t n = 0;
+    void alloc(size_t count) {
+        release();
+        if (count == 0) count = 1;
+        CKT(cudaMalloc(&p, count * sizeof(T)));
+        CKT(cudaMemset(p, 0, count * sizeof(T)));
+        n = count;
+    }
+    void ensure(size_t count) {
+        if (count > n) alloc(count);
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+    }
+    ~DevArray() { release(); }
+};
+
+constexpr double kC0 = 0.28209479177387814;
+
+int num_sh_bases(int degree) { return (degree + 1) * (degree + 1); }
+
+// Mean distance to the 3 nearest other points (PointsTensor::scales, k = 4
+// including the point itself, kdtree_tensor.hpp:26-40), with a uniform grid.
+std::vector<float> knn_mean_distance(const std::vector<float>& xyz) {
+    const int64_t n = (int64_t)xyz.size() / 3;
+    std::vector<float> out(n, 0.01f);
+    if (n < 2) return out;
+    float lo[3] = {1e30f, 1e30f, 1e30f}, hi[3] = {-1e30f, -1e30f, -1e30f};
+    for (int64_t i = 0; i < n; ++i)
+        for (int d = 0; d < 3; ++d) {
+            lo[d] = std::min(lo[d], xyz[3 * i + d]);
+            hi[d] = std::max(hi[d], xyz[3 * i + d]);
+        }
+    const double vol = std::max(1e-12, (double)(hi[0] - lo[0]) * (hi[1] - lo[1]) * (hi[2] - lo[2]));
+    const float cell = (float)std::max(1e-6, std::cbrt(vol / std::max<int64_t>(1, n / 2)));
+    auto key = [&](int cx, int cy, int cz) { return ((int64_t)cx * 73856093) ^ ((int64_t)cy * 19349663) ^ ((int64_t)cz * 83492791); };
+    std::unordered_map<int64_t, std::vector<int64_t>> grid;
+    grid.reserve((size_t)n);
+    auto cell_of = [&](int64_t i, int* c) {
+        for (int d = 0; d < 3; ++d) c[d] = (int)std::floor((xyz[3 * i + d] - lo[d]) / cell);
+    };
+    for (int64_t i = 0; i < n; ++i) {
+        int c[3];
+        cell_of(i, c);
+        grid[key(c[0], c[1], c[2])].push_back(i);
+    }
+    for (int64_t i = 0; i < n; ++i) {
+        int c[3];
+        cell_of(i, c);
+        float best[3] = {1e30f, 1e30f, 1e30f};
+        for (int r = 1; r < 64; ++r) {
+            for (int dx = -r; dx <= r; ++dx)
+                for (int dy = -r; dy <= r; ++dy)
+                    for (int dz = -r; dz <= r; ++dz) {
+                        if (std::max({std::abs(dx), std::abs(dy), std::abs(dz)}) != r && r > 1) continue;
+                        auto it = grid.find(key(c[0] + dx, c[1] + dy, c[2] + dz));
+                        if (it == grid.end()) continue;
+                        for (int64_t j : it->second) {
+                            if (j == i) continue;
+                            const float ex = xyz[3 * j] - xyz[3 * i], ey = xyz[3 * j + 1] - xyz[3 * i + 1],
+                                        ez = xyz[3 * j + 2] - xyz[3 * i + 2];
+                            const float d2 = ex * ex + ey * ey + ez * ez;
+                            if (d2 < best[2]) {
+                                best[2] = d2;
+                                if (best[2] < best[1]) std::swap(best[1], best[2]);
+                                if (best[1] < best[0]) std::swap(best[0], best[1]);
+                            }
+                        }
+                    }
+            // neighbours within r-1 cells are complete once the third best is closer than (r-1) cells
+            if (best[2] < 1e29f && std::sqrt(best[2]) <= (r - 1) * cell) break;
+        }
+        float sum = 0.f;
+        int k = 0;
+        for (float b : best)
+            if (b < 1e29f) {
+                sum += std::sqrt(b);
+                ++k;
+            }
+        out[i] = k ? sum / k : 0.01f;
+    }
+    return out;
+}
+
+struct Trainer {
+    MsplatConfig cfg;
+    Dataset* ds = nullptr;
+    int n = 0, degree = 0, K = 0;
+    DevArray<float> params[6], m[6], v[6], stats[3];
+    int64_t counts[6] = {};
+    float lr[6] = {0.00016f, 0.005f, 0.001f, 0.0025f, 0.000125f, 0.05f};  // model.cpp:142
+    float means_lr_init = 0.00016f, means_lr_final = 0.0000016f;
+    int adam_step = 0;
+    int current_step = 0;
+    std::vector<size_t> cam_indices;
+    size_t cam_pos = 0;
+    std::mt19937 rng{42};
+    DevArray<float> gt_full, gt_scaled, img, loss_dev;
+    DevArray<uint8_t> rgba;
+    float* loss_host = nullptr;  // pinned
+    cudaStream_t stream = nullptr;
+
+    ~Trainer() {
+        if (loss_host) cudaFreeHost(loss_host);
+        if (stream) cudaStreamDestroy(stream);
+    }
+
+    void init_common() {
+        K = num_sh_bases(degree) - 1;
+        const int64_t d[6] = {3, 2, 4, 3, 3LL * K, 1};
+        for (int g = 0; g < 6; ++g) {
+            counts[g] = d[g] * n;
+            params[g].alloc((size_t)counts[g]);
+            m[g].alloc((size_t)counts[g]);
+            v[g].alloc((size_t)counts[g]);
+        }
+        for (auto& s : stats) s.alloc((size_t)n);
+        loss_dev.alloc(1);
+        CKT(cudaHostAlloc(reinterpret_cast<void**>(&loss_host), sizeof(float), cudaHostAllocDefault));
+        CKT(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+        cam_indices.resize(ds->train.size());
+        std::iota(cam_indices.begin(), cam_indices.end(), 0);
+        shuffle();
+    }
+
+    void shuffle() {
+        std::shuffle(cam_indices.begin(), cam_indices.end(), rng);
+        cam_pos = 0;
+    }
+    size_t next_camera() {
+        if (cam_pos >= cam_indices.size()) shuffle();
+        return cam_indices[cam_pos++];
+    }
+
+    void upload(int g, const float* host) {
+        if (counts[g]) CKT(cudaMemcpy(params[g].p, host, counts[g] * sizeof(float), cudaMemcpyHostToDevice));
+    }
+
+    MsplatGaussians gaussians() {
+        MsplatGaussians G;
+        G.num_points = n;
+        G.sh_degree = degree;
+        G.means = params[0].p;
+        G.scales = params[1].p;
+        G.quats = params[2].p;
+        G.features_dc = params[3].p;
+        G.features_rest = K ? params[4].p : nullptr;
+        G.opacities = params[5].p;
+        return G;
+    }
+
+    int downscale_factor(int step) const {  // model.cpp:235-238
+        const int remaining = cfg.numDownscales - step / std::max(1, cfg.resolutionSchedule);
+        return 1 << std::max(remaining, 0);
+    }
+
+    MsplatCamera prepare(const Camera& c, int sf) const {  // model.cpp:500-544
+        const float f = (float)sf;
+        MsplatCamera cam;
+        check_rc(msplat_prepare_camera(c.c2w, c.fx / f, c.fy / f, c.cx / f, c.cy / f,
+                                       static_cast<int>(c.width / f), static_cast<int>(c.height / f), &cam));
+        return cam;
+    }
+
+    // Target image of a camera at downscale factor sf, on the device.
+    const float* target(const Camera& c, int sf, const MsplatCamera& cam) {
+        if (!c.image) throw ApiError("camera has no image");
+        const size_t full = (size_t)c.width * c.height * 3;
+        gt_full.ensure(full);
+        CKT(cudaMemcpyAsync(gt_full.p, c.image, full * sizeof(float), cudaMemcpyHostToDevice, stream));
+        if (sf == 1) return gt_full.p;
+        gt_scaled.ensure((size_t)cam.width * cam.height * 3);
+        launch_resize_area(gt_full.p, c.width, c.height, gt_scaled.p, cam.width, cam.height, stream);
+        return gt_scaled.p;
+    }
+
+    MsplatStats step() {  // Trainer::step, msplat_api.mm:106-128
+        if (ds->train.empty()) throw ApiError("dataset has no training cameras");
+        current_step++;
+        const Camera& c = ds->train[next_camera()];
+        const int sf = downscale_factor(current_step);
+        const MsplatCamera cam = prepare(c, sf);
+        const float* gt = target(c, sf, cam);
+        auto t0 = std::chrono::high_resolution_clock::now();
+        adam_step++;
+        MsplatAdamState A;
+        for (int g = 0; g < 6; ++g) {
+            A.exp_avg[g] = m[g].p;
+            A.exp_avg_sq[g] = v[g].p;
+            A.lr[g] = lr[g];
+        }
+        A.step = adam_step;
+        A.beta1 = 0.9f;
+        A.beta2 = 0.999f;
+        A.eps = 1e-8f;
+        const int degrees_to_use = std::min(current_step / std::max(1, cfg.shDegreeInterval), degree);
+        MsplatGaussians G = gaussians();
+        check_rc(msplat_train_step_fused(&G, &cam, degrees_to_use, cfg.bgColor, gt, 1.0f - cfg.ssimWeight, 0.0f,
+                                         cfg.ssimWeight, &A, stats[0].p, stats[1].p, stats[2].p, loss_dev.p, 0,
+                                         stream));
+        // schedulersStep (model.cpp:183-186); densification (afterTrain) is not part of this build
+        lr[0] = msplat_means_lr(current_step, cfg.iterations, means_lr_init, means_lr_final);
+        CKT(cudaMemcpyAsync(loss_host, loss_dev.p, sizeof(float), cudaMemcpyDeviceToHost, stream));
+        CKT(cudaStreamSynchronize(stream));
+        auto t1 = std::chrono::high_resolution_clock::now();
+        MsplatStats st;
+        st.iteration = current_step;
+        st.splatCount = n;
+        st.msPerStep = std::chrono::duration_cast<std::chrono::microseconds>(t1 - t0).count() / 1000.0f;
+        st.loss = *loss_host;
+        return st;
+    }
+
+    // Renders a camera; returns the device image and its camera.
+    const float* render_cam(const Camera& c, int step, MsplatCamera* out_cam) {
+        const int sf = downscale_factor(step);
+        const MsplatCamera cam = prepare(c, sf);
+        img.ensure((size_t)cam.width * cam.height * 3);
+        const int degrees_to_use = std::min(step / std::max(1, cfg.shDegreeInterval), degree);
+        MsplatGaussians G = gaussians();
+        check_rc(msplat_render(&G, &cam, 1.0f, 0.01f, degrees_to_use, cfg.bgColor, img.p, stream));
+        if (out_cam) *out_cam = cam;
+        return img.p;
+    }
+
+    MsplatPixelBuffer to_host(const float* dev, const MsplatCamera& cam) {
+        const size_t bytes = (size_t)cam.width * cam.height * 3 * sizeof(float);
+        float* buf = static_cast<float*>(std::malloc(bytes));
+        if (!buf) throw ApiError("out of host memory");
+        CKT(cudaMemcpyAsync(buf, dev, bytes, cudaMemcpyDeviceToHost, stream));
+        CKT(cudaStreamSynchronize(stream));
+        return MsplatPixelBuffer{buf, cam.width, cam.height};
+    }
+};
+
+// SSIM for evaluation (core/src/ssim.cpp:61-123): 11-tap sigma-1.5 window,
+// clamp-to-edge padding (unlike the training loss, which zero-pads).
+double ssim_eval(const std::vector<float>& r, const std::vector<float>& g, int H, int W) {
+    float kern[11], ks = 0.f;
+    for (int i = 0; i < 11; ++i) {
+        const float x = (float)(i - 5);
+        kern[i] = std::exp(-(x * x) / (2.0f * 1.5f * 1.5f));
+        ks += kern[i];
+    }
+    for (float& k : kern) k /= ks;
+    const int HW = H * W;
+    std::vector<float> a(HW), b(HW), aa(HW), bb(HW), ab(HW), tmp(HW), m1(HW), m2(HW), s11(HW), s22(HW), s12(HW);
+    auto blur = [&](const std::vector<float>& in, std::vector<float>& out) {
+        for (int y = 0; y < H; ++y)
+            for (int x = 0; x < W; ++x) {
+                float s = 0;
+                for (int k = 0; k < 11; ++k) s += in[y * W + std::min(std::max(x + k - 5, 0), W - 1)] * kern[k];
+                tmp[y * W + x] = s;
+            }
+        for (int y = 0; y < H; ++y)
+            for (int x = 0; x < W; ++x) {
+                float s = 0;
+                for (int k = 0; k < 11; ++k) s += tmp[std::min(std::max(y + k - 5, 0), H - 1) * W + x] * kern[k];
+                out[y * W + x] = s;
+            }
+    };
+    const float C1 = 0.01f * 0.01f, C2 = 0.03f * 0.03f;
+    double sum = 0;
+    for (int c = 0; c < 3; ++c) {
+        for (int i = 0; i < HW; ++i) {
+            a[i] = r[3 * i + c];
+            b[i] = g[3 * i + c];
+            aa[i] = a[i] * a[i];
+            bb[i] = b[i] * b[i];
+            ab[i] = a[i] * b[i];
+        }
+        blur(a, m1);
+        blur(b, m2);
+        blur(aa, s11);
+        blur(bb, s22);
+        blur(ab, s12);
+        for (int i = 0; i < HW; ++i) {
+            const float q11 = m1[i] * m1[i], q22 = m2[i] * m2[i], q12 = m1[i] * m2[i];
+            const float num = (2.0f * q12 + C1) * (2.0f * (s12[i] - q12) + C2);
+            const float den = (q11 + q22 + C1) * ((s11[i] - q11) + (s22[i] - q22) + C2);
+            sum += num / den;
+        }
+    }
+    return sum / (3.0 * HW);
+}
+
+template <typename R, typename F>
+R api(R fallback, F&& f) {
+    try {
+        R r = f();
+        set_last_error("");
+        return r;
+    } catch (const std::exception& e) {
+        set_last_error(e.what());
+        return fallback;
+    }
+}
+
+Trainer* T(MsplatTrainer t) {
+    if (!t) throw ApiError("null trainer");
+    return static_cast<Trainer*>(t);
+}
+Dataset* D(MsplatDataset d) {
+    if (!d) throw ApiError("null dataset");
+    return static_cast<Dataset*>(d);
+}
+
+}  // namespace
+}  // namespace msplat
+
+using namespace msplat;
+
+extern "C" {
+
+MsplatDataset msplat_dataset_create(const char* path, float, bool, int) {
+    set_last_error(
+        (std::string("dataset loaders (COLMAP, Nerfstudio, Polycam) are not part of this build; cannot load '") +
+         (path ? path : "") + "'; use msplat_dataset_create_from_memory")
+            .c_str());
+    return nullptr;
+}
+
+MsplatDataset msplat_dataset_create_from_memory(int numCameras, const float* camToWorld, const float* intrinsics,
+                                                int width, int height, const float* images, int numPoints,
+                                                const float* xyz, const uint8_t* rgb, bool evalMode,
+                                                int testEvery) {
+    return api<MsplatDataset>(nullptr, [&]() -> MsplatDataset {
+        if (numCameras < 0 || (numCameras > 0 && (!camToWorld || !intrinsics)) || width <= 0 || height <= 0 ||
+            numPoints < 0 || (numPoints > 0 && (!xyz || !rgb)))
+            throw ApiError("bad dataset arguments");
+        auto* ds = new Dataset();
+        const size_t img = (size_t)width * height * 3;
+        for (int i = 0; i < numCameras; ++i) {
+            Camera c;
+            std::memcpy(c.c2w, camToWorld + 16 * (size_t)i, sizeof(c.c2w));
+            c.fx = intrinsics[4 * i];
+            c.fy = intrinsics[4 * i + 1];
+            c.cx = intrinsics[4 * i + 2];
+            c.cy = intrinsics[4 * i + 3];
+            c.width = width;
+            c.height = height;
+            if (images) {
+                float* p = nullptr;
+                cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&p), img * sizeof(float), cudaHostAllocDefault);
+                if (e != cudaSuccess) {
+                    delete ds;
+                    throw ApiError(std::string("cudaHostAlloc: ") + cudaGetErrorString(e));
+                }
+                std::memcpy(p, images + img * i, img * sizeof(float));
+                ds->pinned.push_back(p);
+                c.image = p;
+            }
+            // InputData::splitTrainTest: every testEvery-th camera is a test camera
+            if (evalMode && testEvery > 0 && i % testEvery == 0)
+                ds->test.push_back(c);
+            else
+                ds->train.push_back(c);
+        }
+        ds->xyz.assign(xyz, xyz + 3 * (size_t)numPoints);
+        ds->rgb.assign(rgb, rgb + 3 * (size_t)numPoints);
+        return ds;
+    });
+}
+
+void msplat_dataset_destroy(MsplatDataset ds) { delete static_cast<Dataset*>(ds); }
+int msplat_dataset_num_train(MsplatDataset ds) { return api<int>(0, [&] { return (int)D(ds)->train.size(); }); }
+int msplat_dataset_num_test(MsplatDataset ds) { return api<int>(0, [&] { return (int)D(ds)->test.size(); }); }
+void msplat_dataset_camera_pose(MsplatDataset ds, int i, float camToWorld[16]) {
+    api<int>(0, [&] {
+        Dataset* d = D(ds);
+        if (i >= 0 && i < (int)d->train.size()) std::memcpy(camToWorld, d->train[i].c2w, 16 * sizeof(float));
+        return 0;
+    });
+}
+
+MsplatTrainer msplat_trainer_create(MsplatDataset dsh, MsplatConfig config) {
+    return api<MsplatTrainer>(nullptr, [&]() -> MsplatTrainer {
+        Dataset* ds = D(dsh);
+        if (config.shDegree < 0 || config.shDegree > 3) throw ApiError("shDegree must be 0..3");
+        auto* t = new Trainer();
+        try {
+            t->cfg = config;
+            t->ds = ds;
+            t->n = (int)(ds->xyz.size() / 3);
+            t->degree = config.shDegree;
+            t->init_common();
+            const int n = t->n, K = t->K;
+            // Model::Model, model.cpp:61-113
+            std::vector<float> scales(2 * (size_t)n), quats(4 * (size_t)n), dc(3 * (size_t)n),
+                rest((size_t)3 * K * n, 0.f), opac(n, std::log(0.1f / 0.9f));
+            const std::vector<float> knn = knn_mean_distance(ds->xyz);
+            for (int i = 0; i < n; ++i) scales[2 * i] = scales[2 * i + 1] = std::log(knn[i]);
+            std::mt19937 rng(42);
+            std::uniform_real_distribution<float> U(0.0f, 1.0f);
+            for (int i = 0; i < n; ++i) {
+                const float u = U(rng), vv = U(rng), w = U(rng);
+                quats[4 * i + 0] = std::sqrt(1 - u) * std::sin(2 * M_PI * vv);
+                quats[4 * i + 1] = std::sqrt(1 - u) * std::cos(2 * M_PI * vv);
+                quats[4 * i + 2] = std::sqrt(u) * std::sin(2 * M_PI * w);
+                quats[4 * i + 3] = std::sqrt(u) * std::cos(2 * M_PI * w);
+            }
+            for (int i = 0; i < 3 * n; ++i) dc[i] = (float)((ds->rgb[i] / 255.0 - 0.5) / kC0);
+            t->upload(0, ds->xyz.data());
+            t->upload(1, scales.data());
+            t->upload(2, quats.data());
+            t->upload(3, dc.data());
+            t->upload(4, rest.data());
+            t->upload(5, opac.data());
+        } catch (...) {
+            delete t;
+            throw;
+        }
+        return t;
+    });
+}
+
+MsplatTrainer msplat_trainer_create_from_params(MsplatDataset dsh, MsplatConfig config, int numPoints,
+                                                const float* means, const float* scales, const float* quats,
+                                                const float* opacities, const float* featuresDc,
+                                                const float* featuresRest) {
+    return api<MsplatTrainer>(nullptr, [&]() -> MsplatTrainer {
+        Dataset* ds = D(dsh);
+        if (config.shDegree < 0 || config.shDegree > 3) throw ApiError("shDegree must be 0..3");
+        if (numPoints < 0 || (numPoints > 0 && (!means || !scales || !quats || !opacities || !featuresDc)) ||
+            (numPoints > 0 && config.shDegree > 0 && !featuresRest))
+            throw ApiError("bad parameter arrays");
+        auto* t = new Trainer();
+        try {
+            t->cfg = config;
+            t->ds = ds;
+            t->n = numPoints;
+            t->degree = config.shDegree;
+            t->init_common();
+            t->upload(0, means);
+            t->upload(1, scales);
+            t->upload(2, quats);
+            t->upload(3, featuresDc);
+            if (t->K) t->upload(4, featuresRest);
+            t->upload(5, opacities);
+        } catch (...) {
+            delete t;
+            throw;
+        }
+        return t;
+    });
+}
+
+void msplat_trainer_destroy(MsplatTrainer t) { delete static_cast<Trainer*>(t); }
+
+MsplatStats msplat_trainer_step(MsplatTrainer t) {
+    return api<MsplatStats>(MsplatStats{0, 0, 0.f, 0.f}, [&] { return T(t)->step(); });
+}
+
+void msplat_trainer_train(MsplatTrainer t) {
+    api<int>(0, [&] {
+        Trainer* tr = T(t);
+        while (tr->current_step < tr->cfg.iterations) tr->step();
+        return 0;
+    });
+}
+
+MsplatEvalMetrics msplat_trainer_evaluate(MsplatTrainer t) {
+    return api<MsplatEvalMetrics>(MsplatEvalMetrics{0, 0, 0, 0, 0}, [&] {
+        Trainer* tr = T(t);
+        MsplatEvalMetrics mtr{0, 0, 0, 0, tr->n};
+        const auto& cams = tr->ds->test;
+        if (cams.empty()) return mtr;
+        double sp = 0, ss = 0, sl = 0;
+        for (const Camera& c : cams) {
+            MsplatCamera cam;
+            const float* dev = tr->render_cam(c, tr->cfg.iterations, &cam);
+            const size_t e = (size_t)cam.width * cam.height * 3;
+            std::vector<float> r(e), g(e);
+            CKT(cudaMemcpyAsync(r.data(), dev, e * 4, cudaMemcpyDeviceToHost, tr->stream));
+            const float* gt = tr->target(c, tr->downscale_factor(tr->cfg.iterations), cam);
+            CKT(cudaMemcpyAsync(g.data(), gt, e * 4, cudaMemcpyDeviceToHost, tr->stream));
+            CKT(cudaStreamSynchronize(tr->stream));
+            double mse = 0, l1 = 0;
+            for (size_t i = 0; i < e; ++i) {
+                const double d = (double)r[i] - g[i];
+                mse += d * d;
+                l1 += std::fabs(d);
+            }
+            sp += 10.0 * std::log10(1.0 / (mse / e));  // model.cpp:25-32
+            sl += l1 / e;
+            ss += ssim_eval(r, g, cam.height, cam.width);
+        }
+        mtr.psnr = (float)(sp / cams.size());
+        mtr.ssim = (float)(ss / cams.size());
+        mtr.l1 = (float)(sl / cams.size());
+        mtr.numTest = (int)cams.size();
+        return mtr;
+    });
+}
+
+MsplatPixelBuffer msplat_trainer_render(MsplatTrainer t, int cameraIndex, bool useTest) {
+    return api<MsplatPixelBuffer>(MsplatPixelBuffer{nullptr, 0, 0}, [&] {
+        Trainer* tr = T(t);
+        const auto& cams = useTest ? tr->ds->test : tr->ds->train;
+        if (cameraIndex < 0 || cameraIndex >= (int)cams.size()) return MsplatPixelBuffer{nullptr, 0, 0};
+        MsplatCamera cam;
+        const float* dev = tr->render_cam(cams[cameraIndex], tr->current_step, &cam);
+        return tr->to_host(dev, cam);
+    });
+}
+
+MsplatPixelBuffer msplat_trainer_render_pose(MsplatTrainer t, const float camToWorld[16], int refCameraIndex) {
+    return api<MsplatPixelBuffer>(MsplatPixelBuffer{nullptr, 0, 0}, [&] {
+        Trainer* tr = T(t);
+        const auto& cams = tr->ds->train;
+        if (refCameraIndex < 0 || refCameraIndex >= (int)cams.size()) return MsplatPixelBuffer{nullptr, 0, 0};
+        Camera c = cams[refCameraIndex];
+        std::memcpy(c.c2w, camToWorld, sizeof(c.c2w));
+        MsplatCamera cam;
+        const float* dev = tr->render_cam(c, tr->current_step, &cam);
+        return tr->to_host(dev, cam);
+    });
+}
+
+void msplat_trainer_render_pose_to_buffer(MsplatTrainer t, const float camToWorld[16], int refCameraIndex,
+                                          uint8_t* outRGBA, int* outWidth, int* outHeight) {
+    api<int>(0, [&] {
+        Trainer* tr = T(t);
+        const auto& cams = tr->ds->train;
+        if (refCameraIndex < 0 || refCameraIndex >= (int)cams.size()) {
+            *outWidth = 0;
+            *outHeight = 0;
+            return 0;
+        }
+        Camera c = cams[refCameraIndex];
+        std::memcpy(c.c2w, camToWorld, sizeof(c.c2w));
+        const int sf = tr->downscale_factor(tr->current_step);
+        *outWidth = static_cast<int>(c.width / (float)sf);
+        *outHeight = static_cast<int>(c.height / (float)sf);
+        if (!outRGBA) return 0;
+        MsplatCamera cam;
+        const float* dev = tr->render_cam(c, tr->current_step, &cam);
+        const int64_t px = (int64_t)cam.width * cam.height;
+        tr->rgba.ensure((size_t)px * 4);
+        launch_rgba8(dev, tr->rgba.p, px, tr->stream);
+        CKT(cudaMemcpyAsync(outRGBA, tr->rgba.p, (size_t)px * 4, cudaMemcpyDeviceToHost, tr->stream));
+        CKT(cudaStreamSynchronize(tr->stream));
+        return 0;
+    });
+}
+
+static void not_in_build(const char* what) {
+    set_last_error((std::string(what) + " is not part of this build").c_str());
+}
+
+void msplat_trainer_export_ply(MsplatTrainer, const char*) { not_in_build("PLY export"); }
+void msplat_trainer_export_splat(MsplatTrainer, const char*) { not_in_build(".splat export"); }
+int64_t msplat_trainer_extract_mesh(MsplatTrainer, const char*, float, float, float, float) {
+    not_in_build("mesh extraction (TSDF + marching cubes)");
+    return -1;
+}
+void msplat_trainer_save_checkpoint(MsplatTrainer, const char*) { not_in_build("checkpoint save"); }
+int msplat_trainer_load_checkpoint(MsplatTrainer, const char*) {
+    not_in_build("checkpoint load");
+    return -1;
+}
+int msplat_trainer_splat_count(MsplatTrainer t) { return api<int>(0, [&] { return T(t)->n; }); }
+int msplat_trainer_iteration(MsplatTrainer t) { return api<int>(0, [&] { return T(t)->current_step; }); }
+
+int msplat_trainer_get_params(MsplatTrainer t, float* means, float* scales, float* quats, float* opacities,
+                              float* featuresDc, float* featuresRest) {
+    return api<int>(-1, [&] {
+        Trainer* tr = T(t);
+        float* outs[6] = {means, scales, quats, featuresDc, featuresRest, opacities};
+        CKT(cudaStreamSynchronize(tr->stream));
+        for (int g = 0; g < 6; ++g)
+            if (outs[g] && tr->counts[g])
+                CKT(cudaMemcpy(outs[g], tr->params[g].p, tr->counts[g] * sizeof(float), cudaMemcpyDeviceToHost));
+        return 0;
+    });
+}
+
+void msplat_set_metallib_path(const char*) {}
+void msplat_sync(void) { cudaDeviceSynchronize(); }
+void msplat_cleanup(void) { msplat_backend_cleanup(); }
+
+}  // extern "C"
