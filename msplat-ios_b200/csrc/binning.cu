@@ -99,22 +99,59 @@ k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int row0, int ro
     }
 }
 
+// One warp per 32 consecutive Gaussians: their clipped tile rectangles are
+// flattened into (Gaussian, tile) pairs by a warp prefix sum of the areas, and
+// every lane takes one pair per round (owner found by a binary search over the
+// lanes' exclusive offsets), so a warp keeps 32 independent slot atomics in
+// flight whatever the rectangle sizes.
 __global__ void __launch_bounds__(256)
 k_emit_keys(int n, const uint2* __restrict__ rects, const float* __restrict__ depths, int tx, int row0, int row1,
             const int64_t* __restrict__ raw_start, int32_t* __restrict__ fill, uint64_t* __restrict__ keys) {
+    constexpr unsigned full = 0xffffffffu;
+    const int lane = threadIdx.x & 31;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const uint2 r = rects[i];
-    const int x0 = r.x & 0xFFFF, x1 = r.y & 0xFFFF;
-    const int y0 = max((int)(r.x >> 16), row0), y1 = min((int)(r.y >> 16), row1);
-    if (x1 <= x0 || y1 <= y0) return;
-    const uint64_t key = ((uint64_t)__float_as_uint(depths[i]) << 32) | (uint64_t)(uint32_t)i;
-    for (int y = y0; y < y1; ++y)
-        for (int x = x0; x < x1; ++x) {
-            const int t = y * tx + x;
-            const int slot = atomicAdd(&fill[t], 1);
-            keys[raw_start[t] + slot] = key;
+    int x0 = 0, y0 = 0, w = 0, area = 0;
+    uint64_t key = 0;
+    if (i < n) {
+        const uint2 r = rects[i];
+        x0 = r.x & 0xFFFF;
+        const int x1 = r.y & 0xFFFF;
+        y0 = max((int)(r.x >> 16), row0);
+        const int y1 = min((int)(r.y >> 16), row1);
+        w = x1 - x0;
+        if (w > 0 && y1 > y0) area = w * (y1 - y0);
+        key = ((uint64_t)__float_as_uint(depths[i]) << 32) | (uint64_t)(uint32_t)i;
+    }
+    int incl = area;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int v = __shfl_up_sync(full, incl, d);
+        if (lane >= d) incl += v;
+    }
+    const int total = __shfl_sync(full, incl, 31);
+    const int excl = incl - area;
+    for (int base = 0; base < total; base += 32) {
+        const int j = base + lane;
+        // owner: the last lane whose exclusive offset is <= j
+        int lo = 0;
+#pragma unroll
+        for (int step = 16; step > 0; step >>= 1) {
+            const int e = __shfl_sync(full, excl, lo + step);
+            if (lo + step < 32 && e <= j) lo += step;
         }
+        const int o_excl = __shfl_sync(full, excl, lo);
+        const int o_x0 = __shfl_sync(full, x0, lo);
+        const int o_y0 = __shfl_sync(full, y0, lo);
+        const int o_w = __shfl_sync(full, w, lo);
+        const unsigned long long o_key = __shfl_sync(full, (unsigned long long)key, lo);
+        if (j < total) {
+            const int local = j - o_excl;
+            const int ry = local / o_w;
+            const int t = (o_y0 + ry) * tx + o_x0 + (local - ry * o_w);
+            const int slot = atomicAdd(&fill[t], 1);
+            keys[__ldg(raw_start + t) + slot] = o_key;
+        }
+    }
 }
 
 constexpr int kSortThreads = 256;

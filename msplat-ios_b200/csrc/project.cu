@@ -240,12 +240,81 @@ __global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
     }
 }
 
-constexpr int kBwdThreads = 256;
+constexpr int kBwdThreads = 128;  // Gaussians per CTA
 
-// One CTA owns kBwdThreads consecutive Gaussians. Phase 0 stages their SH-rest
-// coefficients in shared memory with coalesced loads; phase 1 (one thread per
-// Gaussian) computes every gradient and applies Adam to the small groups;
-// phase 2 streams the SH-rest group through Adam with coalesced accesses.
+// Coalesced copy of n floats between global and shared memory (float4 when
+// both ends are 16-byte aligned).
+__device__ __forceinline__ void copy_in(float* dst, const float* __restrict__ src, int n) {
+    if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+        const int n4 = n >> 2;
+#pragma unroll 4
+        for (int q = threadIdx.x; q < n4; q += blockDim.x)
+            reinterpret_cast<float4*>(dst)[q] = __ldg(reinterpret_cast<const float4*>(src) + q);
+        for (int q = (n4 << 2) + threadIdx.x; q < n; q += blockDim.x) dst[q] = __ldg(src + q);
+    } else {
+        for (int q = threadIdx.x; q < n; q += blockDim.x) dst[q] = __ldg(src + q);
+    }
+}
+
+// Adam over n contiguous elements of one group; old parameters and gradients
+// come from shared memory, moments and new parameters stream through HBM.
+// When every global pointer is 16-byte aligned, each thread handles four
+// float4 chunks per iteration and issues all their moment loads before any
+// arithmetic, so enough bytes are in flight to saturate HBM.
+template <typename GradAt>
+__device__ __forceinline__ void adam_stream(int n, const float* sparam, GradAt grad, float* __restrict__ p,
+                                            float* __restrict__ m, float* __restrict__ v, float* __restrict__ gout,
+                                            float st, float b1, float b2, float bc, float eps, bool do_adam) {
+    const uintptr_t al = reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(m) |
+                         reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(gout);
+    int done = 0;
+    if (do_adam && (al & 15) == 0) {
+        constexpr int U = 4;
+        const int n4 = n >> 2;
+        const int step = blockDim.x * U;
+        for (int base = threadIdx.x; base < n4; base += step) {
+            float4 mm[U], vv[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = base + u * blockDim.x;
+                if (c < n4) {
+                    mm[u] = reinterpret_cast<const float4*>(m)[c];
+                    vv[u] = reinterpret_cast<const float4*>(v)[c];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = base + u * blockDim.x;
+                if (c >= n4) break;
+                const int e = c << 2;
+                const float g0 = grad(e), g1 = grad(e + 1), g2 = grad(e + 2), g3 = grad(e + 3);
+                float4 pp;
+                pp.x = adam_update(sparam[e], g0, &mm[u].x, &vv[u].x, st, b1, b2, bc, eps);
+                pp.y = adam_update(sparam[e + 1], g1, &mm[u].y, &vv[u].y, st, b1, b2, bc, eps);
+                pp.z = adam_update(sparam[e + 2], g2, &mm[u].z, &vv[u].z, st, b1, b2, bc, eps);
+                pp.w = adam_update(sparam[e + 3], g3, &mm[u].w, &vv[u].w, st, b1, b2, bc, eps);
+                reinterpret_cast<float4*>(p)[c] = pp;
+                reinterpret_cast<float4*>(m)[c] = mm[u];
+                reinterpret_cast<float4*>(v)[c] = vv[u];
+                if (gout) reinterpret_cast<float4*>(gout)[c] = make_float4(g0, g1, g2, g3);
+            }
+        }
+        done = n4 << 2;
+    }
+    for (int q = done + threadIdx.x; q < n; q += blockDim.x) {
+        const float g = grad(q);
+        if (gout) gout[q] = g;
+        if (do_adam) p[q] = adam_update(sparam[q], g, m + q, v + q, st, b1, b2, bc, eps);
+    }
+}
+
+// One CTA owns kBwdThreads consecutive Gaussians [b0, b0 + cnt).
+//  phase 0: stage their parameters and SH-rest coefficients in shared memory
+//           (contiguous, float4 loads);
+//  phase 1: one thread per Gaussian computes the projection and SH VJPs
+//           (project_and_sh_backward_2dgs_kernel) into shared memory;
+//  phase 2: Adam on every group as contiguous streams (fused_adam_kernel),
+//           so moments and parameters are read and written fully coalesced.
 __global__ void __launch_bounds__(kBwdThreads) k_project_backward(ProjBwdArgs a) {
     extern __shared__ float smem[];
     const int K = a.rest_bases;
@@ -253,35 +322,50 @@ __global__ void __launch_bounds__(kBwdThreads) k_project_backward(ProjBwdArgs a)
     const int b0 = a.g_begin + blockIdx.x * kBwdThreads;
     const int cnt = min(kBwdThreads, a.g_end - b0);
     if (cnt <= 0) return;
-    float* sR = smem;                              // [cnt * K3]
-    float* sB = sR + kBwdThreads * K3;             // [256][16]
-    float* sDC = sB + kBwdThreads * 16;            // [256][4]
-    const size_t rest0 = (size_t)b0 * K3;
-    for (int e = threadIdx.x; e < cnt * K3; e += kBwdThreads) sR[e] = a.f_rest[rest0 + e];
+    constexpr int T = kBwdThreads;
+    float* sMean = smem;            // [3T]
+    float* sScale = sMean + 3 * T;  // [2T]
+    float* sQuat = sScale + 2 * T;  // [4T]
+    float* sDc = sQuat + 4 * T;     // [3T]
+    float* sOp = sDc + 3 * T;       // [T]
+    float* gMean = sOp + T;         // [3T] gradients
+    float* gScale = gMean + 3 * T;  // [2T]
+    float* gQuat = gScale + 2 * T;  // [4T]
+    float* gDc = gQuat + 4 * T;     // [3T]
+    float* gOp = gDc + 3 * T;       // [T]
+    float* sB = gOp + T;            // [T][15] SH basis of the used bands
+    float* sDC = sB + 15 * T;       // [T][3] dL/d colour
+    float* sR = sDC + 3 * T;        // [T * K3] SH-rest coefficients
+    copy_in(sMean, a.means + 3 * (size_t)b0, 3 * cnt);
+    copy_in(sScale, a.scales + 2 * (size_t)b0, 2 * cnt);
+    copy_in(sQuat, a.quats + 4 * (size_t)b0, 4 * cnt);
+    copy_in(sDc, a.f_dc + 3 * (size_t)b0, 3 * cnt);
+    copy_in(sOp, a.opacities + (size_t)b0, cnt);
+    if (K3) copy_in(sR, a.f_rest + (size_t)b0 * K3, cnt * K3);
     __syncthreads();
 
     const int t = threadIdx.x;
-    const int i = b0 + t;
     if (t < cnt) {
+        const int i = b0 + t;
         const CameraDev& cam = a.cam;
         const float* pm = cam.projmat;
-        const float* gr = a.raster_grads + (size_t)i * kGradStride;
-        float dT[9];
-        for (int k = 0; k < 9; ++k) dT[k] = gr[k];
-        const float d_opac = gr[9];
-        float dC[3] = {gr[10], gr[11], gr[12]};
-        float dN[3] = {gr[13], gr[14], gr[15]};
+        const float4* gr4 = reinterpret_cast<const float4*>(a.raster_grads + (size_t)i * kGradStride);
+        const float4 q0 = __ldg(gr4), q1 = __ldg(gr4 + 1), q2 = __ldg(gr4 + 2), q3 = __ldg(gr4 + 3);
+        const float dT[9] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w, q2.x};
+        const float d_opac = q2.y;
+        float dC[3] = {q2.z, q2.w, q3.x};
+        const float dN[3] = {q3.y, q3.z, q3.w};
         float g_mean[3] = {0.f, 0.f, 0.f}, g_scale[2] = {0.f, 0.f}, g_quat[4] = {0.f, 0.f, 0.f, 0.f};
-        float g_dc[3] = {0.f, 0.f, 0.f}, g_m2[2] = {0.f, 0.f};
+        float g_m2[2] = {0.f, 0.f};
         float basis[15];
         int nb = 0;
         const int rad = a.radii[i];
         const float* myR = sR + t * K3;
         auto rest_at = [&](int k) { return myR[k]; };
         if (rad > 0) {
-            V3 p = v3(a.means[3 * i], a.means[3 * i + 1], a.means[3 * i + 2]);
-            float ex = det_exp(a.scales[2 * i]), ey = det_exp(a.scales[2 * i + 1]);
-            float q[4] = {a.quats[4 * i], a.quats[4 * i + 1], a.quats[4 * i + 2], a.quats[4 * i + 3]};
+            V3 p = v3(sMean[3 * t], sMean[3 * t + 1], sMean[3 * t + 2]);
+            float ex = det_exp(sScale[2 * t]), ey = det_exp(sScale[2 * t + 1]);
+            float q[4] = {sQuat[4 * t], sQuat[4 * t + 1], sQuat[4 * t + 2], sQuat[4 * t + 3]};
             V3 R[3];
             quat_to_rotmat(q, R);
             float sx = ex * a.glob_scale, sy = ey * a.glob_scale;
@@ -304,8 +388,8 @@ __global__ void __launch_bounds__(kBwdThreads) k_project_backward(ProjBwdArgs a)
             // quat_to_rotmat_vjp with v_R columns (dtuw*sx, dtvw*sy, dN).
             V3 c0 = scale3(dtuw, sx), c1 = scale3(dtvw, sy), c2 = v3(dN[0], dN[1], dN[2]);
             {
-                float s = 1.0f / sqrtf(q[3] * q[3] + q[0] * q[0] + q[1] * q[1] + q[2] * q[2]);
-                float w = q[0] * s, x = q[1] * s, y = q[2] * s, z = q[3] * s;
+                float s_ = 1.0f / sqrtf(q[3] * q[3] + q[0] * q[0] + q[1] * q[1] + q[2] * q[2]);
+                float w = q[0] * s_, x = q[1] * s_, y = q[2] * s_, z = q[3] * s_;
                 // R(c, r): column c, row r.
                 float R00 = c0.x, R01 = c0.y, R02 = c0.z, R10 = c1.x, R11 = c1.y, R12 = c1.z;
                 float R20 = c2.x, R21 = c2.y, R22 = c2.z;
@@ -317,7 +401,6 @@ __global__ void __launch_bounds__(kBwdThreads) k_project_backward(ProjBwdArgs a)
             V3 v = v3(p.x - cam.cam_pos[0], p.y - cam.cam_pos[1], p.z - cam.cam_pos[2]);
             float inv = 1.0f / sqrtf(dot3(v, v));
             V3 dir = scale3(v, inv);
-            for (int c = 0; c < 3; ++c) g_dc[c] = SH_C0 * dC[c];
             nb = sh_basis(a.degrees_to_use, dir, basis);
             if (a.degrees_to_use >= 1) {
                 V3 dd = sh_color_dL_ddir(a.degrees_to_use, dir, rest_at, dC);
@@ -341,49 +424,52 @@ __global__ void __launch_bounds__(kBwdThreads) k_project_backward(ProjBwdArgs a)
         } else {
             dC[0] = dC[1] = dC[2] = 0.f;
         }
-        for (int k = 0; k < 15; ++k) sB[t * 16 + k] = (k < nb) ? basis[k] : 0.f;
-        sDC[t * 4 + 0] = dC[0]; sDC[t * 4 + 1] = dC[1]; sDC[t * 4 + 2] = dC[2];
-        if (a.dL_dmean3D) {
-            for (int c = 0; c < 3; ++c) a.dL_dmean3D[3 * i + c] = g_mean[c];
-            for (int c = 0; c < 2; ++c) a.dL_dscale[2 * i + c] = g_scale[c];
-            for (int c = 0; c < 4; ++c) a.dL_dquat[4 * i + c] = g_quat[c];
-            for (int c = 0; c < 2; ++c) a.dL_dmean2D[2 * i + c] = g_m2[c];
-            for (int c = 0; c < 3; ++c) a.dL_dfeatures_dc[3 * i + c] = g_dc[c];
-            a.dL_dopacity[i] = d_opac;
+        for (int k = 0; k < 15; ++k) sB[t * 15 + k] = (k < nb) ? basis[k] : 0.f;
+        for (int c = 0; c < 3; ++c) {
+            sDC[t * 3 + c] = dC[c];
+            gMean[3 * t + c] = g_mean[c];
+            gDc[3 * t + c] = SH_C0 * dC[c];
         }
-        if (a.do_adam) {
-            const float b1 = a.beta1, b2 = a.beta2, bc = a.bc2_sqrt, eps = a.eps;
-            for (int c = 0; c < 3; ++c)
-                a.means[3 * i + c] = adam_update(a.means[3 * i + c], g_mean[c], &a.exp_avg[0][3 * i + c],
-                                                 &a.exp_avg_sq[0][3 * i + c], a.step_size[0], b1, b2, bc, eps);
-            for (int c = 0; c < 2; ++c)
-                a.scales[2 * i + c] = adam_update(a.scales[2 * i + c], g_scale[c], &a.exp_avg[1][2 * i + c],
-                                                  &a.exp_avg_sq[1][2 * i + c], a.step_size[1], b1, b2, bc, eps);
-            for (int c = 0; c < 4; ++c)
-                a.quats[4 * i + c] = adam_update(a.quats[4 * i + c], g_quat[c], &a.exp_avg[2][4 * i + c],
-                                                 &a.exp_avg_sq[2][4 * i + c], a.step_size[2], b1, b2, bc, eps);
-            for (int c = 0; c < 3; ++c)
-                a.f_dc[3 * i + c] = adam_update(a.f_dc[3 * i + c], g_dc[c], &a.exp_avg[3][3 * i + c],
-                                                &a.exp_avg_sq[3][3 * i + c], a.step_size[3], b1, b2, bc, eps);
-            a.opacities[i] = adam_update(a.opacities[i], d_opac, &a.exp_avg[5][i], &a.exp_avg_sq[5][i],
-                                         a.step_size[5], b1, b2, bc, eps);
+        gScale[2 * t] = g_scale[0]; gScale[2 * t + 1] = g_scale[1];
+        for (int c = 0; c < 4; ++c) gQuat[4 * t + c] = g_quat[c];
+        gOp[t] = d_opac;
+        if (a.dL_dmean2D) {
+            a.dL_dmean2D[2 * i] = g_m2[0];
+            a.dL_dmean2D[2 * i + 1] = g_m2[1];
         }
     }
-    if (K == 0) return;
     __syncthreads();
-    const float b1 = a.beta1, b2 = a.beta2, bc = a.bc2_sqrt, eps = a.eps, st = a.step_size[4];
-    float* m4 = a.do_adam ? a.exp_avg[4] : nullptr;
-    float* v4 = a.do_adam ? a.exp_avg_sq[4] : nullptr;
-    for (int e = threadIdx.x; e < cnt * K3; e += kBwdThreads) {
-        int gl = e / K3;
-        int r = e - gl * K3;
-        int k = r / 3;
-        int c = r - k * 3;
-        float g = sB[gl * 16 + k] * sDC[gl * 4 + c];
-        size_t ge = rest0 + e;
-        if (a.dL_dfeatures_rest) a.dL_dfeatures_rest[ge] = g;
-        if (a.do_adam) a.f_rest[ge] = adam_update(sR[e], g, m4 + ge, v4 + ge, st, b1, b2, bc, eps);
-    }
+    const bool ad = a.do_adam != 0;
+    const float b1 = a.beta1, b2 = a.beta2, bc = a.bc2_sqrt, eps = a.eps;
+    float* const* M = a.exp_avg;
+    float* const* Vv = a.exp_avg_sq;
+    const size_t i0 = (size_t)b0;
+    adam_stream(3 * cnt, sMean, [&](int q) { return gMean[q]; }, a.means + 3 * i0, ad ? M[0] + 3 * i0 : nullptr,
+                ad ? Vv[0] + 3 * i0 : nullptr, a.dL_dmean3D ? a.dL_dmean3D + 3 * i0 : nullptr, a.step_size[0], b1, b2,
+                bc, eps, ad);
+    adam_stream(2 * cnt, sScale, [&](int q) { return gScale[q]; }, a.scales + 2 * i0, ad ? M[1] + 2 * i0 : nullptr,
+                ad ? Vv[1] + 2 * i0 : nullptr, a.dL_dscale ? a.dL_dscale + 2 * i0 : nullptr, a.step_size[1], b1, b2,
+                bc, eps, ad);
+    adam_stream(4 * cnt, sQuat, [&](int q) { return gQuat[q]; }, a.quats + 4 * i0, ad ? M[2] + 4 * i0 : nullptr,
+                ad ? Vv[2] + 4 * i0 : nullptr, a.dL_dquat ? a.dL_dquat + 4 * i0 : nullptr, a.step_size[2], b1, b2,
+                bc, eps, ad);
+    adam_stream(3 * cnt, sDc, [&](int q) { return gDc[q]; }, a.f_dc + 3 * i0, ad ? M[3] + 3 * i0 : nullptr,
+                ad ? Vv[3] + 3 * i0 : nullptr, a.dL_dfeatures_dc ? a.dL_dfeatures_dc + 3 * i0 : nullptr,
+                a.step_size[3], b1, b2, bc, eps, ad);
+    adam_stream(cnt, sOp, [&](int q) { return gOp[q]; }, a.opacities + i0, ad ? M[5] + i0 : nullptr,
+                ad ? Vv[5] + i0 : nullptr, a.dL_dopacity ? a.dL_dopacity + i0 : nullptr, a.step_size[5], b1, b2, bc,
+                eps, ad);
+    if (K3)
+        adam_stream(cnt * K3, sR,
+                    [&](int q) {
+                        const int gl = q / K3;
+                        const int r = q - gl * K3;
+                        const int k = r / 3;
+                        return sB[gl * 15 + k] * sDC[gl * 3 + (r - k * 3)];
+                    },
+                    a.f_rest + i0 * K3, ad ? M[4] + i0 * K3 : nullptr, ad ? Vv[4] + i0 * K3 : nullptr,
+                    a.dL_dfeatures_rest ? a.dL_dfeatures_rest + i0 * K3 : nullptr, a.step_size[4], b1, b2, bc, eps,
+                    ad);
 }
 
 }  // namespace
@@ -397,12 +483,9 @@ void launch_project_forward(const ProjFwdArgs& a, cudaStream_t s) {
 void launch_project_backward(const ProjBwdArgs& a, cudaStream_t s) {
     int cnt = a.g_end - a.g_begin;
     if (cnt <= 0) return;
-    size_t smem = sizeof(float) * (size_t)(kBwdThreads * 3 * a.rest_bases + kBwdThreads * 16 + kBwdThreads * 4);
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
+    const size_t smem = sizeof(float) * (size_t)kBwdThreads * (26 + 15 + 3 + 3 * a.rest_bases);
+    if (smem > 48 * 1024)
         cudaFuncSetAttribute(k_project_backward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        configured = smem;
-    }
     note_launches(1);
     k_project_backward<<<(cnt + kBwdThreads - 1) / kBwdThreads, kBwdThreads, smem, s>>>(a);
 }

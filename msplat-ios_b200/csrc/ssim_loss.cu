@@ -65,82 +65,114 @@ __global__ void __launch_bounds__(kThreads) k_loss_ssim(LossArgs a) {
             sG[q] = vg;
         }
         __syncthreads();
-        // Horizontal blur of img, gt, img^2, gt^2, img*gt.
-        for (int q = threadIdx.x; q < IH * PW; q += kThreads) {
-            const int r = q / PW, cc = q - r * PW;
-            float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f, m4 = 0.f;
-            const float* pi = sI + r * IW + cc;
-            const float* pg = sG + r * IW + cc;
+        // Horizontal blur of img, gt, img^2, gt^2, img*gt; each work item is a
+        // run of HR outputs of one row, so the 11 taps are loaded once per run.
+        constexpr int HR = 6, HRUNS = PW / HR;  // 42 = 7 x 6
+        static_assert(PW % HR == 0, "run length");
+        for (int item = threadIdx.x; item < IH * HRUNS; item += kThreads) {
+            const int r = item / HRUNS, c0 = (item - r * HRUNS) * HR;
+            float xi[HR + 10], yi[HR + 10];
+            const float* pi = sI + r * IW + c0;
+            const float* pg = sG + r * IW + c0;
 #pragma unroll
-            for (int k = 0; k < 11; ++k) {
-                const float w = kW[k], x = pi[k], y = pg[k];
-                m0 += w * x;
-                m1 += w * y;
-                m2 += w * (x * x);
-                m3 += w * (y * y);
-                m4 += w * (x * y);
+            for (int k = 0; k < HR + 10; ++k) {
+                xi[k] = pi[k];
+                yi[k] = pg[k];
             }
-            hb[0 * IH * PW + q] = m0;
-            hb[1 * IH * PW + q] = m1;
-            hb[2 * IH * PW + q] = m2;
-            hb[3 * IH * PW + q] = m3;
-            hb[4 * IH * PW + q] = m4;
+#pragma unroll
+            for (int o = 0; o < HR; ++o) {
+                float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f, m4 = 0.f;
+#pragma unroll
+                for (int k = 0; k < 11; ++k) {
+                    const float w = kW[k], x = xi[o + k], y = yi[o + k];
+                    m0 += w * x;
+                    m1 += w * y;
+                    m2 += w * (x * x);
+                    m3 += w * (y * y);
+                    m4 += w * (x * y);
+                }
+                const int q = r * PW + c0 + o;
+                hb[0 * IH * PW + q] = m0;
+                hb[1 * IH * PW + q] = m1;
+                hb[2 * IH * PW + q] = m2;
+                hb[3 * IH * PW + q] = m3;
+                hb[4 * IH * PW + q] = m4;
+            }
         }
         __syncthreads();
-        // Vertical blur -> SSIM and its partials on the halo-5 region.
-        for (int q = threadIdx.x; q < PH * PW; q += kThreads) {
-            const int r = q / PW, cc = q - r * PW;
-            const int y = y0 - R + r, x = x0 - R + cc;
-            float mu1 = 0.f, mu2 = 0.f, b11 = 0.f, b22 = 0.f, b12 = 0.f;
+        // Vertical blur -> SSIM and its partials on the halo-5 region, runs of
+        // VR outputs down one column.
+        constexpr int VR = 4, VRUNS = (PH + VR - 1) / VR;  // 26 -> 7 runs (last one short)
+        for (int item = threadIdx.x; item < PW * VRUNS; item += kThreads) {
+            const int cc = item % PW, r0 = (item / PW) * VR;
+            float acc[5][VR];
 #pragma unroll
-            for (int k = 0; k < 11; ++k) {
-                const float w = kW[k];
-                const int o = (r + k) * PW + cc;
-                mu1 += w * hb[0 * IH * PW + o];
-                mu2 += w * hb[1 * IH * PW + o];
-                b11 += w * hb[2 * IH * PW + o];
-                b22 += w * hb[3 * IH * PW + o];
-                b12 += w * hb[4 * IH * PW + o];
+            for (int mm = 0; mm < 5; ++mm) {
+                float col[VR + 10];
+#pragma unroll
+                for (int k = 0; k < VR + 10; ++k) {
+                    const int rr = min(r0 + k, IH - 1);
+                    col[k] = hb[mm * IH * PW + rr * PW + cc];
+                }
+#pragma unroll
+                for (int o = 0; o < VR; ++o) {
+                    float sacc = 0.f;
+#pragma unroll
+                    for (int k = 0; k < 11; ++k) sacc += kW[k] * col[o + k];
+                    acc[mm][o] = sacc;
+                }
             }
-            float gm1 = 0.f, gs1 = 0.f, g12 = 0.f;
-            if (y >= 0 && y < H && x >= 0 && x < W) {
-                // Separately rounded operations: sigma1^2, sigma2^2 and sigma12
-                // must round identically where img == gt (flat background),
-                // where the reference's SSIM is exactly 1.
-                const float m1s = fmul(mu1, mu1), m2s = fmul(mu2, mu2), m1m2 = fmul(mu1, mu2);
-                const float v1 = fsub(b11, m1s), v2 = fsub(b22, m2s), v12 = fsub(b12, m1m2);
-                const float A = fadd(fmul(2.0f, m1m2), C1), B = fadd(fmul(2.0f, v12), C2);
-                const float Cd = fadd(fadd(m1s, m2s), C1), Dd = fadd(fadd(v1, v2), C2);
-                const float CD = fmul(Cd, Dd), AB = fmul(A, B);
-                const bool own = r >= R && r < R + OH && cc >= R && cc < R + OW && y < a.row_end;
-                if (own) ssim_sum += (double)(AB / CD);
-                const float inv_CD = 1.0f / CD, inv_Cd = 1.0f / Cd, inv_Dd = 1.0f / Dd;
-                const float d_mu1 = 2.0f * inv_CD * (mu2 * B - mu1 * AB * inv_Cd);
-                const float d_s12 = 2.0f * A * inv_CD;
-                const float d_s1 = -AB * inv_CD * inv_Dd;
-                gs1 = g * d_s1;
-                g12 = g * d_s12;
-                gm1 = g * d_mu1 + gs1 * (-2.0f * mu1) + g12 * (-mu2);
+#pragma unroll
+            for (int o = 0; o < VR; ++o) {
+                const int r = r0 + o;
+                if (r >= PH) break;
+                const int y = y0 - R + r, x = x0 - R + cc;
+                const float mu1 = acc[0][o], mu2 = acc[1][o], b11 = acc[2][o], b22 = acc[3][o], b12 = acc[4][o];
+                float gm1 = 0.f, gs1 = 0.f, g12 = 0.f;
+                if (y >= 0 && y < H && x >= 0 && x < W) {
+                    // Separately rounded operations: sigma1^2, sigma2^2 and sigma12
+                    // must round identically where img == gt (flat background),
+                    // where the reference's SSIM is exactly 1.
+                    const float m1s = fmul(mu1, mu1), m2s = fmul(mu2, mu2), m1m2 = fmul(mu1, mu2);
+                    const float v1 = fsub(b11, m1s), v2 = fsub(b22, m2s), v12 = fsub(b12, m1m2);
+                    const float A = fadd(fmul(2.0f, m1m2), C1), B = fadd(fmul(2.0f, v12), C2);
+                    const float Cd = fadd(fadd(m1s, m2s), C1), Dd = fadd(fadd(v1, v2), C2);
+                    const float CD = fmul(Cd, Dd), AB = fmul(A, B);
+                    const bool own = r >= R && r < R + OH && cc >= R && cc < R + OW && y < a.row_end;
+                    if (own) ssim_sum += (double)(AB / CD);
+                    const float inv_CD = 1.0f / CD, inv_Cd = 1.0f / Cd, inv_Dd = 1.0f / Dd;
+                    const float d_mu1 = 2.0f * inv_CD * (mu2 * B - mu1 * AB * inv_Cd);
+                    const float d_s12 = 2.0f * A * inv_CD;
+                    const float d_s1 = -AB * inv_CD * inv_Dd;
+                    gs1 = g * d_s1;
+                    g12 = g * d_s12;
+                    gm1 = g * d_mu1 + gs1 * (-2.0f * mu1) + g12 * (-mu2);
+                }
+                const int q = r * PW + cc;
+                pmap[0 * PH * PW + q] = gm1;
+                pmap[1 * PH * PW + q] = gs1;
+                pmap[2 * PH * PW + q] = g12;
             }
-            pmap[0 * PH * PW + q] = gm1;
-            pmap[1 * PH * PW + q] = gs1;
-            pmap[2 * PH * PW + q] = g12;
         }
         __syncthreads();
-        for (int q = threadIdx.x; q < PH * OW; q += kThreads) {
-            const int r = q / OW, cc = q - r * OW;
-            float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+        // Horizontal blur of the partials, runs of PR outputs.
+        constexpr int PR = 4, PRUNS = OW / PR;
+        for (int item = threadIdx.x; item < PH * PRUNS; item += kThreads) {
+            const int r = item / PRUNS, c0 = (item - r * PRUNS) * PR;
 #pragma unroll
-            for (int k = 0; k < 11; ++k) {
-                const float w = kW[k];
-                const int o = r * PW + cc + k;
-                s0 += w * pmap[0 * PH * PW + o];
-                s1 += w * pmap[1 * PH * PW + o];
-                s2 += w * pmap[2 * PH * PW + o];
+            for (int mm = 0; mm < 3; ++mm) {
+                float row[PR + 10];
+                const float* src = pmap + mm * PH * PW + r * PW + c0;
+#pragma unroll
+                for (int k = 0; k < PR + 10; ++k) row[k] = src[k];
+#pragma unroll
+                for (int o = 0; o < PR; ++o) {
+                    float sacc = 0.f;
+#pragma unroll
+                    for (int k = 0; k < 11; ++k) sacc += kW[k] * row[o + k];
+                    hp[mm * PH * OW + r * OW + c0 + o] = sacc;
+                }
             }
-            hp[0 * PH * OW + q] = s0;
-            hp[1 * PH * OW + q] = s1;
-            hp[2 * PH * OW + q] = s2;
         }
         __syncthreads();
         for (int q = threadIdx.x; q < OH * OW; q += kThreads) {
