@@ -76,7 +76,7 @@ struct Workspace {
     Buf dL_dmean3D, dL_dscale, dL_dquat, dL_dmean2D, dL_dfeatures_dc, dL_dfeatures_rest, dL_dopacity;
     Buf dL_dtransMat, dL_dnormal3D, dL_dcolors;
     // per tile / intersection
-    Buf tile_diff, raw_counts, raw_start, tile_bins, fill, raw_keys, gaussian_ids;
+    Buf tile_diff, raw_counts, raw_start, tile_bins, fill, raw_keys, gaussian_ids, blend_mask;
     // per pixel
     Buf final_Ts, final_idx, out_img, out_depth, out_normal, out_alpha, out_median, out_dist, dL_dout_img;
     // scalars
@@ -102,7 +102,7 @@ struct Workspace {
                       &normal_opacity, &colors, &aabb, &dL_dmean3D, &dL_dscale, &dL_dquat, &dL_dmean2D,
                       &dL_dfeatures_dc, &dL_dfeatures_rest, &dL_dopacity, &dL_dtransMat, &dL_dnormal3D,
                       &dL_dcolors, &tile_diff, &raw_counts, &raw_start, &tile_bins, &fill, &raw_keys,
-                      &gaussian_ids, &final_Ts, &final_idx, &out_img, &out_depth, &out_normal, &out_alpha,
+                      &gaussian_ids, &blend_mask, &final_Ts, &final_idx, &out_img, &out_depth, &out_normal, &out_alpha,
                       &out_median, &out_dist, &dL_dout_img, &loss_partials, &loss_out, &loss_f, &err, &totals, &row_work};
         for (Buf* b : all) b->release();
         for (auto& set : ev_pending)
@@ -322,6 +322,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     w.kept = kept;
     w.raw_keys.ensure((size_t)(raw_total > 0 ? raw_total : 1) * sizeof(uint64_t));
     w.gaussian_ids.ensure((size_t)(kept > 0 ? kept : 1) * sizeof(int32_t));
+    w.blend_mask.ensure((size_t)(kept > 0 ? kept : 1));
     mark(w, kStEmit, s);
     launch_emit_keys(n, w.rects.as<uint2>(), w.depths.as<float>(), tx, row0, row1, w.raw_start.as<int64_t>(),
                      w.fill.as<int32_t>(), w.raw_keys.as<uint64_t>(), s);
@@ -338,6 +339,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     ra.out_depth = w.out_depth.as<float>(); ra.out_normal = w.out_normal.as<float>();
     ra.out_alpha = w.out_alpha.as<float>(); ra.out_median_depth = w.out_median.as<float>();
     ra.out_distortion = w.out_dist.as<float>();
+    ra.blend_mask = w.blend_mask.as<uint8_t>();
     mark(w, kStRasterFwd, s);
     launch_rasterize_forward(ra, s);
     w.have_pixels = true;
@@ -383,6 +385,7 @@ void stage_raster_backward(Workspace& w, const CameraDev& cam, const float bg[3]
     ba.dL_dout_img = w.dL_dout_img.as<float>();
     ba.dL_dout_distortion = ldist * (1.0f / (float)(cam.height * cam.width * 3)) * 3.0f;  // lambda_dist / HW
     ba.raster_grads = raster_grads;
+    ba.blend_mask = w.blend_mask.as<uint8_t>();
     mark(w, kStRasterBwd, s);
     launch_rasterize_backward(ba, s);
 }

@@ -92,6 +92,9 @@ struct RasterFwdArgs {
     float bg[3];
     float* final_Ts; int32_t* final_idx; float* out_img; float* out_depth; float* out_normal;
     float* out_alpha; float* out_median_depth; float* out_distortion;
+    // [kept intersections] one byte per tile-list entry: bit w set when warp w
+    // of the tile's CTA blended that surfel (read by the backward)
+    uint8_t* blend_mask;
 };
 void launch_rasterize_forward(const RasterFwdArgs& a, cudaStream_t s);
 
@@ -108,6 +111,7 @@ struct RasterBwdArgs {
     const float* dL_dout_median_depth;
     float dL_dout_distortion;            // uniform per-pixel distortion gradient
     float* raster_grads;                 // [N, 16] (+=)
+    const uint8_t* blend_mask;           // written by the forward over the same tiles
 };
 void launch_rasterize_backward(const RasterBwdArgs& a, cudaStream_t s);
 

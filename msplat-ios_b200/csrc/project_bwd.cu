@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(kBwdThreads) k_project_backward(ProjBwdArgs a)
     copy_in(sQuat, a.quats + 4 * (size_t)b0, 4 * cnt);
     copy_in(sDc, a.f_dc + 3 * (size_t)b0, 3 * cnt);
     copy_in(sOp, a.opacities + (size_t)b0, cnt);
-    if (K3) copy_in(sR, a.f_rest + (size_t)b0 * K3, cnt * K3);
+    if constexpr (K3 > 0) copy_in(sR, a.f_rest + (size_t)b0 * K3, cnt * K3);
     __syncthreads();
 
     const int t = threadIdx.x;
@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(kBwdThreads) k_project_backward(ProjBwdArgs a)
     adam_stream(cnt, sOp, [&](int q) { return gOp[q]; }, a.opacities + i0, ad ? M[5] + i0 : nullptr,
                 ad ? Vv[5] + i0 : nullptr, a.dL_dopacity ? a.dL_dopacity + i0 : nullptr, a.step_size[5], b1, b2, bc,
                 eps, ad);
-    if (K3)
+    if constexpr (K3 > 0)
         adam_stream(cnt * K3, sR,
                     [&](int q) {
                         const int gl = q / K3;

@@ -13,10 +13,17 @@
 // 8x8 groups per tile, each re-reading the tile list); the tile's surfels are
 // streamed in batches of 256: ids are read coalesced, the 80-byte per-Gaussian
 // records (written once by the projection) are gathered into shared memory
-// structure-of-arrays, and every thread walks the batch. In the backward the
-// per-(pixel, surfel) gradients are summed across the warp with a recursive
-// halving exchange (16 values in 16 shuffles), across warps in shared memory,
-// and leave the CTA as four float4 atomics per surfel.
+// structure-of-arrays. Each warp owns an 8x4 pixel block: it tests 32 surfel
+// boxes at a time (one per lane), and walks only the surfels whose box meets
+// its block. The forward records, per tile-list entry, which warps blended
+// the surfel (one bit per warp); the backward drops entries no warp blended
+// and each warp visits only its own, so pairs that were rejected in the
+// forward are not evaluated again. In the backward the per-(pixel, surfel)
+// gradients are summed across the warp with a recursive halving exchange
+// (16 values in 16 shuffles), across warps in shared memory, and leave the
+// CTA as four float4 atomics per surfel. The replayed pair evaluation uses
+// the forward's exact operation sequence; the gradient arithmetic after it
+// uses fast reciprocals.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -26,7 +33,7 @@ namespace {
 constexpr int kThreads = 256;
 
 struct Pair {
-    float u, v, pz, rho3d, rho2d, depth, G, alpha;
+    float u, v, inv_z, rho3d, rho2d, depth, G, alpha;
     float kx, ky, kz, lx, ly, lz;
 };
 
@@ -65,7 +72,7 @@ __device__ __forceinline__ bool eval_pair(float px, float py, float4 r0, float4 
     const float og = fmul(r2.w, G);
     const float alpha = (og < 0.99f) ? og : 0.99f;
     if (alpha < 1.0f / 255.0f) return false;
-    e.u = u; e.v = v; e.pz = p_z; e.rho3d = rho3d; e.rho2d = rho2d; e.depth = depth; e.G = G; e.alpha = alpha;
+    e.u = u; e.v = v; e.inv_z = inv_z; e.rho3d = rho3d; e.rho2d = rho2d; e.depth = depth; e.G = G; e.alpha = alpha;
     e.kx = kx; e.ky = ky; e.kz = kz; e.lx = lx; e.ly = ly; e.lz = lz;
     return true;
 }
@@ -111,15 +118,31 @@ __device__ __forceinline__ int4 surfel_box(float4 r0, float4 r1, float4 r2, floa
     return make_int4(to_pix(floorf(x0)), to_pix(floorf(y0)), to_pix(ceilf(x1)), to_pix(ceilf(y1)));
 }
 
-__global__ void __launch_bounds__(kThreads, 5) k_raster_fwd(RasterFwdArgs a) {
+// Packs the per-warp blend flags of batch entry threadIdx.x (one byte per
+// warp in sflag) into one bit per warp and stores it for tile-list entry
+// b0 + threadIdx.x.
+__device__ __forceinline__ void flush_blend_flags(uint8_t* mask, const uint2* sflag, int b0, int end) {
+    const int idx = b0 + threadIdx.x;
+    if (idx >= end) return;
+    const uint2 f = sflag[threadIdx.x];
+    uint32_t m = 0;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) m |= (((f.x >> (8 * w)) & 1u) << w) | (((f.y >> (8 * w)) & 1u) << (w + 4));
+    mask[idx] = (uint8_t)m;
+}
+
+__global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
     __shared__ float4 srec[kRecordF4][kThreads];
     __shared__ float srmax[kThreads];
     __shared__ int4 sbox[kThreads];
+    __shared__ uint2 sflag[kThreads];  // per batch entry: byte w set when warp w blended it
+    constexpr unsigned full = 0xffffffffu;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int tile = (a.tile_row_begin + blockIdx.y) * a.tiles_x + blockIdx.x;
     const int lx = tile_lx(threadIdx.x), ly = tile_ly(threadIdx.x);
     // this warp's 8x4 pixel block
-    const int wx0 = blockIdx.x * kTile + ((threadIdx.x >> 5) & 1) * 8, wx1 = wx0 + 7;
-    const int wy0 = (a.tile_row_begin + blockIdx.y) * kTile + (threadIdx.x >> 6) * 4, wy1 = wy0 + 3;
+    const int wx0 = blockIdx.x * kTile + (warp & 1) * 8, wx1 = wx0 + 7;
+    const int wy0 = (a.tile_row_begin + blockIdx.y) * kTile + (warp >> 1) * 4, wy1 = wy0 + 3;
     const int j = blockIdx.x * kTile + lx;
     const int i = (a.tile_row_begin + blockIdx.y) * kTile + ly;
     const bool inside = (i < a.height) && (j < a.width);
@@ -134,8 +157,12 @@ __global__ void __launch_bounds__(kThreads, 5) k_raster_fwd(RasterFwdArgs a) {
     int median_c = -1, contributor = 0, last_c = 0;
     bool done = !inside;
 
+    int flush_b0 = -1;  // batch whose blend flags are still in sflag
     for (int b0 = range.x; b0 < range.y; b0 += kThreads) {
-        if (__syncthreads_count(done) == kThreads) break;
+        const bool all_done = __syncthreads_count(done) == kThreads;
+        if (flush_b0 >= 0) flush_blend_flags(a.blend_mask, sflag, flush_b0, range.y);
+        flush_b0 = -1;
+        if (all_done) break;
         const int idx = b0 + threadIdx.x;
         if (idx < range.y) {
             const int g = a.gaussian_ids[idx];
@@ -147,45 +174,65 @@ __global__ void __launch_bounds__(kThreads, 5) k_raster_fwd(RasterFwdArgs a) {
             srmax[threadIdx.x] = rm;
             sbox[threadIdx.x] = surfel_box(q[0], q[1], q[2], rm);
         }
+        sflag[threadIdx.x] = make_uint2(0u, 0u);
         __syncthreads();
-        if (done) continue;
+        flush_b0 = b0;
+        if (__all_sync(full, done)) continue;
         const int bs = min(kThreads, range.y - b0);
         const int base = b0 - range.x + 1;  // 1-based position of surfel 0 of this batch in the tile list
-        for (int s = 0; s < bs; ++s) {
-            const int4 box = sbox[s];
-            if (box.x > wx1 || box.z < wx0 || box.y > wy1 || box.w < wy0) continue;  // whole warp
-            if (j < box.x || j > box.z || i < box.y || i > box.w) continue;
-            Pair e;
-            const float4 r2 = srec[2][s];
-            if (!eval_pair(px, py, srec[0][s], srec[1][s], r2, srmax[s], e)) continue;
-            contributor = base + s;
-            const float next_T = fmul(T, fsub(1.0f, e.alpha));
-            if (next_T <= 1e-4f) {
-                done = true;
-                break;
+        // 32 surfels at a time: one box test per lane, then the warp walks
+        // the surfels whose box meets its 8x4 pixel block
+        for (int c = 0; c < bs; c += 32) {
+            bool hit = false;
+            if (c + lane < bs) {
+                const int4 box = sbox[c + lane];
+                hit = !(box.x > wx1 || box.z < wx0 || box.y > wy1 || box.w < wy0);
             }
-            const float w = fmul(e.alpha, T);
-            const float A = fsub(1.f, T);
-            const float m = fmul(mscale, fsub(1.f, __fdiv_rn(kNearN, e.depth)));
-            const float mm = fmul(m, m);
-            dist = ffma(fsub(fadd(fmul(mm, A), M2), fmul(fmul(2.f, m), M1)), w, dist);
-            M1 = ffma(m, w, M1);
-            M2 = ffma(mm, w, M2);
-            if (T > 0.5f) {
-                median_depth = e.depth;
-                median_c = contributor;
+            unsigned bits = __ballot_sync(full, hit);
+            while (bits) {
+                const int s = c + __ffs(bits) - 1;
+                bits &= bits - 1;
+                if (done) continue;
+                const int4 box = sbox[s];
+                if (j < box.x || j > box.z || i < box.y || i > box.w) continue;
+                Pair e;
+                const float4 r2 = srec[2][s];
+                if (!eval_pair(px, py, srec[0][s], srec[1][s], r2, srmax[s], e)) continue;
+                contributor = base + s;
+                const float next_T = fmul(T, fsub(1.0f, e.alpha));
+                if (next_T <= 1e-4f) {
+                    done = true;
+                    continue;
+                }
+                const float w = fmul(e.alpha, T);
+                const float A = fsub(1.f, T);
+                const float m = fmul(mscale, fsub(1.f, __fdiv_rn(kNearN, e.depth)));
+                const float mm = fmul(m, m);
+                dist = ffma(fsub(fadd(fmul(mm, A), M2), fmul(fmul(2.f, m), M1)), w, dist);
+                M1 = ffma(m, w, M1);
+                M2 = ffma(mm, w, M2);
+                if (T > 0.5f) {
+                    median_depth = e.depth;
+                    median_c = contributor;
+                }
+                const float4 r3 = srec[3][s], r4 = srec[4][s];
+                cr = ffma(r3.x, w, cr);
+                cg = ffma(r3.y, w, cg);
+                cb = ffma(r3.z, w, cb);
+                pdepth = ffma(e.depth, w, pdepth);
+                nx = ffma(r3.w, w, nx);
+                ny = ffma(r4.x, w, ny);
+                nz = ffma(r4.y, w, nz);
+                T = next_T;
+                last_c = contributor;
+                reinterpret_cast<uint8_t*>(&sflag[s])[warp] = 1;
             }
-            const float4 r3 = srec[3][s], r4 = srec[4][s];
-            cr = ffma(r3.x, w, cr);
-            cg = ffma(r3.y, w, cg);
-            cb = ffma(r3.z, w, cb);
-            pdepth = ffma(e.depth, w, pdepth);
-            nx = ffma(r3.w, w, nx);
-            ny = ffma(r4.x, w, ny);
-            nz = ffma(r4.y, w, nz);
-            T = next_T;
-            last_c = contributor;
+            if (__all_sync(full, done)) break;
         }
+    }
+    if (flush_b0 >= 0) {
+        __syncthreads();
+        flush_blend_flags(a.blend_mask, sflag, flush_b0, range.y);
     }
     if (!inside) return;
     const size_t pix = (size_t)i * a.width + j;
@@ -245,17 +292,18 @@ template <bool AUX>
 __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
     __shared__ float4 srec[kRecordF4][kThreads];
     __shared__ float srmax[kThreads];
-    __shared__ int4 sbox[kThreads];
     __shared__ int sid[kThreads];
+    __shared__ int srel[kThreads];       // 0-based position in the tile list
+    __shared__ uint8_t smask[kThreads];  // warps that blended the surfel in the forward
     __shared__ float sacc[kThreads][kGradStride];
+    __shared__ int swarp_cnt[kThreads / 32];
     __shared__ int s_max_last;
-    const int lane = threadIdx.x & 31;
+    constexpr unsigned full = 0xffffffffu;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int tile_row = a.tile_row_begin + blockIdx.y;
     const int tile = tile_row * a.tiles_x + blockIdx.x;
     const int j = blockIdx.x * kTile + tile_lx(threadIdx.x);
     const int i = tile_row * kTile + tile_ly(threadIdx.x);
-    const int wx0 = blockIdx.x * kTile + ((threadIdx.x >> 5) & 1) * 8, wx1 = wx0 + 7;
-    const int wy0 = tile_row * kTile + (threadIdx.x >> 6) * 4, wy1 = wy0 + 3;
     const bool inside = (i < a.height) && (j < a.width);
     const float px = (float)j, py = (float)i;
     const int2 range = a.tile_bins[tile];
@@ -299,104 +347,122 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
 
     for (int bend = hi; bend > range.x; bend -= kThreads) {
         const int bs = min(kThreads, bend - range.x);
+        __syncthreads();  // the previous batch is consumed
+        // entries blended by no warp are dropped; the rest are compacted in
+        // back-to-front order
+        const int rel_t = bend - 1 - (int)threadIdx.x - range.x;
+        const uint32_t m = ((int)threadIdx.x < bs) ? a.blend_mask[range.x + rel_t] : 0u;
+        const unsigned bal = __ballot_sync(full, m != 0u);
+        if (lane == 0) swarp_cnt[warp] = __popc(bal);
         __syncthreads();
-        if ((int)threadIdx.x < bs) {
-            const int g = a.gaussian_ids[bend - 1 - threadIdx.x];
-            sid[threadIdx.x] = g;
+        int off = 0, total = 0;
+#pragma unroll
+        for (int w = 0; w < kThreads / 32; ++w) {
+            const int c = swarp_cnt[w];
+            off += (w < warp) ? c : 0;
+            total += c;
+        }
+        if (m != 0u) {
+            const int pos = off + __popc(bal & ((1u << lane) - 1u));
+            const int g = a.gaussian_ids[range.x + rel_t];
+            sid[pos] = g;
+            srel[pos] = rel_t;
+            smask[pos] = (uint8_t)m;
             const float4* r = a.records + (size_t)g * kRecordF4;
             float4 q[kRecordF4];
 #pragma unroll
-            for (int k = 0; k < kRecordF4; ++k) srec[k][threadIdx.x] = q[k] = __ldg(r + k);
-            const float rm = reject_rho(q[2].w);
-            srmax[threadIdx.x] = rm;
-            sbox[threadIdx.x] = surfel_box(q[0], q[1], q[2], rm);
+            for (int k = 0; k < kRecordF4; ++k) srec[k][pos] = q[k] = __ldg(r + k);
+            srmax[pos] = reject_rho(q[2].w);
         }
+        if ((int)threadIdx.x < total) {
 #pragma unroll
-        for (int k = 0; k < kGradStride; ++k) sacc[threadIdx.x][k] = 0.f;
+            for (int k = 0; k < kGradStride; ++k) sacc[threadIdx.x][k] = 0.f;
+        }
         __syncthreads();
-        for (int s = 0; s < bs; ++s) {
-            const int4 box = sbox[s];
-            if (box.x > wx1 || box.z < wx0 || box.y > wy1 || box.w < wy0) continue;  // whole warp
-            const int rel = bend - 1 - s - range.x;
-            const bool in_box = j >= box.x && j <= box.z && i >= box.y && i <= box.w;
-            float g[16];
+        for (int c = 0; c < total; c += 32) {
+            unsigned bits = __ballot_sync(full, c + lane < total && ((smask[c + lane] >> warp) & 1u));
+            while (bits) {
+                const int s = c + __ffs(bits) - 1;
+                bits &= bits - 1;
+                const int rel = srel[s];
+                float g[16];
 #pragma unroll
-            for (int k = 0; k < 16; ++k) g[k] = 0.f;
-            bool contrib = false;
-            Pair e;
-            const float4 r0 = srec[0][s], r1 = srec[1][s], r2 = srec[2][s];
-            if (in_box && rel < last_c && eval_pair(px, py, r0, r1, r2, srmax[s], e)) {
-                contrib = true;
-                const float4 r3 = srec[3][s], r4 = srec[4][s];
-                const float alpha = e.alpha, G = e.G, opa = r2.w;
-                T = T / (1.0f - alpha);
-                const float w = alpha * T;
-                float dL_dalpha = 0.f;
-                const float col[3] = {r3.x, r3.y, r3.z};
+                for (int k = 0; k < 16; ++k) g[k] = 0.f;
+                Pair e;
+                const float4 r0 = srec[0][s], r1 = srec[1][s], r2 = srec[2][s];
+                if (rel < last_c && eval_pair(px, py, r0, r1, r2, srmax[s], e)) {
+                    const float4 r3 = srec[3][s], r4 = srec[4][s];
+                    const float alpha = e.alpha, G = e.G, opa = r2.w;
+                    const float r1ma = __fdividef(1.0f, 1.0f - alpha);
+                    T = T * r1ma;
+                    const float w = alpha * T;
+                    float dL_dalpha = 0.f;
+                    const float col[3] = {r3.x, r3.y, r3.z};
 #pragma unroll
-                for (int c = 0; c < 3; ++c) {
-                    accum_rec[c] = last_alpha * last_color[c] + (1.f - last_alpha) * accum_rec[c];
-                    last_color[c] = col[c];
-                    dL_dalpha += (col[c] - accum_rec[c]) * dpix[c];
-                    g[10 + c] = col[c] > 0.f ? w * dpix[c] : 0.f;
-                }
-                float dL_dz = 0.f;
-                if (AUX) {
-                    const float m_d = mscale * (1.0f - kNearN / e.depth);
-                    const float dmd_dd = (kFarN * kNearN) / ((kFarN - kNearN) * e.depth * e.depth);
-                    if (rel == median_c - 1) dL_dz += dL_dmed;
-                    const float dL_dweight = (final_D2 + m_d * m_d * final_A - 2.0f * m_d * final_D) * dL_dreg;
-                    dL_dalpha += dL_dweight - last_dL_dT;
-                    last_dL_dT = dL_dweight * alpha + (1.0f - alpha) * last_dL_dT;
-                    const float dL_dmd = 2.0f * (T * alpha) * (m_d * final_A - final_D) * dL_dreg;
-                    dL_dz += dL_dmd * dmd_dd;
-                    accum_depth_rec = last_alpha * last_depth + (1.f - last_alpha) * accum_depth_rec;
-                    last_depth = e.depth;
-                    dL_dalpha += (e.depth - accum_depth_rec) * dL_ddepth;
-                    accum_alpha_rec = last_alpha + (1.f - last_alpha) * accum_alpha_rec;
-                    dL_dalpha += (1.0f - accum_alpha_rec) * dL_daccum;
-                    const float nrm[3] = {r3.w, r4.x, r4.y};
-#pragma unroll
-                    for (int c = 0; c < 3; ++c) {
-                        accum_normal_rec[c] = last_alpha * last_normal[c] + (1.f - last_alpha) * accum_normal_rec[c];
-                        last_normal[c] = nrm[c];
-                        dL_dalpha += (nrm[c] - accum_normal_rec[c]) * dnorm2[c];
-                        g[13 + c] = w * dnorm2[c];
+                    for (int c3 = 0; c3 < 3; ++c3) {
+                        accum_rec[c3] = last_alpha * last_color[c3] + (1.f - last_alpha) * accum_rec[c3];
+                        last_color[c3] = col[c3];
+                        dL_dalpha += (col[c3] - accum_rec[c3]) * dpix[c3];
+                        g[10 + c3] = col[c3] > 0.f ? w * dpix[c3] : 0.f;
                     }
+                    float dL_dz = 0.f;
+                    if (AUX) {
+                        const float rd = __fdividef(1.0f, e.depth);
+                        const float m_d = mscale * (1.0f - kNearN * rd);
+                        const float dmd_dd = ((kFarN * kNearN) / (kFarN - kNearN)) * rd * rd;
+                        if (rel == median_c - 1) dL_dz += dL_dmed;
+                        const float dL_dweight = (final_D2 + m_d * m_d * final_A - 2.0f * m_d * final_D) * dL_dreg;
+                        dL_dalpha += dL_dweight - last_dL_dT;
+                        last_dL_dT = dL_dweight * alpha + (1.0f - alpha) * last_dL_dT;
+                        const float dL_dmd = 2.0f * (T * alpha) * (m_d * final_A - final_D) * dL_dreg;
+                        dL_dz += dL_dmd * dmd_dd;
+                        accum_depth_rec = last_alpha * last_depth + (1.f - last_alpha) * accum_depth_rec;
+                        last_depth = e.depth;
+                        dL_dalpha += (e.depth - accum_depth_rec) * dL_ddepth;
+                        accum_alpha_rec = last_alpha + (1.f - last_alpha) * accum_alpha_rec;
+                        dL_dalpha += (1.0f - accum_alpha_rec) * dL_daccum;
+                        const float nrm[3] = {r3.w, r4.x, r4.y};
+#pragma unroll
+                        for (int c3 = 0; c3 < 3; ++c3) {
+                            accum_normal_rec[c3] = last_alpha * last_normal[c3] + (1.f - last_alpha) * accum_normal_rec[c3];
+                            last_normal[c3] = nrm[c3];
+                            dL_dalpha += (nrm[c3] - accum_normal_rec[c3]) * dnorm2[c3];
+                            g[13 + c3] = w * dnorm2[c3];
+                        }
+                    }
+                    dL_dalpha *= T;
+                    last_alpha = alpha;
+                    dL_dalpha += (-T_final * r1ma) * bg_dot;
+                    const float dL_dG = opa * dL_dalpha;
+                    if (AUX) dL_dz += w * dL_ddepth;
+                    if (e.rho3d <= e.rho2d) {
+                        const float dsx = -dL_dG * G * e.u + dL_dz * r1.z;
+                        const float dsy = -dL_dG * G * e.v + dL_dz * r1.w;
+                        const float dpx = dsx * e.inv_z, dpy = dsy * e.inv_z;
+                        const float dpz = -(dpx * e.u + dpy * e.v);
+                        // dk = cross(l, dp), dl = cross(dp, k)
+                        const float dkx = e.ly * dpz - e.lz * dpy, dky = e.lz * dpx - e.lx * dpz, dkz = e.lx * dpy - e.ly * dpx;
+                        const float dlx = dpy * e.kz - dpz * e.ky, dly = dpz * e.kx - dpx * e.kz, dlz = dpx * e.ky - dpy * e.kx;
+                        g[0] = -dkx; g[1] = -dky; g[2] = -dkz;
+                        g[3] = -dlx; g[4] = -dly; g[5] = -dlz;
+                        g[6] = px * dkx + py * dlx + dL_dz * e.u;
+                        g[7] = px * dky + py * dly + dL_dz * e.v;
+                        g[8] = px * dkz + py * dlz + dL_dz;
+                    } else if (AUX) {
+                        g[6] = e.u * dL_dz;
+                        g[7] = e.v * dL_dz;
+                        g[8] = dL_dz;
+                    }
+                    g[9] = G * dL_dalpha * (opa * (1.0f - opa));
                 }
-                dL_dalpha *= T;
-                last_alpha = alpha;
-                dL_dalpha += (-T_final / (1.f - alpha)) * bg_dot;
-                const float dL_dG = opa * dL_dalpha;
-                if (AUX) dL_dz += w * dL_ddepth;
-                if (e.rho3d <= e.rho2d) {
-                    const float dsx = -dL_dG * G * e.u + dL_dz * r1.z;
-                    const float dsy = -dL_dG * G * e.v + dL_dz * r1.w;
-                    const float dpx = dsx / e.pz, dpy = dsy / e.pz;
-                    const float dpz = -(dpx * e.u + dpy * e.v);
-                    // dk = cross(l, dp), dl = cross(dp, k)
-                    const float dkx = e.ly * dpz - e.lz * dpy, dky = e.lz * dpx - e.lx * dpz, dkz = e.lx * dpy - e.ly * dpx;
-                    const float dlx = dpy * e.kz - dpz * e.ky, dly = dpz * e.kx - dpx * e.kz, dlz = dpx * e.ky - dpy * e.kx;
-                    g[0] = -dkx; g[1] = -dky; g[2] = -dkz;
-                    g[3] = -dlx; g[4] = -dly; g[5] = -dlz;
-                    g[6] = px * dkx + py * dlx + dL_dz * e.u;
-                    g[7] = px * dky + py * dly + dL_dz * e.v;
-                    g[8] = px * dkz + py * dlz + dL_dz;
-                } else if (AUX) {
-                    g[6] = e.u * dL_dz;
-                    g[7] = e.v * dL_dz;
-                    g[8] = dL_dz;
-                }
-                g[9] = G * dL_dalpha * (opa * (1.0f - opa));
-            }
-            if (__any_sync(0xffffffffu, contrib)) {
+                // the forward's flags guarantee a contributing lane here
                 const float tot = warp_halving_sum16(g, lane);
                 const int vi = lane >> 1;
                 if (!(lane & 1) && (AUX || vi < 13) && tot != 0.f) atomicAdd(&sacc[s][vi], tot);
             }
         }
         __syncthreads();
-        for (int q = threadIdx.x; q < bs * 4; q += kThreads) {
+        for (int q = threadIdx.x; q < total * 4; q += kThreads) {
             const int s = q >> 2, part = q & 3;
             const float4 v = make_float4(sacc[s][4 * part], sacc[s][4 * part + 1], sacc[s][4 * part + 2],
                                          sacc[s][4 * part + 3]);
