@@ -26,8 +26,15 @@ constexpr float kFarN = 100.0f;
 //   r1 = (Tv.y, Tv.z, Tw.x, Tw.y)
 //   r2 = (Tw.z, xy.x, xy.y, sigmoid(opacity))
 //   r3 = (rgb.r, rgb.g, rgb.b, normal.x)   rgb = max(raw SH colour + 0.5, 0)
-//   r4 = (normal.y, normal.z, 0, 0)
+//   r4 = (normal.y, normal.z, rmax, 0)   rmax = reject_rho(sigmoid(opacity))
 constexpr int kRecordF4 = 5;
+
+// Rho above which a surfel of opacity o is certainly skipped by the 1/255
+// alpha cut: o * exp(-rho/2) < 1/255 for rho > 2 ln(255 o); the +0.01 margin
+// covers the rounding of det_exp and of this bound. Negative for o < 1/255.
+__device__ __forceinline__ float reject_rho(float opac) {
+    return opac > 0.f ? 2.0f * logf(255.0f * opac) + 0.01f : -1.0f;
+}
 
 // Per-Gaussian raster-space gradient record accumulated by the backward
 // rasteriser: 16 floats = 4 x float4.

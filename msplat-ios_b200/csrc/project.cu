@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
     rec[1] = make_float4(T1.y, T1.z, T2.x, T2.y);
     rec[2] = make_float4(T2.z, cxp, cyp, opac);
     rec[3] = make_float4(rgb[0], rgb[1], rgb[2], nrm.x);
-    rec[4] = make_float4(nrm.y, nrm.z, 0.f, 0.f);
+    rec[4] = make_float4(nrm.y, nrm.z, reject_rho(opac), 0.f);
     if (a.num_tiles_hit) {
         a.num_tiles_hit[i] = area;
         a.xys[2 * i] = cxp; a.xys[2 * i + 1] = cyp;

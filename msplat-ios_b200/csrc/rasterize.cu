@@ -37,12 +37,6 @@ struct Pair {
     float kx, ky, kz, lx, ly, lz;
 };
 
-// Rho above which a surfel of opacity o is certainly skipped by the 1/255
-// alpha cut: o * exp(-rho/2) < 1/255 for rho > 2 ln(255 o); the +0.01 margin
-// covers the rounding of det_exp and of this bound. Negative for o < 1/255.
-__device__ __forceinline__ float reject_rho(float opac) {
-    return opac > 0.f ? 2.0f * logf(255.0f * opac) + 0.01f : -1.0f;
-}
 
 // Per-(pixel, surfel) evaluation with a pinned IEEE operation sequence
 // (identical in the forward and the backward replay, and in the CPU checker).
@@ -133,7 +127,6 @@ __device__ __forceinline__ void flush_blend_flags(uint8_t* mask, const uint2* sf
 
 __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
     __shared__ float4 srec[kRecordF4][kThreads];
-    __shared__ float srmax[kThreads];
     __shared__ int4 sbox[kThreads];
     __shared__ uint2 sflag[kThreads];  // per batch entry: byte w set when warp w blended it
     constexpr unsigned full = 0xffffffffu;
@@ -170,9 +163,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
             float4 q[kRecordF4];
 #pragma unroll
             for (int k = 0; k < kRecordF4; ++k) srec[k][threadIdx.x] = q[k] = __ldg(r + k);
-            const float rm = reject_rho(q[2].w);
-            srmax[threadIdx.x] = rm;
-            sbox[threadIdx.x] = surfel_box(q[0], q[1], q[2], rm);
+            sbox[threadIdx.x] = surfel_box(q[0], q[1], q[2], q[4].z);
         }
         sflag[threadIdx.x] = make_uint2(0u, 0u);
         __syncthreads();
@@ -193,11 +184,11 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
                 const int s = c + __ffs(bits) - 1;
                 bits &= bits - 1;
                 if (done) continue;
-                const int4 box = sbox[s];
-                if (j < box.x || j > box.z || i < box.y || i > box.w) continue;
+                // no per-pixel box test: the box meets this warp's block, so
+                // the warp evaluates the surfel anyway, and eval_pair's exact
+                // early rejection covers the pixels outside the box
                 Pair e;
-                const float4 r2 = srec[2][s];
-                if (!eval_pair(px, py, srec[0][s], srec[1][s], r2, srmax[s], e)) continue;
+                if (!eval_pair(px, py, srec[0][s], srec[1][s], srec[2][s], srec[4][s].z, e)) continue;
                 contributor = base + s;
                 const float next_T = fmul(T, fsub(1.0f, e.alpha));
                 if (next_T <= 1e-4f) {
@@ -291,7 +282,6 @@ __device__ __forceinline__ float warp_halving_sum16(float (&v)[16], int lane) {
 template <bool AUX>
 __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
     __shared__ float4 srec[kRecordF4][kThreads];
-    __shared__ float srmax[kThreads];
     __shared__ int sid[kThreads];
     __shared__ int srel[kThreads];       // 0-based position in the tile list
     __shared__ uint8_t smask[kThreads];  // warps that blended the surfel in the forward
@@ -369,10 +359,8 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
             srel[pos] = rel_t;
             smask[pos] = (uint8_t)m;
             const float4* r = a.records + (size_t)g * kRecordF4;
-            float4 q[kRecordF4];
 #pragma unroll
-            for (int k = 0; k < kRecordF4; ++k) srec[k][pos] = q[k] = __ldg(r + k);
-            srmax[pos] = reject_rho(q[2].w);
+            for (int k = 0; k < kRecordF4; ++k) srec[k][pos] = __ldg(r + k);
         }
         if ((int)threadIdx.x < total) {
 #pragma unroll
@@ -390,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
                 for (int k = 0; k < 16; ++k) g[k] = 0.f;
                 Pair e;
                 const float4 r0 = srec[0][s], r1 = srec[1][s], r2 = srec[2][s];
-                if (rel < last_c && eval_pair(px, py, r0, r1, r2, srmax[s], e)) {
+                if (rel < last_c && eval_pair(px, py, r0, r1, r2, srec[4][s].z, e)) {
                     const float4 r3 = srec[3][s], r4 = srec[4][s];
                     const float alpha = e.alpha, G = e.G, opa = r2.w;
                     const float r1ma = __fdividef(1.0f, 1.0f - alpha);
