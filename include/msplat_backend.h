@@ -161,10 +161,10 @@ int msplat_shard_project_backward_adam(const MsplatGaussians* g, const MsplatCam
  * memory at run time (hosts whose GPU memory all comes from their own pool
  * allocator, or that fix their memory budget at start-up): it calls no
  * cudaMalloc/cudaFree and no allocating library routine. Its scratch lives in
- * fixed arrays inside the library's device image, about 1.5 MiB held by every
+ * fixed arrays inside the library's device image, about 192 KiB held by every
  * GPU that loads the library until the process exits, which limits images to
- * 65,536 blocks of 32x16 pixels (e.g. 8192 x 4096); larger sizes are rejected
- * with MSPLAT_ERR_ARGUMENT. Inputs and outputs are caller-owned device
+ * 8192 loss blocks (54-column strips: widths up to 442,368 pixels); wider
+ * images are rejected with MSPLAT_ERR_ARGUMENT. Inputs and outputs are caller-owned device
  * memory: out_img and gt [H,W,3], out_distortion [H,W] (may be NULL when
  * lambda_dist == 0), dL_dout_img [H,W,3] (written), loss_out one float
  * (written, may be NULL). The first call on a device looks up the scratch

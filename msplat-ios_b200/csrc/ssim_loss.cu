@@ -9,14 +9,27 @@
 // dL/dssim = -lambda_dssim / (3HW) uniform, dL/dimg = lambda_l1 * sign(r-g) /
 // (3HW) + blur(g_mu1) + 2 img blur(g_sigma1^2) + gt blur(g_sigma12).
 //
-// One CTA produces a 32x16 tile of dL/dimg for one channel at a time: it
-// stages the rendered and target images with a 10-pixel halo in shared
-// memory, blurs the five moment maps horizontally then vertically over a
-// 5-pixel halo, evaluates SSIM and its per-pixel partials there (zero outside
-// the image, as the adjoint of zero padding requires), and blurs the partials
-// back to the tile. The image and target are read once (plus halo) and
-// dL/dimg is written once; no [H,W,3] intermediate touches HBM. Loss partial
-// sums are reduced per CTA in double and summed in a fixed order afterwards.
+// One CTA walks down a strip of SW = 54 output columns over a segment of
+// rows, for all three channels at once, one image row per step:
+//   S1  load image and target row r (columns x0-10 .. x0+SW+10) into shared
+//       memory (double-buffered);
+//   S2  blur row r-1 horizontally: the five moments img, gt, img^2, gt^2,
+//       img*gt for the 64 columns x0-5 .. x0+SW+5;
+//   S3  blur vertically over the last 11 moment rows, evaluate SSIM and its
+//       three per-pixel partials at row r-6 (zero outside the image, as the
+//       adjoint of zero padding requires);
+//   S4  blur the partials of row r-7 horizontally onto the SW output columns;
+//   S5  blur them vertically over the last 11 rows and write dL/dimg of row
+//       r-12, together with the L1 term.
+// Each thread owns one (channel, column) item of S2/S3 and one of S4/S5; the
+// 11-row windows of its moments and partials live in registers (the step loop
+// is unrolled 11 times so that every ring index is a constant), so the only
+// shared-memory traffic is the horizontal taps. The only recomputed halo is
+// 10 columns per strip and 22 rows per segment. The image and target are read
+// once and dL/dimg is written once; no [H,W,3] intermediate touches HBM. Loss
+// partial sums are reduced per CTA in double and summed in a fixed order
+// afterwards.
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -31,116 +44,147 @@ __constant__ float kW[11] = {0.001028380084f, 0.007598758135f, 0.036000772128f, 
                              0.213005537711f, 0.266011724862f, 0.213005537711f, 0.109360689510f,
                              0.036000772128f, 0.007598758135f, 0.001028380084f};
 
-constexpr int OW = 32, OH = 16, R = 5;
-constexpr int IW = OW + 4 * R, IH = OH + 4 * R;  // input region (halo 10)
-constexpr int PW = OW + 2 * R, PH = OH + 2 * R;  // partial region (halo 5)
-constexpr int kThreads = 256;
-constexpr int kSmemFloats = 2 * IH * IW + 5 * IH * PW + 3 * PH * PW + 3 * PH * OW;
+constexpr int R = 5;
+constexpr int CW = 64;             // columns of moments and partials per strip
+constexpr int SW = CW - 2 * R;     // output columns per strip
+constexpr int IWID = SW + 4 * R;   // input columns per strip
+constexpr int kThreads = 3 * CW;   // one thread per (channel, column) of S2/S3
+constexpr int kOutItems = 3 * SW;  // threads with an S4/S5 item
+constexpr int kRing = 2 * R + 1;   // rows in a vertical window
+constexpr int kTargetBlocks = 4 * 148;
+constexpr int kMinSegRows = 16;
 
-__global__ void __launch_bounds__(kThreads) k_loss_ssim(LossArgs a) {
-    extern __shared__ float sm[];
-    float* sI = sm;                     // [IH][IW]
-    float* sG = sI + IH * IW;           // [IH][IW]
-    float* hb = sG + IH * IW;           // [5][IH][PW]
-    float* pmap = hb + 5 * IH * PW;     // [3][PH][PW]
-    float* hp = pmap + 3 * PH * PW;     // [3][PH][OW]
+struct LossGrid {
+    int strips, segs, seg_rows;
+};
+
+// Strips x row segments: about kTargetBlocks CTAs, segments of at least
+// kMinSegRows rows.
+LossGrid loss_grid(int width, int rows) {
+    LossGrid g;
+    g.strips = (width + SW - 1) / SW;
+    int segs = (kTargetBlocks + g.strips - 1) / g.strips;
+    segs = std::max(1, std::min(segs, (rows + kMinSegRows - 1) / kMinSegRows));
+    g.seg_rows = (rows + segs - 1) / segs;
+    g.segs = (rows + g.seg_rows - 1) / g.seg_rows;
+    return g;
+}
+
+__global__ void __launch_bounds__(kThreads, 2) k_loss_ssim(LossArgs a, int seg_rows) {
+    __shared__ float sIn[2][2][3][IWID];  // [buffer][image, target][channel][column]
+    __shared__ float sP[2][3][3][CW];     // [buffer][partial][channel][column]
+    __shared__ double red[3][kThreads];
     const int W = a.width, H = a.height;
-    const int x0 = blockIdx.x * OW;
-    const int y0 = a.row_begin + blockIdx.y * OH;
+    const int t = threadIdx.x;
+    const int ch = t / CW, col = t - ch * CW;      // S2/S3 item
+    const bool out_item = t < kOutItems;
+    const int och = t / SW, ocol = t - och * SW;   // S4/S5 item
+    const int x0 = blockIdx.x * SW;
+    const int Y0 = a.row_begin + blockIdx.y * seg_rows;
+    const int Y1 = min(Y0 + seg_rows, a.row_end);
+    const int ybase = Y0 - 2 * R;  // input row of step 0
+    const int nsteps = (Y1 - Y0) + 4 * R + 2;
+    const int xm = x0 - R + col;   // image column of the S2/S3 item
+    const int xo = x0 + ocol;      // image column of the S4/S5 item
+    const bool own_col = col >= R && col < R + SW && xm < W;
     const float C1 = 0.0001f, C2 = 0.0009f;
     const float g = -a.lambda_dssim * a.inv_num;
     double l1_sum = 0.0, ssim_sum = 0.0, dist_sum = 0.0;
 
-    for (int c = 0; c < 3; ++c) {
-        for (int q = threadIdx.x; q < IH * IW; q += kThreads) {
-            const int r = q / IW, cc = q - r * IW;
-            const int y = y0 - 2 * R + r, x = x0 - 2 * R + cc;
-            float vi = 0.f, vg = 0.f;
-            if (y >= 0 && y < H && x >= 0 && x < W) {
-                const size_t e = ((size_t)y * W + x) * 3 + c;
-                vi = a.out_img[e];
-                vg = a.gt[e];
+    float hm[kRing][5], hp[kRing][3];
+#pragma unroll
+    for (int k = 0; k < kRing; ++k) {
+#pragma unroll
+        for (int m = 0; m < 5; ++m) hm[k][m] = 0.f;
+#pragma unroll
+        for (int m = 0; m < 3; ++m) hp[k][m] = 0.f;
+    }
+    // S1 of one row: each thread moves up to two (image, target) pairs of the
+    // contiguous span [x0-10, x0+SW+10) x 3 channels
+    constexpr int kSpan = 3 * IWID;
+    static_assert(kSpan <= 2 * kThreads, "two loads per thread");
+    auto fetch = [&](int y, float (&v)[2][2]) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int q = t + u * kThreads;
+            const int xx = x0 - 2 * R + q / 3;
+            v[u][0] = 0.f;
+            v[u][1] = 0.f;
+            if (q < kSpan && y >= 0 && y < H && xx >= 0 && xx < W) {
+                const size_t e = ((size_t)y * W + xx) * 3 + (q - (q / 3) * 3);
+                v[u][0] = __ldg(a.out_img + e);
+                v[u][1] = __ldg(a.gt + e);
             }
-            sI[q] = vi;
-            sG[q] = vg;
         }
-        __syncthreads();
-        // Horizontal blur of img, gt, img^2, gt^2, img*gt; each work item is a
-        // run of HR outputs of one row, so the 11 taps are loaded once per run.
-        constexpr int HR = 6, HRUNS = PW / HR;  // 42 = 7 x 6
-        static_assert(PW % HR == 0, "run length");
-        for (int item = threadIdx.x; item < IH * HRUNS; item += kThreads) {
-            const int r = item / HRUNS, c0 = (item - r * HRUNS) * HR;
-            float xi[HR + 10], yi[HR + 10];
-            const float* pi = sI + r * IW + c0;
-            const float* pg = sG + r * IW + c0;
+    };
+    auto stash = [&](int buf, const float (&v)[2][2]) {
 #pragma unroll
-            for (int k = 0; k < HR + 10; ++k) {
-                xi[k] = pi[k];
-                yi[k] = pg[k];
+        for (int u = 0; u < 2; ++u) {
+            const int q = t + u * kThreads;
+            if (q < kSpan) {
+                const int c = q % 3, xc = q / 3;
+                sIn[buf][0][c][xc] = v[u][0];
+                sIn[buf][1][c][xc] = v[u][1];
             }
+        }
+    };
+    {
+        float v[2][2];
+        fetch(ybase, v);
+        stash(0, v);
+    }
+    __syncthreads();
+
+    for (int t0 = 0; t0 < nsteps; t0 += kRing) {
 #pragma unroll
-            for (int o = 0; o < HR; ++o) {
+        for (int k = 0; k < kRing; ++k) {
+            const int step = t0 + k;  // sIn[step & 1] holds input row ybase + step
+            // S1 (issued first, stored last): input row ybase + step + 1
+            float nv[2][2];
+            fetch(ybase + step + 1, nv);
+            // S2: moments of input row ybase + step
+            {
+                const float* pi = &sIn[step & 1][0][ch][col];
+                const float* pg = &sIn[step & 1][1][ch][col];
                 float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f, m4 = 0.f;
 #pragma unroll
-                for (int k = 0; k < 11; ++k) {
-                    const float w = kW[k], x = xi[o + k], y = yi[o + k];
+                for (int j = 0; j < kRing; ++j) {
+                    const float w = kW[j], x = pi[j], y = pg[j];
                     m0 += w * x;
                     m1 += w * y;
                     m2 += w * (x * x);
                     m3 += w * (y * y);
                     m4 += w * (x * y);
                 }
-                const int q = r * PW + c0 + o;
-                hb[0 * IH * PW + q] = m0;
-                hb[1 * IH * PW + q] = m1;
-                hb[2 * IH * PW + q] = m2;
-                hb[3 * IH * PW + q] = m3;
-                hb[4 * IH * PW + q] = m4;
+                float* slot = hm[k];
+                slot[0] = m0; slot[1] = m1; slot[2] = m2; slot[3] = m3; slot[4] = m4;
             }
-        }
-        __syncthreads();
-        // Vertical blur -> SSIM and its partials on the halo-5 region, runs of
-        // VR outputs down one column.
-        constexpr int VR = 4, VRUNS = (PH + VR - 1) / VR;  // 26 -> 7 runs (last one short)
-        for (int item = threadIdx.x; item < PW * VRUNS; item += kThreads) {
-            const int cc = item % PW, r0 = (item / PW) * VR;
-            float acc[5][VR];
+            // S3: SSIM partials of row ybase + step - 5 from moment rows
+            // ybase + step - 10 .. ybase + step (ring slots k+1 .. k+11)
+            {
+                const int cy = ybase + step - R;
+                float acc[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int mm = 0; mm < 5; ++mm) {
-                float col[VR + 10];
+                for (int j = 0; j < kRing; ++j) {
+                    const float w = kW[j];
+                    const float* slot = hm[(k + 1 + j) % kRing];
 #pragma unroll
-                for (int k = 0; k < VR + 10; ++k) {
-                    const int rr = min(r0 + k, IH - 1);
-                    col[k] = hb[mm * IH * PW + rr * PW + cc];
+                    for (int m = 0; m < 5; ++m) acc[m] += w * slot[m];
                 }
-#pragma unroll
-                for (int o = 0; o < VR; ++o) {
-                    float sacc = 0.f;
-#pragma unroll
-                    for (int k = 0; k < 11; ++k) sacc += kW[k] * col[o + k];
-                    acc[mm][o] = sacc;
-                }
-            }
-#pragma unroll
-            for (int o = 0; o < VR; ++o) {
-                const int r = r0 + o;
-                if (r >= PH) break;
-                const int y = y0 - R + r, x = x0 - R + cc;
-                const float mu1 = acc[0][o], mu2 = acc[1][o], b11 = acc[2][o], b22 = acc[3][o], b12 = acc[4][o];
                 float gm1 = 0.f, gs1 = 0.f, g12 = 0.f;
-                if (y >= 0 && y < H && x >= 0 && x < W) {
-                    // Separately rounded operations: sigma1^2, sigma2^2 and sigma12
-                    // must round identically where img == gt (flat background),
-                    // where the reference's SSIM is exactly 1.
+                if (cy >= 0 && cy < H && xm >= 0 && xm < W) {
+                    const float mu1 = acc[0], mu2 = acc[1], b11 = acc[2], b22 = acc[3], b12 = acc[4];
+                    // Separately rounded operations: sigma1^2, sigma2^2 and
+                    // sigma12 must round identically where img == gt (flat
+                    // background), where the reference's SSIM is exactly 1.
                     const float m1s = fmul(mu1, mu1), m2s = fmul(mu2, mu2), m1m2 = fmul(mu1, mu2);
                     const float v1 = fsub(b11, m1s), v2 = fsub(b22, m2s), v12 = fsub(b12, m1m2);
                     const float A = fadd(fmul(2.0f, m1m2), C1), B = fadd(fmul(2.0f, v12), C2);
                     const float Cd = fadd(fadd(m1s, m2s), C1), Dd = fadd(fadd(v1, v2), C2);
                     const float CD = fmul(Cd, Dd), AB = fmul(A, B);
-                    const bool own = r >= R && r < R + OH && cc >= R && cc < R + OW && y < a.row_end;
-                    if (own) ssim_sum += (double)(AB / CD);
-                    const float inv_CD = 1.0f / CD, inv_Cd = 1.0f / Cd, inv_Dd = 1.0f / Dd;
+                    if (own_col && cy >= Y0 && cy < Y1) ssim_sum += (double)(AB / CD);
+                    const float inv_CD = __fdividef(1.0f, CD), inv_Cd = __fdividef(1.0f, Cd);
+                    const float inv_Dd = __fdividef(1.0f, Dd);
                     const float d_mu1 = 2.0f * inv_CD * (mu2 * B - mu1 * AB * inv_Cd);
                     const float d_s12 = 2.0f * A * inv_CD;
                     const float d_s1 = -AB * inv_CD * inv_Dd;
@@ -148,70 +192,65 @@ __global__ void __launch_bounds__(kThreads) k_loss_ssim(LossArgs a) {
                     g12 = g * d_s12;
                     gm1 = g * d_mu1 + gs1 * (-2.0f * mu1) + g12 * (-mu2);
                 }
-                const int q = r * PW + cc;
-                pmap[0 * PH * PW + q] = gm1;
-                pmap[1 * PH * PW + q] = gs1;
-                pmap[2 * PH * PW + q] = g12;
+                sP[step & 1][0][ch][col] = gm1;
+                sP[step & 1][1][ch][col] = gs1;
+                sP[step & 1][2][ch][col] = g12;
             }
-        }
-        __syncthreads();
-        // Horizontal blur of the partials, runs of PR outputs.
-        constexpr int PR = 4, PRUNS = OW / PR;
-        for (int item = threadIdx.x; item < PH * PRUNS; item += kThreads) {
-            const int r = item / PRUNS, c0 = (item - r * PRUNS) * PR;
+            if (out_item) {
+                // S4: horizontal blur of the partials of row ybase + step - 6
+                // (written last step) into ring slot k
+                const int pb = (step + 1) & 1;
 #pragma unroll
-            for (int mm = 0; mm < 3; ++mm) {
-                float row[PR + 10];
-                const float* src = pmap + mm * PH * PW + r * PW + c0;
+                for (int m = 0; m < 3; ++m) {
+                    const float* src = &sP[pb][m][och][ocol];
+                    float acc = 0.f;
 #pragma unroll
-                for (int k = 0; k < PR + 10; ++k) row[k] = src[k];
+                    for (int j = 0; j < kRing; ++j) acc += kW[j] * src[j];
+                    hp[k][m] = acc;
+                }
+                // S5: dL/dimg of row ybase + step - 11 from partial rows
+                // ybase + step - 16 .. ybase + step - 6 (slots k+1 .. k+11)
+                const int oy = ybase + step - 2 * R - 1;
+                if (oy >= Y0 && oy < Y1 && xo < W) {
+                    float bm1 = 0.f, bs1 = 0.f, b12 = 0.f;
 #pragma unroll
-                for (int o = 0; o < PR; ++o) {
-                    float sacc = 0.f;
-#pragma unroll
-                    for (int k = 0; k < 11; ++k) sacc += kW[k] * row[o + k];
-                    hp[mm * PH * OW + r * OW + c0 + o] = sacc;
+                    for (int j = 0; j < kRing; ++j) {
+                        const float w = kW[j];
+                        const float* slot = hp[(k + 1 + j) % kRing];
+                        bm1 += w * slot[0];
+                        bs1 += w * slot[1];
+                        b12 += w * slot[2];
+                    }
+                    const size_t pix = (size_t)oy * W + xo;
+                    const float va = __ldg(a.out_img + pix * 3 + och), vb = __ldg(a.gt + pix * 3 + och);
+                    const float diff = va - vb;
+                    l1_sum += (double)(a.lambda_l1 * fabsf(diff) * a.inv_num);
+                    const float sg = diff > 0.0f ? 1.0f : (diff < 0.0f ? -1.0f : 0.0f);
+                    const float l1g = a.lambda_l1 * sg * a.inv_num;
+                    a.dL_dout_img[pix * 3 + och] = l1g + (bm1 + 2.0f * va * bs1 + vb * b12);
+                    if (och == 0 && a.lambda_dist != 0.f)
+                        dist_sum += (double)(a.lambda_dist * a.out_distortion[pix] * (a.inv_num * 3.0f));
                 }
             }
+            stash((step + 1) & 1, nv);
+            __syncthreads();
         }
-        __syncthreads();
-        for (int q = threadIdx.x; q < OH * OW; q += kThreads) {
-            const int r = q / OW, cc = q - r * OW;
-            const int y = y0 + r, x = x0 + cc;
-            if (y >= a.row_end || y >= H || x >= W) continue;
-            float bm1 = 0.f, bs1 = 0.f, b12 = 0.f;
-#pragma unroll
-            for (int k = 0; k < 11; ++k) {
-                const float w = kW[k];
-                const int o = (r + k) * OW + cc;
-                bm1 += w * hp[0 * PH * OW + o];
-                bs1 += w * hp[1 * PH * OW + o];
-                b12 += w * hp[2 * PH * OW + o];
-            }
-            const float va = sI[(r + 2 * R) * IW + cc + 2 * R];
-            const float vb = sG[(r + 2 * R) * IW + cc + 2 * R];
-            const float diff = va - vb;
-            l1_sum += (double)(a.lambda_l1 * fabsf(diff) * a.inv_num);
-            const float sg = diff > 0.0f ? 1.0f : (diff < 0.0f ? -1.0f : 0.0f);
-            const float l1g = a.lambda_l1 * sg * a.inv_num;
-            const size_t pix = (size_t)y * W + x;
-            a.dL_dout_img[pix * 3 + c] = l1g + (bm1 + 2.0f * va * bs1 + vb * b12);
-            if (c == 0 && a.lambda_dist != 0.f) dist_sum += (double)(a.lambda_dist * a.out_distortion[pix] * (a.inv_num * 3.0f));
-        }
-        __syncthreads();
     }
     // Block reduction of the three partial sums in a fixed order.
-    __shared__ double red[3][kThreads];
-    red[0][threadIdx.x] = l1_sum;
-    red[1][threadIdx.x] = ssim_sum;
-    red[2][threadIdx.x] = dist_sum;
+    red[0][t] = l1_sum;
+    red[1][t] = ssim_sum;
+    red[2][t] = dist_sum;
     __syncthreads();
-    for (int off = kThreads / 2; off > 0; off >>= 1) {
-        if ((int)threadIdx.x < off)
-            for (int k = 0; k < 3; ++k) red[k][threadIdx.x] += red[k][threadIdx.x + off];
+    if (t < 64) {
+        for (int k = 0; k < 3; ++k) red[k][t] += red[k][t + 64] + red[k][t + 128];
+    }
+    __syncthreads();
+    for (int off = 32; off > 0; off >>= 1) {
+        if (t < off)
+            for (int k = 0; k < 3; ++k) red[k][t] += red[k][t + off];
         __syncthreads();
     }
-    if (threadIdx.x == 0) {
+    if (t == 0) {
         const size_t b = (size_t)blockIdx.y * gridDim.x + blockIdx.x;
         a.partials[3 * b + 0] = red[0][0];
         a.partials[3 * b + 1] = red[1][0];
@@ -247,17 +286,17 @@ __global__ void __launch_bounds__(1024) k_loss_finalize(const double* partials, 
 }  // namespace
 
 int loss_num_blocks(int width, int row_begin, int row_end) {
-    return ((width + OW - 1) / OW) * ((row_end - row_begin + OH - 1) / OH);
+    if (row_end <= row_begin || width <= 0) return 0;
+    const LossGrid g = loss_grid(width, row_end - row_begin);
+    return g.strips * g.segs;
 }
 
 void launch_loss_ssim(const LossArgs& a, cudaStream_t s) {
     const int rows = a.row_end - a.row_begin;
-    if (rows <= 0) return;
-    dim3 grid((a.width + OW - 1) / OW, (rows + OH - 1) / OH);
-    const size_t smem = sizeof(float) * kSmemFloats;
-    cudaFuncSetAttribute(k_loss_ssim, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (rows <= 0 || a.width <= 0) return;
+    const LossGrid g = loss_grid(a.width, rows);
     note_launches(1);
-    k_loss_ssim<<<grid, kThreads, smem, s>>>(a);
+    k_loss_ssim<<<dim3(g.strips, g.segs), kThreads, 0, s>>>(a, g.seg_rows);
 }
 
 void launch_loss_finalize(const double* partials, int num_blocks, float lambda_dssim, float inv_num, double* out,
@@ -272,10 +311,10 @@ void launch_loss_finalize(const double* partials, int num_blocks, float lambda_d
 // loss terms and the error word) in fixed arrays that belong to the library's
 // device image instead of workspace buffers, so the entry point never
 // allocates. Every GPU that loads the library holds these arrays (about
-// 1.5 MiB) until the process exits. Host code cannot use the array names as
+// 192 KiB) until the process exits. Host code cannot use the array names as
 // device addresses; the addresses are looked up once per device with
 // cudaGetSymbolAddress.
-constexpr int kNoAllocMaxBlocks = 65536;  // 32x16-pixel loss blocks: e.g. 8192 x 4096
+constexpr int kNoAllocMaxBlocks = 8192;  // loss CTAs (strips x row segments): widths up to 442,368
 static __device__ __align__(256) double g_noalloc_partials[kNoAllocMaxBlocks * 3];
 static __device__ __align__(256) double g_noalloc_terms[4];
 static __device__ __align__(256) uint32_t g_noalloc_err[4];
@@ -344,11 +383,10 @@ int loss_ssim_noalloc(const float* out_img, const float* gt, const float* out_di
         *msg = "out_distortion is required when lambda_dist != 0";
         return MSPLAT_ERR_ARGUMENT;
     }
-    const int64_t nb = (int64_t)((width + OW - 1) / OW) * ((height + OH - 1) / OH);
+    const int64_t nb = loss_num_blocks(width, 0, height);
     if (nb > kNoAllocMaxBlocks) {
-        *msg = "image too large for the allocation-free loss: " + std::to_string(nb) +
-               " blocks of 32x16 pixels, the fixed scratch holds " + std::to_string(kNoAllocMaxBlocks) +
-               " (e.g. 8192 x 4096)";
+        *msg = "image too wide for the allocation-free loss: " + std::to_string(nb) + " loss blocks of " +
+               std::to_string(SW) + "-column strips, the fixed scratch holds " + std::to_string(kNoAllocMaxBlocks);
         return MSPLAT_ERR_ARGUMENT;
     }
     NoAllocScratch sc;

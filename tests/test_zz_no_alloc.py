@@ -62,9 +62,18 @@ def test_noalloc_loss_matches_regular_entry_point_twice():
 def test_noalloc_loss_rejects_images_beyond_its_fixed_scratch():
     torch = pytest.importorskip("torch")
     B, L = _lib()
-    buf = torch.zeros(16, device="cuda")
+    # 500000 x 1 pixels need 9260 loss blocks (54-column strips), more than
+    # the 8192 the fixed scratch holds. The buffers are full-sized anyway, so
+    # a regression in the size check cannot make the kernel read or write
+    # outside them.
+    w, h = 500_000, 1
+    img = torch.zeros(h, w, 3, device="cuda")
+    gt = torch.zeros_like(img)
+    dimg = torch.zeros_like(img)
+    loss = torch.zeros(1, device="cuda")
     stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
-    p = buf.data_ptr()
-    rc = L.msplat_loss_ssim_noalloc(p, p, None, 16384, 8192, 0.8, 0.0, 0.2, p, p, stream)
+    rc = L.msplat_loss_ssim_noalloc(img.data_ptr(), gt.data_ptr(), None, w, h, 0.8, 0.0, 0.2, dimg.data_ptr(),
+                                    loss.data_ptr(), stream)
+    torch.cuda.synchronize()
     assert rc == 1
-    assert "too large" in L.msplat_last_error().decode()
+    assert "too wide" in L.msplat_last_error().decode()
