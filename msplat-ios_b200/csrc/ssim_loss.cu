@@ -49,23 +49,31 @@ constexpr int CW = 64;             // columns of moments and partials per strip
 constexpr int SW = CW - 2 * R;     // output columns per strip
 constexpr int IWID = SW + 4 * R;   // input columns per strip
 constexpr int kThreads = 3 * CW;   // one thread per (channel, column) of S2/S3
-constexpr int kOutItems = 3 * SW;  // threads with an S4/S5 item
 constexpr int kRing = 2 * R + 1;   // rows in a vertical window
-constexpr int kTargetBlocks = 4 * 148;
-constexpr int kMinSegRows = 16;
+constexpr int kSlots = 2 * 148;  // resident CTAs: 2 per SM (__launch_bounds__ below) x 148 SMs
+constexpr int kMaxSegs = 64;
 
 struct LossGrid {
     int strips, segs, seg_rows;
 };
 
-// Strips x row segments: about kTargetBlocks CTAs, segments of at least
-// kMinSegRows rows.
+// Strips x row segments. Every CTA of a segment length L costs about L + 22
+// row steps; the segment count minimises waves x (L + 22), so the grid fills
+// whole waves of resident CTAs with the least recomputed halo.
 LossGrid loss_grid(int width, int rows) {
     LossGrid g;
     g.strips = (width + SW - 1) / SW;
-    int segs = (kTargetBlocks + g.strips - 1) / g.strips;
-    segs = std::max(1, std::min(segs, (rows + kMinSegRows - 1) / kMinSegRows));
-    g.seg_rows = (rows + segs - 1) / segs;
+    int best_segs = 1;
+    int64_t best_cost = -1;
+    for (int segs = 1; segs <= kMaxSegs && segs <= rows; ++segs) {
+        const int64_t waves = ((int64_t)g.strips * segs + kSlots - 1) / kSlots;
+        const int64_t cost = waves * ((rows + segs - 1) / segs + 4 * R + 2);
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best_segs = segs;
+        }
+    }
+    g.seg_rows = (rows + best_segs - 1) / best_segs;
     g.segs = (rows + g.seg_rows - 1) / g.seg_rows;
     return g;
 }
@@ -77,8 +85,10 @@ __global__ void __launch_bounds__(kThreads, 2) k_loss_ssim(LossArgs a, int seg_r
     const int W = a.width, H = a.height;
     const int t = threadIdx.x;
     const int ch = t / CW, col = t - ch * CW;      // S2/S3 item
-    const bool out_item = t < kOutItems;
-    const int och = t / SW, ocol = t - och * SW;   // S4/S5 item
+    // S4/S5 item: same channel, output column col (threads col >= SW idle),
+    // so that no warp spans two channels
+    const bool out_item = col < SW;
+    const int och = ch, ocol = col;
     const int x0 = blockIdx.x * SW;
     const int Y0 = a.row_begin + blockIdx.y * seg_rows;
     const int Y1 = min(Y0 + seg_rows, a.row_end);
