@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cameras", type=int, default=0,
+                    help="use only the first C ring cameras (fewer target images on the device); 0 = all")
     return ap.parse_args()
 
 
@@ -123,16 +125,18 @@ def cameras(B, S, cfg, scene):
 # ---------------------------------------------------------------- byte model
 def raster_bwd_bytes(kept: int, n_vis: int, pixels: int) -> int:
     """Algorithmic HBM bytes of one rasterize_backward launch in this design:
-    4 B per kept intersection (sorted id), 80 B per visible Gaussian (raster
-    record, read once), 32 B per pixel (final T/M1/M2, last/median index,
-    dL/dimg), 64 B read + 64 B written per visible Gaussian (gradient record)."""
-    return 4 * kept + 80 * n_vis + 32 * pixels + 128 * n_vis
+    5 B per kept intersection (sorted id + the forward's per-warp blend byte),
+    80 B per visible Gaussian (raster record, read once), 32 B per pixel
+    (final T/M1/M2, last/median index, dL/dimg), 64 B read + 64 B written per
+    visible Gaussian (gradient record)."""
+    return 5 * kept + 80 * n_vis + 32 * pixels + 128 * n_vis
 
 
 def raster_fwd_bytes(kept: int, n_vis: int, pixels: int) -> int:
-    """4 B per kept intersection, 80 B per visible Gaussian, 60 B per pixel of
-    outputs (image, T/M1/M2, indices, depth, normal, alpha, median, distortion)."""
-    return 4 * kept + 80 * n_vis + 60 * pixels
+    """5 B per kept intersection (sorted id read, blend byte written), 80 B per
+    visible Gaussian, 60 B per pixel of outputs (image, T/M1/M2, indices,
+    depth, normal, alpha, median, distortion)."""
+    return 5 * kept + 80 * n_vis + 60 * pixels
 
 
 def run_ours(args, ws, rank, local):
@@ -147,6 +151,8 @@ def run_ours(args, ws, rank, local):
     if ws > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=300))
     cams = cameras(B, S, cfg, scene)
+    if args.cameras > 0:
+        cams = cams[:args.cameras]
     C = len(cams)
     n = cfg.n
     bg = S.BACKGROUND
@@ -301,7 +307,7 @@ def run_ours(args, ws, rank, local):
                 "scaling": "strong" if ws > 1 else "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded; shapes/distributions of BASELINE config %d)" % args.config,
                 "config": {"workload": f"config {args.config}: {cfg.n} Gaussians SH{cfg.degree}, "
-                                       f"{cfg.width}x{cfg.height}, {cfg.num_cameras} ring cameras",
+                                       f"{cfg.width}x{cfg.height}, {C} ring cameras",
                            "gaussians": cfg.n, "image": [cfg.width, cfg.height], "sh_degree": cfg.degree,
                            "parallelism": f"tile-row sharding x{ws}" if ws > 1 else "single GPU",
                            "l2": "inputs larger than L2 (params+Adam state %.1f GB)" % (n * 58 * 12 / 1e9)},
