@@ -240,7 +240,8 @@ def run_ours(args, ws, rank, local):
     traffic = None
     try:
         tr = json.load(open(os.path.join(REPO, "profiles", "traffic.json")))
-        if tr.get("kernel") == dom and tr.get("config") == args.config:
+        # the capture is of a single-GPU launch over the whole image
+        if tr.get("kernel") == dom and tr.get("config") == args.config and ws == 1 and args.cameras == 0:
             traffic = tr.get("bytes_per_launch")
     except (OSError, ValueError):
         pass
