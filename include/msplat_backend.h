@@ -156,6 +156,72 @@ int msplat_shard_project_backward_adam(const MsplatGaussians* g, const MsplatCam
                                        const MsplatAdamState* adam, float* xys_grad_norm, float* vis_counts,
                                        float* max_2d_size, void* stream);
 
+/* Densification: replaces msplat_densify (core/metal/bindings.h:143-157, impl
+ * core/metal/msplat_metal.mm:1339-1594, kernels core/metal/msplat_metal.metal:
+ * 3231-3491) as driven by Model::afterTrain (core/src/model.cpp:240-306).
+ * Same decisions: a Gaussian with vis_counts > 0 and average screen gradient
+ * (xys_grad_norm / vis_counts) * half_max_dim > grad_thresh splits when its
+ * largest scale exceeds size_thresh (or, with check_screen, its max_2d_size
+ * exceeds screen_thresh), and is duplicated when its largest scale does not;
+ * a split produces two children at parent + R(q) (n * scale, 0) with scales
+ * shrunk by log_size_fac and zero moments, and the parent's own scale shrinks
+ * too (a Gaussian that both splits and duplicates duplicates the shrunk
+ * parent); duplicates copy the parent with zero moments. Then the grown set
+ * [originals | children in split order | duplicates in duplicate order] is
+ * culled: sigmoid(opacity) < cull_alpha_thresh, every split parent, and with
+ * check_huge a largest scale above cull_scale_thresh or (originals, with
+ * check_screen) max_2d_size above cull_screen_size; survivors keep their
+ * order. The reference compacts the scales with a row stride of 3 although
+ * 2DGS scales have 2 entries (msplat_metal.mm:1365, 1377), which scrambles
+ * them; this build compacts every group with its true row size.
+ * Two calls: msplat_densify_plan classifies on the device, reads back the
+ * counts (synchronising `stream`) and keeps the per-Gaussian decisions in the
+ * library's workspace; msplat_densify_apply then writes the new set into
+ * caller-allocated arrays of plan->new_count rows (out, out_adam->exp_avg /
+ * exp_avg_sq; other fields of out_adam are ignored). random_samples holds
+ * 2 * num_splits * 3 standard normals (device): the values the reference
+ * draws from std::mt19937(step) / std::normal_distribution<float> for split
+ * ordinal o, child k at [(2 o + k) * 3, +3). Call apply right after plan with
+ * the same g, adam and args; inputs are not modified. */
+typedef struct MsplatDensifyArgs {
+    float grad_thresh;         /* densifyGradThresh */
+    float size_thresh;         /* densifySizeThresh */
+    float screen_thresh;       /* splitScreenSize */
+    int32_t check_screen;      /* step < stopScreenSizeAt */
+    float cull_alpha_thresh;   /* 0.1 (model.cpp:270) */
+    float cull_scale_thresh;   /* 0.5 */
+    float cull_screen_size;    /* 0.15 */
+    int32_t check_huge;        /* step > refineEvery * resetAlphaEvery */
+    float half_max_dim;        /* 0.5 * max(width, height) of the last step */
+    float log_size_fac;        /* log(1.6) */
+    const float* xys_grad_norm; /* [N] device, accumulated by the steps */
+    const float* vis_counts;    /* [N] device */
+    const float* max_2d_size;   /* [N] device */
+} MsplatDensifyArgs;
+
+typedef struct MsplatDensifyPlan {
+    int32_t num_splits;  /* Gaussians that split */
+    int32_t num_dups;    /* Gaussians duplicated */
+    int32_t new_count;   /* Gaussians after growth and culling */
+} MsplatDensifyPlan;
+
+int msplat_densify_plan(const MsplatGaussians* g, const MsplatDensifyArgs* args, MsplatDensifyPlan* plan,
+                        void* stream);
+int msplat_densify_apply(const MsplatGaussians* g, const MsplatAdamState* adam, const MsplatDensifyArgs* args,
+                         const float* random_samples, const MsplatGaussians* out, const MsplatAdamState* out_adam,
+                         void* stream);
+
+/* The split samples of Model::afterTrain (core/src/model.cpp:254-259): the
+ * first `count` draws of std::normal_distribution<float>(0, 1) from
+ * std::mt19937(seed), written to host memory. Host-only. */
+int msplat_normal_samples(uint32_t seed, int64_t count, float* out);
+
+/* Opacity reset of Model::afterTrain (core/src/model.cpp:290-299): every
+ * opacity logit above max_logit becomes max_logit, and the opacity group's
+ * moments (n floats each, may be NULL) are zeroed. Asynchronous. */
+int msplat_reset_opacity(float* opacities, float* exp_avg, float* exp_avg_sq, int32_t n, float max_logit,
+                         void* stream);
+
 /* Allocation-free L1 + DSSIM (+ distortion) loss, forward and backward. No
  * counterpart in the reference. For callers that may not allocate device
  * memory at run time (hosts whose GPU memory all comes from their own pool

@@ -8,8 +8,13 @@
  *   - dataset loaders (COLMAP / Nerfstudio / Polycam) are not part of this
  *     build: msplat_dataset_create returns NULL with msplat_last_error() set;
  *     build datasets with msplat_dataset_create_from_memory instead;
- *   - densification, PLY/.splat export, mesh extraction and checkpoints are
- *     not part of this build: those calls record an error and return;
+ *   - densification runs inside msplat_trainer_step as in Model::afterTrain
+ *     (with the scale compaction fixed to 2 floats per row, see
+ *     msplat_densify_plan); PLY/.splat export and "MSPL" v1 checkpoints are
+ *     byte-compatible with the reference's; a checkpoint whose SH degree
+ *     differs from the trainer's is rejected (the reference reads it anyway);
+ *   - mesh extraction (TSDF + marching cubes) is not part of this build: the
+ *     call records an error and returns -1;
  *   - errors never escape as C++ exceptions: failed calls return NULL / zero
  *     structures and set msplat_last_error() (declared in msplat_backend.h);
  *   - msplat_set_metallib_path is accepted and ignored.

@@ -27,7 +27,8 @@ REPO = os.path.dirname(HERE)
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
           "-I", os.path.join(REPO, "include"), "-I", CSRC]
-PER_FILE = {"project.cu": ["-fmad=false"], "project_bwd.cu": ["-prec-div=false", "-prec-sqrt=false"]}
+PER_FILE = {"project.cu": ["-fmad=false"], "densify.cu": ["-fmad=false"],
+            "project_bwd.cu": ["-prec-div=false", "-prec-sqrt=false"]}
 HOST_SOURCES = ["model.cpp"]
 
 

@@ -3,15 +3,17 @@
 // shuffle and learning-rate schedule, rendering and evaluation. Host code over
 // the backend C ABI (include/msplat_backend.h) and the CUDA runtime.
 //
-// Follows core/src/msplat_api.mm (Dataset/Trainer, :20-280; C API :282-407)
-// and core/src/model.cpp (Model ctor :43-121, setupOptimizers :123-168,
-// schedulersStep :183-186, getDownscaleFactor :235-238, prepareCam :500-544,
-// fullIteration :762-829).
+// Follows core/src/msplat_api.mm (Dataset/Trainer, :20-280; C API :282-407),
+// core/src/model.cpp (Model ctor :43-121, setupOptimizers :123-168,
+// schedulersStep :183-186, getDownscaleFactor :235-238, afterTrain :240-306,
+// checkpoints :341-498, prepareCam :500-544, fullIteration :762-829) and
+// core/src/loaders/save_gaussians.cpp (PLY :11-58, .splat :60-111).
 #include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <fstream>
 #include <numeric>
 #include <random>
 #include <stdexcept>
@@ -52,6 +54,10 @@ struct Dataset {
     std::vector<float> xyz;
     std::vector<uint8_t> rgb;
     std::vector<float*> pinned;
+    // InputData::scale / translation (the loaders' normalisation); in-memory
+    // datasets are used as given
+    float scale = 1.0f;
+    float translation[3] = {0.f, 0.f, 0.f};
     ~Dataset() {
         for (float* p : pinned) cudaFreeHost(p);
     }
@@ -66,6 +72,7 @@ struct DevArray {
         if (count == 0) count = 1;
         CKT(cudaMalloc(&p, count * sizeof(T)));
         CKT(cudaMemset(p, 0, count * sizeof(T)));
+        CKT(cudaDeviceSynchronize());  // zeroed before any stream of the trainer touches it
         n = count;
     }
     void ensure(size_t count) {
@@ -156,6 +163,7 @@ struct Trainer {
     float means_lr_init = 0.00016f, means_lr_final = 0.0000016f;
     int adam_step = 0;
     int current_step = 0;
+    int last_w = 0, last_h = 0;  // camera size of the last step (model.cpp:764)
     std::vector<size_t> cam_indices;
     size_t cam_pos = 0;
     std::mt19937 rng{42};
@@ -245,6 +253,8 @@ struct Trainer {
         const int sf = downscale_factor(current_step);
         const MsplatCamera cam = prepare(c, sf);
         const float* gt = target(c, sf, cam);
+        last_w = cam.width;
+        last_h = cam.height;
         auto t0 = std::chrono::high_resolution_clock::now();
         adam_step++;
         MsplatAdamState A;
@@ -262,9 +272,10 @@ struct Trainer {
         check_rc(msplat_train_step_fused(&G, &cam, degrees_to_use, cfg.bgColor, gt, 1.0f - cfg.ssimWeight, 0.0f,
                                          cfg.ssimWeight, &A, stats[0].p, stats[1].p, stats[2].p, loss_dev.p, 0,
                                          stream));
-        // schedulersStep (model.cpp:183-186); densification (afterTrain) is not part of this build
+        // schedulersStep (model.cpp:183-186), then afterTrain (:240-306)
         lr[0] = msplat_means_lr(current_step, cfg.iterations, means_lr_init, means_lr_final);
         CKT(cudaMemcpyAsync(loss_host, loss_dev.p, sizeof(float), cudaMemcpyDeviceToHost, stream));
+        after_train(current_step);
         CKT(cudaStreamSynchronize(stream));
         auto t1 = std::chrono::high_resolution_clock::now();
         MsplatStats st;
@@ -273,6 +284,281 @@ struct Trainer {
         st.msPerStep = std::chrono::duration_cast<std::chrono::microseconds>(t1 - t0).count() / 1000.0f;
         st.loss = *loss_host;
         return st;
+    }
+
+    int64_t width_of(int g) const {
+        const int64_t d[6] = {3, 2, 4, 3, 3LL * K, 1};
+        return d[g];
+    }
+
+    // Replaces all parameter and moment arrays by `np`/`nm`/`nv` of `count` rows.
+    void adopt(int count, DevArray<float> (&np)[6], DevArray<float> (&nm)[6], DevArray<float> (&nv)[6]) {
+        for (int g = 0; g < 6; ++g) {
+            std::swap(params[g].p, np[g].p);
+            std::swap(params[g].n, np[g].n);
+            std::swap(m[g].p, nm[g].p);
+            std::swap(m[g].n, nm[g].n);
+            std::swap(v[g].p, nv[g].p);
+            std::swap(v[g].n, nv[g].n);
+            counts[g] = width_of(g) * count;
+        }
+        n = count;
+    }
+
+    // Model::afterTrain (model.cpp:240-306): every refineEvery steps after the
+    // warm-up, densify (split / duplicate / cull) while below the 250k cap and
+    // outside the opacity-reset window, reset opacities once per reset
+    // interval, and restart the densification statistics.
+    void after_train(int step) {
+        const int every = cfg.refineEvery;
+        if (every <= 0 || step % every != 0 || step <= cfg.warmupLength) return;
+        const int reset_interval = cfg.resetAlphaEvery * every;
+        const int stop_split_at = cfg.iterations - 500;
+        constexpr int kMaxSplats = 250000;
+        const int num_cameras = (int)ds->train.size();
+        const bool do_densify = reset_interval > 0 && step < stop_split_at &&
+                                step % reset_interval > num_cameras + every && n < kMaxSplats;
+        if (do_densify) {
+            MsplatDensifyArgs a;
+            a.grad_thresh = cfg.densifyGradThresh;
+            a.size_thresh = cfg.densifySizeThresh;
+            a.screen_thresh = cfg.splitScreenSize;
+            a.check_screen = step < cfg.stopScreenSizeAt ? 1 : 0;
+            a.cull_alpha_thresh = 0.1f;
+            a.cull_scale_thresh = 0.5f;
+            a.cull_screen_size = 0.15f;
+            a.check_huge = step > every * cfg.resetAlphaEvery ? 1 : 0;
+            a.half_max_dim = 0.5f * static_cast<float>(std::max(last_w, last_h));
+            a.log_size_fac = std::log(1.6f);
+            a.xys_grad_norm = stats[0].p;
+            a.vis_counts = stats[1].p;
+            a.max_2d_size = stats[2].p;
+            MsplatGaussians G = gaussians();
+            MsplatDensifyPlan plan;
+            check_rc(msplat_densify_plan(&G, &a, &plan, stream));
+            DevArray<float> samples;
+            if (plan.num_splits > 0) {
+                std::vector<float> host(6 * (size_t)plan.num_splits);
+                check_rc(msplat_normal_samples((uint32_t)step, (int64_t)host.size(), host.data()));
+                samples.alloc(host.size());
+                CKT(cudaMemcpy(samples.p, host.data(), host.size() * sizeof(float), cudaMemcpyHostToDevice));
+            }
+            const int nn = plan.new_count;
+            DevArray<float> np[6], nm[6], nv[6];
+            for (int g = 0; g < 6; ++g) {
+                np[g].alloc((size_t)(width_of(g) * nn));
+                nm[g].alloc((size_t)(width_of(g) * nn));
+                nv[g].alloc((size_t)(width_of(g) * nn));
+            }
+            MsplatGaussians O;
+            O.num_points = nn;
+            O.sh_degree = degree;
+            O.means = np[0].p;
+            O.scales = np[1].p;
+            O.quats = np[2].p;
+            O.features_dc = np[3].p;
+            O.features_rest = K ? np[4].p : nullptr;
+            O.opacities = np[5].p;
+            MsplatAdamState Ain{}, Aout{};
+            for (int g = 0; g < 6; ++g) {
+                Ain.exp_avg[g] = m[g].p;
+                Ain.exp_avg_sq[g] = v[g].p;
+                Aout.exp_avg[g] = nm[g].p;
+                Aout.exp_avg_sq[g] = nv[g].p;
+            }
+            check_rc(msplat_densify_apply(&G, &Ain, &a, samples.p, &O, &Aout, stream));
+            CKT(cudaStreamSynchronize(stream));
+            adopt(nn, np, nm, nv);
+        }
+        if (reset_interval > 0 && step < stop_split_at && step % reset_interval == every)
+            check_rc(msplat_reset_opacity(params[5].p, m[5].p, v[5].p, n, -1.3862943611198906f, stream));
+        // xysGradNorm / visCounts / max2DSize are released and re-created
+        // zeroed with the current count at the next step (model.cpp:302-304, 771-775)
+        CKT(cudaStreamSynchronize(stream));
+        for (auto& st : stats) st.alloc((size_t)n);
+    }
+
+    // ---- checkpoints: "MSPL" version 1 (model.cpp:341-498) ----
+    void write_tensor(std::ofstream& f, const float* dev, std::vector<int64_t> shape) {
+        const uint32_t ndim = (uint32_t)shape.size();
+        f.write(reinterpret_cast<const char*>(&ndim), sizeof(ndim));
+        int64_t numel = 1;
+        for (int64_t d : shape) {
+            f.write(reinterpret_cast<const char*>(&d), sizeof(d));
+            numel *= d;
+        }
+        const uint64_t bytes = (uint64_t)numel * sizeof(float);
+        f.write(reinterpret_cast<const char*>(&bytes), sizeof(bytes));
+        std::vector<float> host((size_t)numel);
+        if (numel) CKT(cudaMemcpy(host.data(), dev, bytes, cudaMemcpyDeviceToHost));
+        f.write(reinterpret_cast<const char*>(host.data()), (std::streamsize)bytes);
+    }
+
+    std::vector<std::vector<int64_t>> group_shapes(int count) const {
+        return {{count, 3}, {count, 2}, {count, 4}, {count, 3}, {count, K, 3}, {count, 1}};
+    }
+
+    void save_checkpoint(const std::string& path) {
+        CKT(cudaStreamSynchronize(stream));
+        std::ofstream f(path, std::ios::binary);
+        if (!f.is_open()) throw ApiError("Cannot open checkpoint file for writing: " + path);
+        const uint32_t header[6] = {0x4C50534Du, 1u, (uint32_t)current_step, (uint32_t)n, (uint32_t)degree,
+                                    (uint32_t)adam_step};
+        f.write(reinterpret_cast<const char*>(header), sizeof(header));
+        f.write(reinterpret_cast<const char*>(lr), sizeof(lr));
+        f.write(reinterpret_cast<const char*>(&means_lr_init), sizeof(float));
+        f.write(reinterpret_cast<const char*>(&means_lr_final), sizeof(float));
+        const auto shapes = group_shapes(n);
+        for (int g = 0; g < 6; ++g) write_tensor(f, params[g].p, shapes[g]);
+        for (int g = 0; g < 6; ++g) write_tensor(f, m[g].p, shapes[g]);
+        for (int g = 0; g < 6; ++g) write_tensor(f, v[g].p, shapes[g]);
+        if (!f) throw ApiError("error writing checkpoint: " + path);
+    }
+
+    int load_checkpoint(const std::string& path) {
+        std::ifstream f(path, std::ios::binary);
+        if (!f.is_open()) throw ApiError("Cannot open checkpoint file: " + path);
+        uint32_t magic = 0, version = 0;
+        f.read(reinterpret_cast<char*>(&magic), 4);
+        f.read(reinterpret_cast<char*>(&version), 4);
+        if (!f || magic != 0x4C50534Du) throw ApiError("Not a valid msplat checkpoint file");
+        if (version != 1) throw ApiError("Unsupported checkpoint version: " + std::to_string(version));
+        uint32_t step = 0, num = 0, sh = 0, adam_steps = 0;
+        f.read(reinterpret_cast<char*>(&step), 4);
+        f.read(reinterpret_cast<char*>(&num), 4);
+        f.read(reinterpret_cast<char*>(&sh), 4);
+        f.read(reinterpret_cast<char*>(&adam_steps), 4);
+        float file_lr[6], lr_init = 0.f, lr_final = 0.f;
+        f.read(reinterpret_cast<char*>(file_lr), sizeof(file_lr));
+        f.read(reinterpret_cast<char*>(&lr_init), 4);
+        f.read(reinterpret_cast<char*>(&lr_final), 4);
+        if (!f) throw ApiError("truncated checkpoint: " + path);
+        if ((int)sh != degree)
+            throw ApiError("checkpoint SH degree " + std::to_string(sh) + " does not match the trainer's " +
+                           std::to_string(degree));
+        const int count = (int)num;
+        const auto shapes = group_shapes(count);
+        std::vector<float> data[18];
+        for (int k = 0; k < 18; ++k) {
+            uint32_t ndim = 0;
+            f.read(reinterpret_cast<char*>(&ndim), 4);
+            if (!f || ndim > 8) throw ApiError("corrupt checkpoint tensor header: " + path);
+            std::vector<int64_t> shape(ndim);
+            for (uint32_t d = 0; d < ndim; ++d) f.read(reinterpret_cast<char*>(&shape[d]), 8);
+            uint64_t bytes = 0;
+            f.read(reinterpret_cast<char*>(&bytes), 8);
+            if (!f || shape != shapes[k % 6])
+                throw ApiError("checkpoint tensor " + std::to_string(k) + " has an unexpected shape");
+            const uint64_t want = (uint64_t)(width_of(k % 6) * count) * sizeof(float);
+            if (bytes != want) throw ApiError("checkpoint tensor " + std::to_string(k) + " has an unexpected size");
+            data[k].resize(bytes / sizeof(float));
+            f.read(reinterpret_cast<char*>(data[k].data()), (std::streamsize)bytes);
+            if (!f) throw ApiError("truncated checkpoint: " + path);
+        }
+        CKT(cudaStreamSynchronize(stream));
+        DevArray<float> np[6], nm[6], nv[6];
+        DevArray<float>* dst[3] = {np, nm, nv};
+        for (int k = 0; k < 18; ++k) {
+            DevArray<float>& a = dst[k / 6][k % 6];
+            a.alloc(data[k].size());
+            if (!data[k].empty())
+                CKT(cudaMemcpy(a.p, data[k].data(), data[k].size() * sizeof(float), cudaMemcpyHostToDevice));
+        }
+        adopt(count, np, nm, nv);
+        std::memcpy(lr, file_lr, sizeof(lr));
+        means_lr_init = lr_init;
+        means_lr_final = lr_final;
+        adam_step = (int)adam_steps;
+        current_step = (int)step;
+        for (auto& st : stats) st.alloc((size_t)n);
+        shuffle();  // Trainer::loadCheckpoint re-shuffles (msplat_api.mm:260-265)
+        return current_step;
+    }
+
+    // ---- exports (save_gaussians.cpp) ----
+    std::vector<float> host_group(int g) {
+        std::vector<float> h((size_t)counts[g]);
+        if (counts[g]) CKT(cudaMemcpy(h.data(), params[g].p, h.size() * sizeof(float), cudaMemcpyDeviceToHost));
+        return h;
+    }
+
+    void export_ply(const std::string& path) {  // saveGaussianPly, :11-58
+        CKT(cudaStreamSynchronize(stream));
+        std::ofstream o(path, std::ios::binary);
+        if (!o.is_open()) throw ApiError("Cannot open PLY file for writing: " + path);
+        const int fr_bases = K, num_fr = 3 * K, num_scales = 2;
+        o << "ply\nformat binary_little_endian 1.0\n";
+        o << "comment msplat v" << current_step << "\n";
+        o << "element vertex " << n << "\n";
+        o << "property float x\nproperty float y\nproperty float z\n";
+        o << "property float nx\nproperty float ny\nproperty float nz\n";
+        for (int i = 0; i < 3; ++i) o << "property float f_dc_" << i << "\n";
+        for (int i = 0; i < num_fr; ++i) o << "property float f_rest_" << i << "\n";
+        o << "property float opacity\n";
+        for (int i = 0; i < num_scales; ++i) o << "property float scale_" << i << "\n";
+        o << "property float rot_0\nproperty float rot_1\nproperty float rot_2\nproperty float rot_3\n";
+        o << "end_header\n";
+        const std::vector<float> mp = host_group(0), sp = host_group(1), qp = host_group(2), dp = host_group(3),
+                                 frp = host_group(4), op = host_group(5);
+        const bool keep = cfg.keepCrs;
+        const float sc = ds->scale;
+        const int row_floats = 3 + 3 + 3 + num_fr + 1 + num_scales + 4;
+        std::vector<float> row(row_floats);
+        for (int64_t i = 0; i < n; ++i) {
+            int c = 0;
+            for (int j = 0; j < 3; ++j) row[c++] = keep ? (mp[i * 3 + j] / sc + ds->translation[j]) : mp[i * 3 + j];
+            row[c++] = 0.f;
+            row[c++] = 0.f;
+            row[c++] = 0.f;
+            for (int j = 0; j < 3; ++j) row[c++] = dp[i * 3 + j];
+            for (int ch = 0; ch < 3; ++ch)  // [bases, 3] -> [3, bases]
+                for (int b = 0; b < fr_bases; ++b) row[c++] = frp[i * fr_bases * 3 + b * 3 + ch];
+            row[c++] = op[i];
+            for (int j = 0; j < num_scales; ++j)
+                row[c++] = keep ? std::log(std::exp(sp[i * num_scales + j]) / sc) : sp[i * num_scales + j];
+            for (int j = 0; j < 4; ++j) row[c++] = qp[i * 4 + j];
+            o.write(reinterpret_cast<const char*>(row.data()), row_floats * sizeof(float));
+        }
+        if (!o) throw ApiError("error writing PLY: " + path);
+    }
+
+    void export_splat(const std::string& path) {  // saveGaussianSplat, :60-111
+        CKT(cudaStreamSynchronize(stream));
+        std::ofstream o(path, std::ios::binary);
+        if (!o.is_open()) throw ApiError("Cannot open .splat file for writing: " + path);
+        const std::vector<float> mp = host_group(0), sp = host_group(1), qp = host_group(2), dp = host_group(3),
+                                 op = host_group(5);
+        const bool keep = cfg.keepCrs;
+        const float scl = ds->scale;
+        std::vector<float> order(n);
+        for (int64_t i = 0; i < n; ++i) {
+            float s = 0.0f;
+            for (int j = 0; j < 2; ++j) s += std::exp(sp[i * 2 + j]);
+            if (keep) s /= scl;
+            order[i] = s / (1.0f + std::exp(-op[i]));
+        }
+        std::vector<size_t> idx(n);
+        std::iota(idx.begin(), idx.end(), 0);
+        std::sort(idx.begin(), idx.end(), [&](size_t a, size_t b) { return order[a] > order[b]; });
+        for (size_t i : idx) {
+            float mm[3];
+            for (int j = 0; j < 3; ++j) mm[j] = keep ? (mp[i * 3 + j] / scl + ds->translation[j]) : mp[i * 3 + j];
+            o.write(reinterpret_cast<const char*>(mm), 12);
+            float sc[3] = {0.f, 0.f, 0.f};
+            for (int j = 0; j < 2; ++j) sc[j] = keep ? (std::exp(sp[i * 2 + j]) / scl) : std::exp(sp[i * 2 + j]);
+            sc[2] = 1e-5f;  // 2DGS surfels are flat discs
+            o.write(reinterpret_cast<const char*>(sc), 12);
+            uint8_t rgba[4];
+            for (int j = 0; j < 3; ++j)
+                rgba[j] = (uint8_t)std::clamp(((double)dp[i * 3 + j] * kC0 + 0.5) * 255.0, 0.0, 255.0);
+            const float sig = 1.0f / (1.0f + std::exp(-op[i]));
+            rgba[3] = (uint8_t)std::clamp(sig * 255.0f, 0.0f, 255.0f);
+            o.write(reinterpret_cast<const char*>(rgba), 4);
+            uint8_t q[4];
+            for (int j = 0; j < 4; ++j) q[j] = (uint8_t)std::clamp(qp[i * 4 + j] * 128.0f + 128.0f, 0.0f, 255.0f);
+            o.write(reinterpret_cast<const char*>(q), 4);
+        }
+        if (!o) throw ApiError("error writing .splat: " + path);
     }
 
     // Renders a camera; returns the device image and its camera.
@@ -612,16 +898,36 @@ static void not_in_build(const char* what) {
     set_last_error((std::string(what) + " is not part of this build").c_str());
 }
 
-void msplat_trainer_export_ply(MsplatTrainer, const char*) { not_in_build("PLY export"); }
-void msplat_trainer_export_splat(MsplatTrainer, const char*) { not_in_build(".splat export"); }
+void msplat_trainer_export_ply(MsplatTrainer t, const char* path) {
+    api<int>(0, [&] {
+        if (!path) throw ApiError("null path");
+        T(t)->export_ply(path);
+        return 0;
+    });
+}
+void msplat_trainer_export_splat(MsplatTrainer t, const char* path) {
+    api<int>(0, [&] {
+        if (!path) throw ApiError("null path");
+        T(t)->export_splat(path);
+        return 0;
+    });
+}
 int64_t msplat_trainer_extract_mesh(MsplatTrainer, const char*, float, float, float, float) {
     not_in_build("mesh extraction (TSDF + marching cubes)");
     return -1;
 }
-void msplat_trainer_save_checkpoint(MsplatTrainer, const char*) { not_in_build("checkpoint save"); }
-int msplat_trainer_load_checkpoint(MsplatTrainer, const char*) {
-    not_in_build("checkpoint load");
-    return -1;
+void msplat_trainer_save_checkpoint(MsplatTrainer t, const char* path) {
+    api<int>(0, [&] {
+        if (!path) throw ApiError("null path");
+        T(t)->save_checkpoint(path);
+        return 0;
+    });
+}
+int msplat_trainer_load_checkpoint(MsplatTrainer t, const char* path) {
+    return api<int>(-1, [&] {
+        if (!path) throw ApiError("null path");
+        return T(t)->load_checkpoint(path);
+    });
 }
 int msplat_trainer_splat_count(MsplatTrainer t) { return api<int>(0, [&] { return T(t)->n; }); }
 int msplat_trainer_iteration(MsplatTrainer t) { return api<int>(0, [&] { return T(t)->current_step; }); }

@@ -4,6 +4,7 @@ trainer-level C API (include/msplat_c_api.h) of libmsplat_b200.so."""
 from __future__ import annotations
 
 import ctypes as C
+import os
 import dataclasses
 from typing import Callable, List, Optional
 
@@ -114,6 +115,11 @@ def _lib():
         getattr(L, nm).restype = i
     L.msplat_trainer_get_params.argtypes = [vp, fp, fp, fp, fp, fp, fp]
     L.msplat_trainer_get_params.restype = i
+    for nm in ("msplat_trainer_export_ply", "msplat_trainer_export_splat", "msplat_trainer_save_checkpoint"):
+        getattr(L, nm).argtypes = [vp, C.c_char_p]
+        getattr(L, nm).restype = None
+    L.msplat_trainer_load_checkpoint.argtypes = [vp, C.c_char_p]
+    L.msplat_trainer_load_checkpoint.restype = i
     L.msplat_sync.argtypes = []
     L.msplat_cleanup.argtypes = []
     L._libc = C.CDLL(None)
@@ -257,6 +263,30 @@ class GaussianTrainer:
         if rc:
             raise RuntimeError(_err(_lib()))
         return out
+
+    def _path_call(self, name: str, path: str):
+        L = _lib()
+        r = getattr(L, name)(self._h, os.fspath(path).encode())
+        msg = _err(L)
+        if msg:
+            raise RuntimeError(msg)
+        return r
+
+    def export_ply(self, path: str):
+        """Export the current Gaussians as a PLY file (saveGaussianPly)."""
+        self._path_call("msplat_trainer_export_ply", path)
+
+    def export_splat(self, path: str):
+        """Export the current Gaussians as a .splat file (saveGaussianSplat)."""
+        self._path_call("msplat_trainer_export_splat", path)
+
+    def save_checkpoint(self, path: str):
+        """Save a training checkpoint ("MSPL" version 1)."""
+        self._path_call("msplat_trainer_save_checkpoint", path)
+
+    def load_checkpoint(self, path: str) -> int:
+        """Load a training checkpoint and resume from the saved iteration."""
+        return self._path_call("msplat_trainer_load_checkpoint", path)
 
     @property
     def splat_count(self) -> int:

@@ -41,6 +41,18 @@ class MsplatAdamState(C.Structure):
                 ("step", C.c_int32), ("beta1", C.c_float), ("beta2", C.c_float), ("eps", C.c_float)]
 
 
+class MsplatDensifyArgs(C.Structure):
+    _fields_ = [("grad_thresh", C.c_float), ("size_thresh", C.c_float), ("screen_thresh", C.c_float),
+                ("check_screen", C.c_int32), ("cull_alpha_thresh", C.c_float), ("cull_scale_thresh", C.c_float),
+                ("cull_screen_size", C.c_float), ("check_huge", C.c_int32), ("half_max_dim", C.c_float),
+                ("log_size_fac", C.c_float), ("xys_grad_norm", C.c_void_p), ("vis_counts", C.c_void_p),
+                ("max_2d_size", C.c_void_p)]
+
+
+class MsplatDensifyPlan(C.Structure):
+    _fields_ = [("num_splits", C.c_int32), ("num_dups", C.c_int32), ("new_count", C.c_int32)]
+
+
 class MsplatTensorRef(C.Structure):
     _fields_ = [("data", C.c_void_p), ("shape", C.c_int64 * 4), ("ndim", C.c_int32), ("dtype", C.c_int32)]
 
@@ -73,6 +85,14 @@ def load():
     L.msplat_shard_project_backward_adam.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, vp,
                                                      i32, i32, C.POINTER(MsplatAdamState), vp, vp, vp, vp]
     L.msplat_last_tensor.argtypes = [C.c_char_p, C.POINTER(MsplatTensorRef)]
+    L.msplat_densify_plan.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatDensifyArgs),
+                                      C.POINTER(MsplatDensifyPlan), vp]
+    L.msplat_densify_apply.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatAdamState),
+                                       C.POINTER(MsplatDensifyArgs), vp, C.POINTER(MsplatGaussians),
+                                       C.POINTER(MsplatAdamState), vp]
+    L.msplat_reset_opacity.argtypes = [vp, vp, vp, i32, f, vp]
+    L.msplat_normal_samples.argtypes = [u32, i64, vp]
+    L.msplat_normal_samples.restype = C.c_int
     L.msplat_last_num_intersections.restype = i64
     L.msplat_last_status_flags.restype = u32
     L.msplat_launch_count.restype = i64
@@ -84,7 +104,8 @@ def load():
     L.msplat_stage_name.restype = C.c_char_p
     L.msplat_last_error.restype = C.c_char_p
     for name in ("msplat_render", "msplat_train_step_2dgs", "msplat_fused_adam", "msplat_train_step_fused",
-                 "msplat_shard_forward_backward", "msplat_shard_project_backward_adam", "msplat_last_tensor"):
+                 "msplat_shard_forward_backward", "msplat_shard_project_backward_adam", "msplat_last_tensor",
+                 "msplat_densify_plan", "msplat_densify_apply", "msplat_reset_opacity"):
         getattr(L, name).restype = C.c_int
     _lib = L
     return L
@@ -294,3 +315,45 @@ def stage_times() -> dict:
     if k < 0:
         raise MsplatError(2, L.msplat_last_error().decode())
     return {L.msplat_stage_name(i).decode(): (ms[i], cnt[i]) for i in range(k)}
+
+
+def densify(g: "DeviceGaussians", adam: "AdamState", stats, args: dict, seed: int, stream=None):
+    """Densification through msplat_densify_plan / msplat_densify_apply.
+    stats = (xys_grad_norm, vis_counts, max_2d_size) device tensors; args holds
+    the MsplatDensifyArgs thresholds; split samples are std::mt19937(seed)
+    normals (as the reference draws them). Returns (new DeviceGaussians, new
+    AdamState, plan dict)."""
+    import torch
+    a = MsplatDensifyArgs(**args)
+    a.xys_grad_norm, a.vis_counts, a.max_2d_size = (_ptr(s) for s in stats)
+    gs = g.struct()
+    plan = MsplatDensifyPlan()
+    L = load()
+    _check(L.msplat_densify_plan(C.byref(gs), C.byref(a), C.byref(plan), _stream(stream)))
+    n_new = plan.new_count
+    dev = g.means.device
+    samples = torch.from_numpy(normal_samples(seed, 6 * plan.num_splits)).to(dev) if plan.num_splits else None
+    outs = [torch.zeros((n_new,) + tuple(t.shape[1:]), dtype=torch.float32, device=dev) for t in g.groups()]
+    new_g = DeviceGaussians.__new__(DeviceGaussians)
+    new_g.means, new_g.scales, new_g.quats, new_g.f_dc, new_g.f_rest, new_g.opacities = outs
+    new_g.sh_degree = g.sh_degree
+    new_adam = AdamState(new_g)
+    new_adam.lr, new_adam.step = list(adam.lr), adam.step
+    new_adam.beta1, new_adam.beta2, new_adam.eps = adam.beta1, adam.beta2, adam.eps
+    ogs = new_g.struct()
+    _check(L.msplat_densify_apply(C.byref(gs), C.byref(adam.struct()), C.byref(a), _ptr(samples), C.byref(ogs),
+                                  C.byref(new_adam.struct()), _stream(stream)))
+    return new_g, new_adam, {"num_splits": plan.num_splits, "num_dups": plan.num_dups, "new_count": n_new}
+
+
+def normal_samples(seed: int, count: int):
+    """std::mt19937(seed) / std::normal_distribution<float>(0, 1) draws from
+    the library's host code (the draws the trainer makes for its splits)."""
+    out = np.zeros(max(count, 1), np.float32)
+    load().msplat_normal_samples(seed, count, out.ctypes.data)
+    return out[:count]
+
+
+def reset_opacity(opacities, exp_avg, exp_avg_sq, max_logit: float, stream=None):
+    _check(load().msplat_reset_opacity(_ptr(opacities), _ptr(exp_avg), _ptr(exp_avg_sq), opacities.numel(),
+                                       max_logit, _stream(stream)))

@@ -14,6 +14,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <random>
 #include <vector>
 #ifdef _OPENMP
 #include <omp.h>
@@ -1038,6 +1039,131 @@ double orc_time_step_sample(const OrcStepArgs* a, const OrcCamera* cam, int tile
         if (stage_seconds) stage_seconds[q] = st[q];
     }
     return total;
+}
+
+
+void orc_normal_samples(uint32_t seed, int64_t count, float* out) {
+    // model.cpp:254-259
+    std::mt19937 rng(seed);
+    std::normal_distribution<float> dist(0.0f, 1.0f);
+    for (int64_t i = 0; i < count; ++i) out[i] = dist(rng);
+}
+
+int orc_densify(int n, int cap, int rest_bases, const OrcDensifyArgs* a, const float* xys_grad_norm,
+                const float* vis_counts, const float* max_2d_size, float* const params[6], float* const m[6],
+                float* const v[6], const float* random_samples, int* num_splits, int* num_dups) {
+    const int K3 = 3 * rest_bases;
+    const int w[6] = {3, 2, 4, 3, K3, 1};
+    float* means = params[0];
+    float* scales = params[1];
+    float* quats = params[2];
+    float* opac = params[5];
+    // Stage 1: densify_classify_kernel (metal:3231-3263)
+    std::vector<int> split(n, 0), dup(n, 0);
+    for (int i = 0; i < n; ++i) {
+        const float vc = vis_counts[i];
+        if (vc <= 0.0f) continue;
+        const float avg_grad = (xys_grad_norm[i] / vc) * a->half_max_dim;
+        const bool high_grad = avg_grad > a->grad_thresh;
+        float max_scale = orc_exp(scales[2 * i]);
+        max_scale = std::fmax(max_scale, orc_exp(scales[2 * i + 1]));
+        const bool is_large = max_scale > a->size_thresh;
+        bool do_split = is_large;
+        if (a->check_screen && max_2d_size[i] > a->screen_thresh) do_split = true;
+        do_split = do_split && high_grad;
+        split[i] = do_split ? 1 : 0;
+        dup[i] = (!is_large && high_grad) ? 1 : 0;
+    }
+    // Stages 2-3: inclusive prefix sums of the flags
+    std::vector<int> split_prefix(n), dup_prefix(n);
+    int acc_s = 0, acc_d = 0;
+    for (int i = 0; i < n; ++i) {
+        acc_s += split[i];
+        acc_d += dup[i];
+        split_prefix[i] = acc_s;
+        dup_prefix[i] = acc_d;
+    }
+    const int S = acc_s, D = acc_d;
+    if (num_splits) *num_splits = S;
+    if (num_dups) *num_dups = D;
+    const int n_new = n + 2 * S + D;
+    if (n_new > cap) return -1;
+    // Stage 4: densify_append_split_kernel (metal:3265-3340)
+    for (int i = 0; i < n; ++i) {
+        if (!split[i]) continue;
+        const int ord = split_prefix[i] - 1;
+        const int c0 = n + 2 * ord;
+        float qw = quats[i * 4], qx = quats[i * 4 + 1], qy = quats[i * 4 + 2], qz = quats[i * 4 + 3];
+        const float qlen = std::sqrt(qw * qw + qx * qx + qy * qy + qz * qz);
+        qw /= qlen; qx /= qlen; qy /= qlen; qz /= qlen;
+        const float sx = orc_exp(scales[i * 2]);
+        const float sy = orc_exp(scales[i * 2 + 1]);
+        const float sz = 0.0f;  // 2DGS: no third axis
+        for (int k = 0; k < 2; ++k) {
+            const int child = c0 + k;
+            const int ri = ord * 2 + k;
+            const float r0 = random_samples[ri * 3] * sx;
+            const float r1 = random_samples[ri * 3 + 1] * sy;
+            const float r2 = random_samples[ri * 3 + 2] * sz;
+            const float v0 = (1 - 2 * (qy * qy + qz * qz)) * r0 + 2 * (qx * qy - qw * qz) * r1 + 2 * (qx * qz + qw * qy) * r2;
+            const float v1 = 2 * (qx * qy + qw * qz) * r0 + (1 - 2 * (qx * qx + qz * qz)) * r1 + 2 * (qy * qz - qw * qx) * r2;
+            const float v2 = 2 * (qx * qz - qw * qy) * r0 + 2 * (qy * qz + qw * qx) * r1 + (1 - 2 * (qx * qx + qy * qy)) * r2;
+            means[child * 3] = means[i * 3] + v0;
+            means[child * 3 + 1] = means[i * 3 + 1] + v1;
+            means[child * 3 + 2] = means[i * 3 + 2] + v2;
+            for (int j = 0; j < 2; ++j) scales[child * 2 + j] = scales[i * 2 + j] - a->log_size_fac;
+            for (int gi = 2; gi < 6; ++gi)
+                for (int j = 0; j < w[gi]; ++j) params[gi][(size_t)child * w[gi] + j] = params[gi][(size_t)i * w[gi] + j];
+            for (int gi = 0; gi < 6; ++gi)
+                for (int j = 0; j < w[gi]; ++j) {
+                    m[gi][(size_t)child * w[gi] + j] = 0.0f;
+                    v[gi][(size_t)child * w[gi] + j] = 0.0f;
+                }
+        }
+        for (int j = 0; j < 2; ++j) scales[i * 2 + j] -= a->log_size_fac;
+    }
+    // Stage 5: densify_append_dup_kernel (metal:3342-3394)
+    for (int i = 0; i < n; ++i) {
+        if (!dup[i]) continue;
+        const int dst = n + 2 * S + dup_prefix[i] - 1;
+        for (int gi = 0; gi < 6; ++gi)
+            for (int j = 0; j < w[gi]; ++j) {
+                params[gi][(size_t)dst * w[gi] + j] = params[gi][(size_t)i * w[gi] + j];
+                m[gi][(size_t)dst * w[gi] + j] = 0.0f;
+                v[gi][(size_t)dst * w[gi] + j] = 0.0f;
+            }
+    }
+    // Stage 6: densify_cull_classify_kernel (metal:3408-3441)
+    std::vector<int> keep(n_new, 0);
+    for (int idx = 0; idx < n_new; ++idx) {
+        const float opacity_sigmoid = 1.0f / (1.0f + orc_exp(-opac[idx]));
+        bool cull = opacity_sigmoid < a->cull_alpha_thresh;
+        if (idx < n && split[idx]) cull = true;
+        if (a->check_huge) {
+            float max_s = orc_exp(scales[idx * 2]);
+            max_s = std::fmax(max_s, orc_exp(scales[idx * 2 + 1]));
+            if (max_s > a->cull_scale_thresh) cull = true;
+            if (a->check_screen && idx < n && max_2d_size[idx] > a->cull_screen_size) cull = true;
+        }
+        keep[idx] = cull ? 0 : 1;
+    }
+    // Stages 7-8: keep prefix and compaction, every group with its own row size
+    int out = 0;
+    std::vector<int> dst_of(n_new, -1);
+    for (int idx = 0; idx < n_new; ++idx)
+        if (keep[idx]) dst_of[idx] = out++;
+    float* const* groups[3] = {params, m, v};
+    for (int t = 0; t < 3; ++t)
+        for (int gi = 0; gi < 6; ++gi) {
+            float* buf = groups[t][gi];
+            if (w[gi] == 0) continue;
+            for (int idx = 0; idx < n_new; ++idx) {
+                const int d = dst_of[idx];
+                if (d < 0 || d == idx) continue;
+                std::memmove(buf + (size_t)d * w[gi], buf + (size_t)idx * w[gi], sizeof(float) * w[gi]);
+            }
+        }
+    return out;
 }
 
 }  // extern "C"

@@ -169,6 +169,31 @@ void orc_render(int n, const float* means, const float* scales, const float* qua
 double orc_time_step_sample(const OrcStepArgs* a, const OrcCamera* cam, int tile_row_stride,
                             double* stage_seconds);
 
+/* Densification as the reference stages it (msplat_densify,
+ * core/metal/msplat_metal.mm:1339-1594; kernels core/metal/msplat_metal.metal:
+ * 3231-3491): classify, append split children at [n + 2 o, n + 2 o + 1],
+ * shrink split parents, append duplicates at [n + 2 S + d], cull-classify the
+ * grown set, compact. The buffers hold `cap` >= 3n rows (params[6], m[6],
+ * v[6] in Model group order, rows of 3, 2, 4, 3, 3K, 1 floats); stats are
+ * xys_grad_norm, vis_counts, max_2d_size [n]; random_samples [2n, 3]. One
+ * deliberate difference: the compaction moves scales rows of 2 floats (the
+ * reference's stride table says 3, msplat_metal.mm:1365, 1377). Returns the
+ * new count; *num_splits and *num_dups receive the growth counts. */
+typedef struct OrcDensifyArgs {
+    float grad_thresh, size_thresh, screen_thresh;
+    int check_screen;
+    float cull_alpha_thresh, cull_scale_thresh, cull_screen_size;
+    int check_huge;
+    float half_max_dim, log_size_fac;
+} OrcDensifyArgs;
+int orc_densify(int n, int cap, int rest_bases, const OrcDensifyArgs* a, const float* xys_grad_norm,
+                const float* vis_counts, const float* max_2d_size, float* const params[6], float* const m[6],
+                float* const v[6], const float* random_samples, int* num_splits, int* num_dups);
+
+/* The split samples of Model::afterTrain (model.cpp:254-259): `count` draws
+ * of std::normal_distribution<float>(0, 1) from std::mt19937(seed). */
+void orc_normal_samples(uint32_t seed, int64_t count, float* out);
+
 /* Threads the oracle may use (OpenMP); <= 0 means all. Returns the count. */
 int orc_set_threads(int n);
 

@@ -43,6 +43,13 @@ class OrcStepArgs(C.Structure):
                 ("lambda_dssim", C.c_float)]
 
 
+class OrcDensifyArgs(C.Structure):
+    _fields_ = [("grad_thresh", C.c_float), ("size_thresh", C.c_float), ("screen_thresh", C.c_float),
+                ("check_screen", C.c_int), ("cull_alpha_thresh", C.c_float), ("cull_scale_thresh", C.c_float),
+                ("cull_screen_size", C.c_float), ("check_huge", C.c_int), ("half_max_dim", C.c_float),
+                ("log_size_fac", C.c_float)]
+
+
 def build() -> str:
     subprocess.run(["make", "-s", "-C", HERE], check=True)
     return LIB_PATH
@@ -89,6 +96,11 @@ def lib():
         L.orc_time_step_sample.restype = C.c_double
         L.orc_time_step_sample.argtypes = [C.POINTER(OrcStepArgs), C.POINTER(OrcCamera), C.c_int,
                                            C.POINTER(C.c_double)]
+        L.orc_densify.restype = C.c_int
+        L.orc_densify.argtypes = [C.c_int, C.c_int, C.c_int, C.POINTER(OrcDensifyArgs), f32p, f32p, f32p,
+                                  C.c_void_p * 6, C.c_void_p * 6, C.c_void_p * 6, f32p, C.POINTER(C.c_int),
+                                  C.POINTER(C.c_int)]
+        L.orc_normal_samples.argtypes = [C.c_uint32, C.c_int64, f32p]
         _lib = L
     return _lib
 
@@ -307,3 +319,42 @@ class OracleTrainer:
                                     img.ctypes.data, C.byref(kept))
         del keep
         return dict(loss=loss, grads=grads, out_img=img, kept=kept.value)
+
+
+def normal_samples(seed: int, count: int):
+    """std::mt19937(seed) / std::normal_distribution<float>(0, 1) draws (model.cpp:254-259)."""
+    out = np.zeros(max(count, 1), np.float32)
+    lib().orc_normal_samples(seed, count, out)
+    return out[:count]
+
+
+def densify(groups, m, v, degree, stats, args: dict, random_samples):
+    """Staged reference densification (orc_densify). groups/m/v: six arrays each
+    in Model order (means, scales, quats, f_dc, f_rest, opacities) with N rows;
+    stats: (xys_grad_norm, vis_counts, max_2d_size). Returns (groups, m, v,
+    num_splits, num_dups) with the new row count."""
+    n = groups[0].shape[0]
+    cap = 3 * n
+    K = (degree + 1) ** 2 - 1
+    widths = [3, 2, 4, 3, 3 * K, 1]
+    bufs = []
+    for arrs in (groups, m, v):
+        row = []
+        for a, w in zip(arrs, widths):
+            b = np.zeros((cap, w) if w else (cap, 0), np.float32)
+            b[:n] = np.asarray(a, np.float32).reshape(n, w)
+            row.append(b)
+        bufs.append(row)
+    ptrs = [(C.c_void_p * 6)(*[b.ctypes.data if b.size else None for b in row]) for row in bufs]
+    rs = _c(random_samples).reshape(-1)
+    need = 6 * n
+    if rs.size < need:
+        rs = np.concatenate([rs, np.zeros(need - rs.size, np.float32)])
+    a = OrcDensifyArgs(**args)
+    ns, nd = C.c_int(0), C.c_int(0)
+    new_n = lib().orc_densify(n, cap, K, C.byref(a), _c(stats[0]).reshape(-1), _c(stats[1]).reshape(-1),
+                              _c(stats[2]).reshape(-1), ptrs[0], ptrs[1], ptrs[2], rs, C.byref(ns), C.byref(nd))
+    if new_n < 0:
+        raise RuntimeError("densify capacity exceeded")
+    out = [[b[:new_n].copy() for b in row] for row in bufs]
+    return out[0], out[1], out[2], ns.value, nd.value
