@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--render-frames", type=int, default=20,
+                    help="render-only frames timed after the training steps (single GPU); 0 = skip")
     ap.add_argument("--cameras", type=int, default=0,
                     help="use only the first C ring cameras (fewer target images on the device); 0 = all")
     return ap.parse_args()
@@ -254,6 +256,25 @@ def run_ours(args, ws, rank, local):
                 "algorithmic_bytes": alg, "ms_per_launch": round(per_stage[dom], 4),
                 "pairs_upper_bound_per_s": round(kept * 256 / (per_stage[dom] * 1e-3), 1)}
 
+    # render-only forward (msplat_render, msplat_metal.mm:545-772): projection,
+    # binning, sort and the forward rasteriser per frame, image left on the device
+    render = None
+    if ws == 1 and args.render_frames > 0:
+        frame = torch.empty(cfg.height, cfg.width, 3, device=dev)
+        for k in range(3):
+            B.render(g, cams[k % C], cfg.degree, bg, out_img=frame)
+        torch.cuda.synchronize()
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record(stream)
+        for k in range(args.render_frames):
+            B.render(g, cams[k % C], cfg.degree, bg, out_img=frame)
+        r1.record(stream)
+        torch.cuda.synchronize()
+        rms = r0.elapsed_time(r1) / args.render_frames
+        render = {"value": round(1000.0 / rms, 2), "unit": "frames/s", "ms_per_frame": round(rms, 3),
+                  "frames": args.render_frames, "path": "msplat_render, image kept on the device"}
+        del frame
+
     # e2e through the public trainer API (msplat_trainer_step): every step
     # copies its target image host->device from pinned memory and reads the
     # loss back, as a user of msplat_c_api.h does.
@@ -278,6 +299,18 @@ def run_ours(args, ws, rank, local):
         e2e = {"value": round(1.0 / e2e_s, 3), "unit": "iters/s", "h2d_bytes_per_step": int(host_imgs[0].nbytes),
                "d2h_bytes_per_step": 4, "steps": e2e_steps,
                "path": "msplat_trainer_step (public C API): target image H2D from pinned memory, loss D2H, sync"}
+        if render is not None:
+            # viewer path: msplat_trainer_render_pose_to_buffer, RGBA8 into a host buffer
+            pose = ds.camera_pose(0)
+            for _ in range(2):
+                trainer.render_rgba(pose, 0)
+            t0 = time.perf_counter()
+            nv = min(10, args.render_frames)
+            for _ in range(nv):
+                trainer.render_rgba(pose, 0)
+            render["e2e_rgba8"] = {"value": round(nv / (time.perf_counter() - t0), 2), "unit": "frames/s",
+                                   "d2h_bytes_per_frame": cfg.width * cfg.height * 4,
+                                   "path": "msplat_trainer_render_pose_to_buffer (public C API), RGBA8 to host"}
         del trainer, ds
     elif e2e_steps > 0:
         host_gt = [gts[k].cpu().pin_memory() for k in range(min(C, 4))]
@@ -313,7 +346,7 @@ def run_ours(args, ws, rank, local):
                            "parallelism": f"tile-row sharding x{ws}" if ws > 1 else "single GPU",
                            "l2": "inputs larger than L2 (params+Adam state %.1f GB)" % (n * 58 * 12 / 1e9)},
                 "mpix_per_s": round(pixels * value / 1e6, 2),
-                "e2e": e2e, "gpu_launches": int(launches), "clocks": clk, "roofline": roof,
+                "e2e": e2e, "render": render, "gpu_launches": int(launches), "clocks": clk, "roofline": roof,
                 "stage_ms": {k: round(v, 4) for k, v in per_stage.items()},
                 "intersections": kept, "visible_gaussians": n_vis, "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
