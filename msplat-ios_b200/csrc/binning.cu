@@ -14,9 +14,12 @@
 //      and scans both the raw and the kept counts;
 //   3. each (Gaussian, tile) pair appends the key (depth_bits << 32) | id into
 //      its tile's raw segment (slot order is irrelevant, the set is exact);
-//   4. one CTA per tile keeps, for overfull tiles, the 2048 lowest Gaussian
-//      ids (a three-pass radix select on the id bits) and sorts the kept keys
-//      ascending in shared memory. Output: the sorted Gaussian ids.
+//   4. per tile, the kept keys are sorted ascending with a register-blocked
+//      bitonic network (keys in registers; partners in the same warp reached
+//      by shuffles, only cross-warp partners through shared memory): one warp
+//      per tile up to 512 keys, one CTA above that; for an overfull tile the
+//      CTA first keeps the 2048 lowest Gaussian ids (a three-pass radix select
+//      on the id bits). Output: the sorted Gaussian ids.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -155,89 +158,227 @@ k_emit_keys(int n, const uint2* __restrict__ rects, const float* __restrict__ de
 }
 
 constexpr int kSortThreads = 256;
+constexpr int kWarpSortMax = 512;  // tiles up to this many keys are sorted by one warp
 
-__device__ __forceinline__ void bitonic_sort(uint64_t* data, int n) {
-    for (int k = 2; k <= n; k <<= 1) {
+// Compare-exchange for an ascending (up) or descending block.
+__device__ __forceinline__ void cmp_swap(uint64_t& a, uint64_t& b, bool up) {
+    const bool sw = (a > b) == up;
+    const uint64_t lo = sw ? b : a, hi = sw ? a : b;
+    a = lo;
+    b = hi;
+}
+
+// v = min(v, o) when keep_min, else max(v, o).
+__device__ __forceinline__ uint64_t keep_of(uint64_t v, uint64_t o, bool keep_min) {
+    return ((v < o) == keep_min) ? v : o;
+}
+
+// Bitonic sort of G * E 64-bit keys held "blocked": thread t of the group
+// holds elements [E t, E t + E) in v.
+//  - block sizes k <= E stay inside the thread: a compile-time network;
+//  - for k > E the direction (element & k) is the same for all of a thread's
+//    elements; stages with partner distance j < E are register
+//    compare-exchanges, j < 32 E shuffles within the warp, and larger j go
+//    through shared memory (xchg, G * E keys, element (t, r) stored at
+//    r * G + t so that a warp's accesses hit distinct banks).
+template <int E, int G>
+__device__ __forceinline__ void bitonic_blocked(uint64_t (&v)[E], int t, uint64_t* xchg) {
+    const int lane = t & 31;
+    const int base = t * E;
+#pragma unroll
+    for (int k = 2; k <= E; k <<= 1) {
+#pragma unroll
         for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int q = threadIdx.x; q < (n >> 1); q += kSortThreads) {
-                const int lo = ((q & ~(j - 1)) << 1) | (q & (j - 1));
-                const int hi = lo | j;
-                const bool up = (lo & k) == 0;
-                const uint64_t a = data[lo], b = data[hi];
-                if ((a > b) == up) {
-                    data[lo] = b;
-                    data[hi] = a;
-                }
+#pragma unroll
+            for (int r = 0; r < E; ++r) {
+                const int p = r ^ j;
+                if (p > r) cmp_swap(v[r], v[p], (((base + r) & k) == 0));
             }
-            __syncthreads();
+        }
+    }
+    for (int k = 2 * E; k <= G * E; k <<= 1) {
+        const bool up = (base & k) == 0;
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            if (j < E) {
+#pragma unroll
+                for (int jj = 1; jj < E; jj <<= 1) {
+                    if (jj == j) {
+#pragma unroll
+                        for (int r = 0; r < E; ++r) {
+                            const int p = r ^ jj;
+                            if (p > r) cmp_swap(v[r], v[p], up);
+                        }
+                    }
+                }
+            } else if (G == 32 || j < 32 * E) {
+                const int lm = j / E;
+                const bool keep_min = ((lane & lm) == 0) == up;
+#pragma unroll
+                for (int r = 0; r < E; ++r) v[r] = keep_of(v[r], __shfl_xor_sync(0xffffffffu, v[r], lm), keep_min);
+            } else if constexpr (G > 32) {
+                const int pt = t ^ (j / E);
+                const bool keep_min = ((base & j) == 0) == up;
+                __syncthreads();
+#pragma unroll
+                for (int r = 0; r < E; ++r) xchg[r * G + t] = v[r];
+                __syncthreads();
+#pragma unroll
+                for (int r = 0; r < E; ++r) v[r] = keep_of(v[r], xchg[r * G + pt], keep_min);
+            }
         }
     }
 }
 
+template <int E, int G>
+__device__ __forceinline__ void sort_and_store(const uint64_t* src, int count, int t, uint64_t* xchg, int32_t* dst,
+                                               int kept) {
+    uint64_t v[E];
+#pragma unroll
+    for (int r = 0; r < E; ++r) {
+        const int e = t * E + r;
+        v[r] = e < count ? src[e] : ~0ull;
+    }
+    bitonic_blocked<E, G>(v, t, xchg);
+#pragma unroll
+    for (int r = 0; r < E; ++r) {
+        const int e = t * E + r;
+        if (e < kept) dst[e] = (int32_t)(uint32_t)v[r];
+    }
+}
+
+// Tiles with at most kWarpSortMax keys: one warp per tile, no barriers.
+__global__ void __launch_bounds__(kSortThreads)
+k_tile_sort_warp(const int32_t* __restrict__ raw_counts, const int64_t* __restrict__ raw_start,
+                 const uint64_t* __restrict__ keys, const int2* __restrict__ tile_bins,
+                 int32_t* __restrict__ gaussian_ids, int tile0, int num_tiles) {
+    const int w = blockIdx.x * (kSortThreads / 32) + (threadIdx.x >> 5);
+    if (w >= num_tiles) return;
+    const int t = tile0 + w;
+    const int count = raw_counts[t];
+    if (count <= 0 || count > kWarpSortMax) return;
+    const uint64_t* src = keys + raw_start[t];
+    int32_t* dst = gaussian_ids + tile_bins[t].x;
+    const int lane = threadIdx.x & 31;
+    if (count <= 128)
+        sort_and_store<4, 32>(src, count, lane, nullptr, dst, count);
+    else if (count <= 256)
+        sort_and_store<8, 32>(src, count, lane, nullptr, dst, count);
+    else
+        sort_and_store<16, 32>(src, count, lane, nullptr, dst, count);
+}
+
+constexpr int kSelectBins = 4096;
+
+// Exclusive scan of one int per thread over the CTA.
+__device__ __forceinline__ int cta_exclusive_scan(int v) {
+    __shared__ int warp_sum[kSortThreads / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int inc = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, inc, d);
+        if (lane >= d) inc += o;
+    }
+    if (lane == 31) warp_sum[warp] = inc;
+    __syncthreads();
+    int base = 0;
+#pragma unroll
+    for (int w = 0; w < kSortThreads / 32; ++w) base += (w < warp) ? warp_sum[w] : 0;
+    __syncthreads();
+    return base + inc - v;
+}
+
+// Smallest digit d of the histogram with sum(hist[0..d]) >= need; writes d
+// and need - sum(hist[0..d-1]). Requires sum(hist) >= need.
+__device__ __forceinline__ void find_digit(const int* hist, int need, int* s_digit, int* s_need) {
+    constexpr int per = kSelectBins / kSortThreads;
+    int local[per];
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < per; ++i) {
+        local[i] = hist[threadIdx.x * per + i];
+        sum += local[i];
+    }
+    const int ex = cta_exclusive_scan(sum);
+    if (ex < need && ex + sum >= need) {
+        int cum = ex;
+#pragma unroll
+        for (int i = 0; i < per; ++i) {
+            if (cum + local[i] >= need) {
+                *s_digit = threadIdx.x * per + i;
+                *s_need = need - cum;
+                break;
+            }
+            cum += local[i];
+        }
+    }
+    __syncthreads();
+}
+
+// Tiles with more than kWarpSortMax keys: one CTA per tile; for overfull
+// tiles first the radix select of the 2048 lowest ids.
 __global__ void __launch_bounds__(kSortThreads)
 k_tile_sort(const int32_t* __restrict__ raw_counts, const int64_t* __restrict__ raw_start,
             const uint64_t* __restrict__ keys, const int2* __restrict__ tile_bins,
             int32_t* __restrict__ gaussian_ids, int tile0, uint32_t* err) {
     __shared__ uint64_t data[kMaxTileElems];
-    __shared__ int hist[256];
+    __shared__ int hist[kSelectBins];
     __shared__ uint32_t s_prefix;
-    __shared__ int s_need, s_count;
+    __shared__ int s_digit, s_need, s_count;
     const int t = tile0 + blockIdx.x;
     const int count = raw_counts[t];
-    if (count <= 0) return;
+    if (count <= kWarpSortMax) return;
     const uint64_t* src = keys + raw_start[t];
-    const int out = tile_bins[t].x;
-    int n;
+    int32_t* dst = gaussian_ids + tile_bins[t].x;
     if (count <= kMaxTileElems) {
-        n = 1;
-        while (n < count) n <<= 1;
-        for (int q = threadIdx.x; q < n; q += kSortThreads) data[q] = q < count ? src[q] : ~0ull;
-        __syncthreads();
-    } else {
-        // Radix select on the 24-bit Gaussian id: find theta such that exactly
-        // 2048 ids of this tile are <= theta.
-        if (threadIdx.x == 0) {
-            s_prefix = 0;
-            s_need = kMaxTileElems;
-            if (err) atomicOr(err, kErrTileOverflow);
-        }
-        for (int shift = 16; shift >= 0; shift -= 8) {
-            hist[threadIdx.x] = 0;
-            __syncthreads();
-            const uint32_t prefix = s_prefix;
-            for (int q = threadIdx.x; q < count; q += kSortThreads) {
-                const uint32_t id = (uint32_t)src[q];
-                if ((id >> (shift + 8)) == prefix) atomicAdd(&hist[(id >> shift) & 255], 1);
-            }
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                int need = s_need, cum = 0, d = 0;
-                for (; d < 256; ++d) {
-                    if (cum + hist[d] >= need) break;
-                    cum += hist[d];
-                }
-                s_need = need - cum;
-                s_prefix = (prefix << 8) | (uint32_t)d;
-            }
-            __syncthreads();
-        }
-        const uint32_t theta = s_prefix;
-        if (threadIdx.x == 0) s_count = 0;
-        __syncthreads();
-        for (int q = threadIdx.x; q < count; q += kSortThreads) {
-            const uint64_t key = src[q];
-            if ((uint32_t)key <= theta) {
-                const int slot = atomicAdd(&s_count, 1);
-                if (slot < kMaxTileElems) data[slot] = key;
-            }
-        }
-        __syncthreads();
-        if (threadIdx.x == 0 && s_count != kMaxTileElems && err) atomicOr(err, kErrCapacity);
-        n = kMaxTileElems;
+        if (count <= 4 * kSortThreads)
+            sort_and_store<4, kSortThreads>(src, count, threadIdx.x, data, dst, count);
+        else
+            sort_and_store<8, kSortThreads>(src, count, threadIdx.x, data, dst, count);
+        return;
     }
-    bitonic_sort(data, n);
-    const int kept = min(count, kMaxTileElems);
-    for (int q = threadIdx.x; q < kept; q += kSortThreads) gaussian_ids[out + q] = (int32_t)(uint32_t)data[q];
+    // Radix select on the 24-bit Gaussian id (two 12-bit digits): find theta
+    // such that exactly 2048 ids of this tile are <= theta.
+    if (threadIdx.x == 0 && err) atomicOr(err, kErrTileOverflow);
+    for (int q = threadIdx.x; q < kSelectBins; q += kSortThreads) hist[q] = 0;
+    __syncthreads();
+    for (int q = threadIdx.x; q < count; q += kSortThreads) atomicAdd(&hist[((uint32_t)src[q] >> 12) & 4095], 1);
+    __syncthreads();
+    find_digit(hist, kMaxTileElems, &s_digit, &s_need);
+    const uint32_t hi_digit = (uint32_t)s_digit;
+    const int need2 = s_need;
+    for (int q = threadIdx.x; q < kSelectBins; q += kSortThreads) hist[q] = 0;
+    __syncthreads();
+    for (int q = threadIdx.x; q < count; q += kSortThreads) {
+        const uint32_t id = (uint32_t)src[q];
+        if (((id >> 12) & 4095) == hi_digit) atomicAdd(&hist[id & 4095], 1);
+    }
+    __syncthreads();
+    find_digit(hist, need2, &s_digit, &s_need);
+    if (threadIdx.x == 0) s_prefix = (hi_digit << 12) | (uint32_t)s_digit;
+    __syncthreads();
+    const uint32_t theta = s_prefix;
+    if (threadIdx.x == 0) s_count = 0;
+    __syncthreads();
+    for (int q = threadIdx.x; q < count; q += kSortThreads) {
+        const uint64_t key = src[q];
+        if ((uint32_t)key <= theta) {
+            const int slot = atomicAdd(&s_count, 1);
+            if (slot < kMaxTileElems) data[slot] = key;
+        }
+    }
+    __syncthreads();
+    const int got = s_count;
+    if (threadIdx.x == 0 && got != kMaxTileElems && err) atomicOr(err, kErrCapacity);
+    uint64_t v[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        const int e = threadIdx.x * 8 + r;
+        v[r] = e < got && e < kMaxTileElems ? data[e] : ~0ull;
+    }
+    bitonic_blocked<8, kSortThreads>(v, threadIdx.x, data);
+#pragma unroll
+    for (int r = 0; r < 8; ++r) dst[threadIdx.x * 8 + r] = (int32_t)(uint32_t)v[r];
 }
 
 }  // namespace
@@ -261,7 +402,11 @@ void launch_tile_sort(int tile0, int num_tiles, const int32_t* raw_counts, const
                       const uint64_t* raw_keys, const int2* tile_bins, int32_t* gaussian_ids, uint32_t* err,
                       cudaStream_t s) {
     if (num_tiles <= 0) return;
-    note_launches(1);
+    note_launches(2);
+    const int warps = kSortThreads / 32;
+    k_tile_sort_warp<<<(num_tiles + warps - 1) / warps, kSortThreads, 0, s>>>(raw_counts, raw_start, raw_keys,
+                                                                              tile_bins, gaussian_ids, tile0,
+                                                                              num_tiles);
     k_tile_sort<<<num_tiles, kSortThreads, 0, s>>>(raw_counts, raw_start, raw_keys, tile_bins, gaussian_ids, tile0,
                                                     err);
 }
