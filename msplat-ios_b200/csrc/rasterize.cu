@@ -19,9 +19,10 @@
 // the surfel (one bit per warp); the backward drops entries no warp blended
 // and each warp visits only its own, so pairs that were rejected in the
 // forward are not evaluated again. In the backward the per-(pixel, surfel)
-// gradients are summed across the warp with a recursive halving exchange
-// (16 values in 16 shuffles), across warps in shared memory, and leave the
-// CTA as four float4 atomics per surfel. The replayed pair evaluation uses
+// gradients are summed across the warp through a per-warp transpose buffer in
+// shared memory (13 stores, four 16-byte loads and one shuffle per lane),
+// across warps in shared memory, and leave the CTA as four float4 atomics per
+// surfel. The replayed pair evaluation uses
 // the forward's exact operation sequence; the gradient arithmetic after it
 // uses fast reciprocals.
 #include "common.cuh"
@@ -244,48 +245,34 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
     a.out_distortion[pix] = dist;
 }
 
-// Sums v[0..15] across the warp; afterwards lane L (L even) holds the total of
-// value index L >> 1 (odd lanes hold a copy).
-__device__ __forceinline__ float warp_halving_sum16(float (&v)[16], int lane) {
-    constexpr unsigned full = 0xffffffffu;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const bool up = lane & 16;
-        const float send = up ? v[k] : v[k + 8];
-        const float keep = up ? v[k + 8] : v[k];
-        v[k] = keep + __shfl_xor_sync(full, send, 16);
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const bool up = lane & 8;
-        const float send = up ? v[k] : v[k + 4];
-        const float keep = up ? v[k + 4] : v[k];
-        v[k] = keep + __shfl_xor_sync(full, send, 8);
-    }
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const bool up = lane & 4;
-        const float send = up ? v[k] : v[k + 2];
-        const float keep = up ? v[k + 2] : v[k];
-        v[k] = keep + __shfl_xor_sync(full, send, 4);
-    }
-    {
-        const bool up = lane & 2;
-        const float send = up ? v[0] : v[1];
-        const float keep = up ? v[1] : v[0];
-        v[0] = keep + __shfl_xor_sync(full, send, 2);
-    }
-    v[0] += __shfl_xor_sync(full, v[0], 1);
-    return v[0];
+// Gradient values reduced per (warp, surfel): 13 for the colour-only kernel,
+// 16 with the auxiliary (normal) gradients.
+template <bool AUX>
+constexpr int bwd_values() { return AUX ? 16 : 13; }
+// Dynamic shared memory of k_raster_bwd: records [5][256] float4, the
+// per-batch accumulator [256][16] and the per-warp transpose buffers
+// [8][NV][36] of the warp reduction.
+template <bool AUX>
+constexpr size_t bwd_dynamic_smem() {
+    return sizeof(float4) * kRecordF4 * kThreads + sizeof(float) * kThreads * kGradStride +
+           sizeof(float) * (kThreads / 32) * bwd_values<AUX>() * 36;
 }
 
 template <bool AUX>
 __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
-    __shared__ float4 srec[kRecordF4][kThreads];
+    extern __shared__ __align__(16) unsigned char dsm[];
+    constexpr int NV = bwd_values<AUX>();
+    float4 (*srec)[kThreads] = reinterpret_cast<float4 (*)[kThreads]>(dsm);
+    float (*sacc)[kGradStride] =
+        reinterpret_cast<float (*)[kGradStride]>(dsm + sizeof(float4) * kRecordF4 * kThreads);
+    // per-warp transpose buffer of the warp reduction: value k of lane L at
+    // [k][L]; rows of 36 floats keep both the stores and the 16-byte loads
+    // free of bank conflicts
+    float (*sred)[NV][36] = reinterpret_cast<float (*)[NV][36]>(
+        dsm + sizeof(float4) * kRecordF4 * kThreads + sizeof(float) * kThreads * kGradStride);
     __shared__ int sid[kThreads];
     __shared__ int srel[kThreads];       // 0-based position in the tile list
     __shared__ uint8_t smask[kThreads];  // warps that blended the surfel in the forward
-    __shared__ float sacc[kThreads][kGradStride];
     __shared__ int swarp_cnt[kThreads / 32];
     __shared__ int s_max_last;
     constexpr unsigned full = 0xffffffffu;
@@ -443,10 +430,24 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
                     }
                     g[9] = G * dL_dalpha * (opa * (1.0f - opa));
                 }
-                // the forward's flags guarantee a contributing lane here
-                const float tot = warp_halving_sum16(g, lane);
+                // the forward's flags guarantee a contributing lane here: sum
+                // value vi over the warp, lanes 2 vi and 2 vi + 1 each adding
+                // 16 of the 32 lanes' entries
+                float* wb = &sred[warp][0][0];
+#pragma unroll
+                for (int k = 0; k < NV; ++k) wb[k * 36 + lane] = g[k];
+                __syncwarp();
                 const int vi = lane >> 1;
-                if (!(lane & 1) && (AUX || vi < 13) && tot != 0.f) atomicAdd(&sacc[s][vi], tot);
+                float tot = 0.f;
+                if (vi < NV) {
+                    const float4* row = reinterpret_cast<const float4*>(wb + vi * 36 + (lane & 1) * 16);
+                    const float4 q0 = row[0], q1 = row[1], q2 = row[2], q3 = row[3];
+                    tot = ((q0.x + q0.y) + (q0.z + q0.w)) + ((q1.x + q1.y) + (q1.z + q1.w)) +
+                          (((q2.x + q2.y) + (q2.z + q2.w)) + ((q3.x + q3.y) + (q3.z + q3.w)));
+                }
+                tot += __shfl_xor_sync(full, tot, 1);
+                __syncwarp();
+                if (!(lane & 1) && vi < NV && tot != 0.f) atomicAdd(&sacc[s][vi], tot);
             }
         }
         __syncthreads();
@@ -475,10 +476,17 @@ void launch_rasterize_backward(const RasterBwdArgs& a, cudaStream_t s) {
     const bool aux = a.dL_dout_depth || a.dL_dout_alpha || a.dL_dout_normal || a.dL_dout_median_depth ||
                      a.dL_dout_distortion != 0.0f;
     note_launches(1);
-    if (aux)
-        k_raster_bwd<true><<<dim3(a.tiles_x, rows), kThreads, 0, s>>>(a);
-    else
-        k_raster_bwd<false><<<dim3(a.tiles_x, rows), kThreads, 0, s>>>(a);
+    if (aux) {
+        constexpr size_t smem = bwd_dynamic_smem<true>();
+        cudaFuncSetAttribute(k_raster_bwd<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_raster_bwd<true>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        k_raster_bwd<true><<<dim3(a.tiles_x, rows), kThreads, smem, s>>>(a);
+    } else {
+        constexpr size_t smem = bwd_dynamic_smem<false>();
+        cudaFuncSetAttribute(k_raster_bwd<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_raster_bwd<false>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        k_raster_bwd<false><<<dim3(a.tiles_x, rows), kThreads, smem, s>>>(a);
+    }
 }
 
 }  // namespace msplat
