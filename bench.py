@@ -298,7 +298,9 @@ def run_ours(args, ws, rank, local):
         e2e_s = (time.perf_counter() - t0) / e2e_steps
         e2e = {"value": round(1.0 / e2e_s, 3), "unit": "iters/s", "h2d_bytes_per_step": int(host_imgs[0].nbytes),
                "d2h_bytes_per_step": 4, "steps": e2e_steps,
-               "path": "msplat_trainer_step (public C API): target image H2D from pinned memory, loss D2H, sync"}
+               "path": ("msplat_trainer_step (public C API): each step's target image H2D from pinned memory "
+                        "(the trainer copies the next camera's image on a copy stream during the current step), "
+                        "loss D2H, sync")}
         if render is not None:
             # viewer path: msplat_trainer_render_pose_to_buffer, RGBA8 into a host buffer
             pose = ds.camera_pose(0)
@@ -313,23 +315,55 @@ def run_ours(args, ws, rank, local):
                                    "path": "msplat_trainer_render_pose_to_buffer (public C API), RGBA8 to host"}
         del trainer, ds
     elif e2e_steps > 0:
+        # each step's target is copied host->device on a copy stream while the
+        # previous step computes (two device buffers)
         host_gt = [gts[k].cpu().pin_memory() for k in range(min(C, 4))]
-        dev_gt = torch.empty_like(gts[0])
+        dev_gt = [torch.empty_like(gts[0]), torch.empty_like(gts[0])]
+        copy_stream = torch.cuda.Stream(device=dev)
+        ready = [torch.cuda.Event(), torch.cuda.Event()]
+        free = [torch.cuda.Event(), torch.cuda.Event()]
         parts_host = torch.zeros(3, dtype=torch.float64).pin_memory()
+        for b in range(2):
+            free[b].record(stream)
+
+        def prefetch(k):
+            b = k % 2
+            copy_stream.wait_event(free[b])
+            with torch.cuda.stream(copy_stream):
+                dev_gt[b].copy_(host_gt[k % len(host_gt)], non_blocking=True)
+                ready[b].record(copy_stream)
+
         dist.barrier()
         t0 = time.perf_counter()
+        prefetch(0)
         for k in range(e2e_steps):
-            dev_gt.copy_(host_gt[k % len(host_gt)], non_blocking=True)
+            b = k % 2
+            stream.wait_event(ready[b])
             adam.step += 1
-            fb, pa = sharding.gpu_step_fns(B, g, cams[k % C], cfg.degree, bg, dev_gt, l1, ld, SSIM_WEIGHT, adam, stats)
+            fb, pa = sharding.gpu_step_fns(B, g, cams[k % C], cfg.degree, bg, dev_gt[b], l1, ld, SSIM_WEIGHT, adam,
+                                           stats)
             sharding.sharded_step(dist, plan, fb, pa, rg, rg_shard, g.full, parts)
+            free[b].record(stream)
+            if k + 1 < e2e_steps:
+                prefetch(k + 1)
             parts_host.copy_(parts, non_blocking=True)
             stream.synchronize()
         e2e_s = torch.tensor([(time.perf_counter() - t0) / e2e_steps], device=dev, dtype=torch.float64)
         dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
         e2e = {"value": round(1.0 / float(e2e_s.item()), 3), "unit": "iters/s",
                "h2d_bytes_per_step": int(gts[0].numel() * 4), "d2h_bytes_per_step": 24, "steps": e2e_steps,
-               "path": "msplat_shard_* C ABI + NCCL per rank: target image H2D from pinned memory, loss sums D2H"}
+               "path": ("msplat_shard_* C ABI + NCCL per rank: target image H2D from pinned memory on a copy "
+                        "stream overlapping the previous step, loss sums D2H")}
+
+    ranks = None
+    if ws > 1:
+        mine = {"rank": rank, "tile_rows": [plan.row0, plan.row1], "intersections": kept,
+                "rasterize_forward_ms": round(per_stage.get("rasterize_forward", 0.0), 4),
+                "rasterize_backward_ms": round(per_stage.get("rasterize_backward", 0.0), 4),
+                "loss_ssim_ms": round(per_stage.get("loss_ssim", 0.0), 4),
+                "stage_sum_ms": round(sum(per_stage.values()), 4)}
+        ranks = [None] * ws
+        dist.all_gather_object(ranks, mine)
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -349,6 +383,8 @@ def run_ours(args, ws, rank, local):
                 "e2e": e2e, "render": render, "gpu_launches": int(launches), "clocks": clk, "roofline": roof,
                 "stage_ms": {k: round(v, 4) for k, v in per_stage.items()},
                 "intersections": kept, "visible_gaussians": n_vis, "cpu_baseline": cpu}
+        if ranks is not None:
+            line["ranks"] = ranks
         print(json.dumps(line), flush=True)
     if ws > 1:
         dist.barrier()

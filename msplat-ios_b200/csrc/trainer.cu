@@ -171,8 +171,24 @@ struct Trainer {
     DevArray<uint8_t> rgba;
     float* loss_host = nullptr;  // pinned
     cudaStream_t stream = nullptr;
+    // Full-resolution targets of training cameras, double-buffered: while a
+    // step computes, the next camera's image is copied into the other buffer
+    // on copy_stream (the reference reads images through unified memory and
+    // needs no copy, msplat_api.mm / input_data.cpp:17-75).
+    DevArray<float> tgt[2];
+    long tgt_cam[2] = {-1, -1};
+    int tgt_cur = 0;
+    cudaEvent_t tgt_ready[2] = {nullptr, nullptr}, tgt_free[2] = {nullptr, nullptr};
+    cudaStream_t copy_stream = nullptr;
 
     ~Trainer() {
+        if (copy_stream) cudaStreamSynchronize(copy_stream);
+        if (stream) cudaStreamSynchronize(stream);
+        for (int b = 0; b < 2; ++b) {
+            if (tgt_ready[b]) cudaEventDestroy(tgt_ready[b]);
+            if (tgt_free[b]) cudaEventDestroy(tgt_free[b]);
+        }
+        if (copy_stream) cudaStreamDestroy(copy_stream);
         if (loss_host) cudaFreeHost(loss_host);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -190,6 +206,12 @@ struct Trainer {
         loss_dev.alloc(1);
         CKT(cudaHostAlloc(reinterpret_cast<void**>(&loss_host), sizeof(float), cudaHostAllocDefault));
         CKT(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+        CKT(cudaStreamCreateWithFlags(&copy_stream, cudaStreamNonBlocking));
+        for (int b = 0; b < 2; ++b) {
+            CKT(cudaEventCreateWithFlags(&tgt_ready[b], cudaEventDisableTiming));
+            CKT(cudaEventCreateWithFlags(&tgt_free[b], cudaEventDisableTiming));
+            CKT(cudaEventRecord(tgt_free[b], stream));
+        }
         cam_indices.resize(ds->train.size());
         std::iota(cam_indices.begin(), cam_indices.end(), 0);
         shuffle();
@@ -202,6 +224,51 @@ struct Trainer {
     size_t next_camera() {
         if (cam_pos >= cam_indices.size()) shuffle();
         return cam_indices[cam_pos++];
+    }
+    // The camera next_camera() will return (shuffling a little early does not
+    // change the order).
+    size_t peek_camera() {
+        if (cam_pos >= cam_indices.size()) shuffle();
+        return cam_indices[cam_pos];
+    }
+
+    // Full-resolution target of training camera ci on the device, ordered
+    // before the work that `stream` receives next.
+    const float* train_target(size_t ci) {
+        const Camera& c = ds->train[ci];
+        if (!c.image) throw ApiError("camera has no image");
+        for (int b = 0; b < 2; ++b)
+            if (tgt_cam[b] == (long)ci) {
+                CKT(cudaStreamWaitEvent(stream, tgt_ready[b], 0));
+                tgt_cur = b;
+                return tgt[b].p;
+            }
+        const int b = 1 - tgt_cur;
+        const size_t full = (size_t)c.width * c.height * 3;
+        tgt[b].ensure(full);
+        tgt_cam[b] = -1;
+        CKT(cudaStreamWaitEvent(stream, tgt_free[b], 0));
+        CKT(cudaMemcpyAsync(tgt[b].p, c.image, full * sizeof(float), cudaMemcpyHostToDevice, stream));
+        tgt_cam[b] = (long)ci;
+        tgt_cur = b;
+        return tgt[b].p;
+    }
+
+    // After the step's work on buffer tgt_cur is enqueued: mark it, and start
+    // copying camera ci's target into the other buffer on copy_stream.
+    void prefetch_target(size_t ci) {
+        CKT(cudaEventRecord(tgt_free[tgt_cur], stream));
+        const int b = 1 - tgt_cur;
+        if (tgt_cam[b] == (long)ci || tgt_cam[tgt_cur] == (long)ci) return;
+        const Camera& c = ds->train[ci];
+        if (!c.image) return;
+        const size_t full = (size_t)c.width * c.height * 3;
+        tgt[b].ensure(full);
+        tgt_cam[b] = -1;
+        CKT(cudaStreamWaitEvent(copy_stream, tgt_free[b], 0));
+        CKT(cudaMemcpyAsync(tgt[b].p, c.image, full * sizeof(float), cudaMemcpyHostToDevice, copy_stream));
+        CKT(cudaEventRecord(tgt_ready[b], copy_stream));
+        tgt_cam[b] = (long)ci;
     }
 
     void upload(int g, const float* host) {
@@ -249,10 +316,16 @@ struct Trainer {
     MsplatStats step() {  // Trainer::step, msplat_api.mm:106-128
         if (ds->train.empty()) throw ApiError("dataset has no training cameras");
         current_step++;
-        const Camera& c = ds->train[next_camera()];
+        const size_t ci = next_camera();
+        const Camera& c = ds->train[ci];
         const int sf = downscale_factor(current_step);
         const MsplatCamera cam = prepare(c, sf);
-        const float* gt = target(c, sf, cam);
+        const float* gt = train_target(ci);
+        if (sf != 1) {
+            gt_scaled.ensure((size_t)cam.width * cam.height * 3);
+            launch_resize_area(gt, c.width, c.height, gt_scaled.p, cam.width, cam.height, stream);
+            gt = gt_scaled.p;
+        }
         last_w = cam.width;
         last_h = cam.height;
         auto t0 = std::chrono::high_resolution_clock::now();
@@ -272,6 +345,7 @@ struct Trainer {
         check_rc(msplat_train_step_fused(&G, &cam, degrees_to_use, cfg.bgColor, gt, 1.0f - cfg.ssimWeight, 0.0f,
                                          cfg.ssimWeight, &A, stats[0].p, stats[1].p, stats[2].p, loss_dev.p, 0,
                                          stream));
+        prefetch_target(peek_camera());
         // schedulersStep (model.cpp:183-186), then afterTrain (:240-306)
         lr[0] = msplat_means_lr(current_step, cfg.iterations, means_lr_init, means_lr_final);
         CKT(cudaMemcpyAsync(loss_host, loss_dev.p, sizeof(float), cudaMemcpyDeviceToHost, stream));
