@@ -81,8 +81,7 @@ struct Workspace {
     Buf final_Ts, final_idx, out_img, out_depth, out_normal, out_alpha, out_median, out_dist, dL_dout_img;
     // scalars
     Buf loss_partials, loss_out, loss_f, err, totals, row_work;
-    std::vector<int64_t> h_row_work;
-    int64_t* h_totals = nullptr;  // pinned [2]
+    int64_t* h_totals = nullptr;  // pinned [4]: raw, kept, band begin, band end
     uint32_t* h_err = nullptr;    // pinned [1]
     // shape bookkeeping of the last call
     int n = 0, K = 0, W = 0, H = 0, tx = 0, ty = 0;
@@ -123,10 +122,13 @@ std::vector<Workspace*> g_ws;
 // Stage timing: CUDA events recorded on the launch stream at stage
 // boundaries, read back only when msplat_stage_times() is called.
 enum Stage { kStProject = 0, kStCounts, kStEmit, kStSort, kStRasterFwd, kStLoss, kStRasterBwd, kStProjectBwd,
-             kNumStages };
+             kStBetweenShardCalls, kNumStages };
+// between_shard_calls: from the end of msplat_shard_forward_backward to the
+// start of msplat_shard_project_backward_adam on the stream (the caller's
+// reduce-scatter and any wait for slower ranks)
 const char* kStageNames[kNumStages] = {"project_forward", "tile_counts", "emit_keys", "tile_sort",
                                        "rasterize_forward", "loss_ssim", "rasterize_backward",
-                                       "project_backward_adam"};
+                                       "project_backward_adam", "between_shard_calls"};
 bool g_timing = false;
 double g_stage_ms[kNumStages] = {};
 int64_t g_stage_n[kNumStages] = {};
@@ -142,7 +144,7 @@ Workspace& workspace() {
     }
     Workspace& w = *g_ws[dev];
     if (!w.h_totals) {
-        CK(cudaHostAlloc(reinterpret_cast<void**>(&w.h_totals), 2 * sizeof(int64_t), cudaHostAllocDefault));
+        CK(cudaHostAlloc(reinterpret_cast<void**>(&w.h_totals), 4 * sizeof(int64_t), cudaHostAllocDefault));
         CK(cudaHostAlloc(reinterpret_cast<void**>(&w.h_err), sizeof(uint32_t), cudaHostAllocDefault));
     }
     return w;
@@ -218,27 +220,6 @@ CameraDev make_cam(const MsplatCamera* c) {
 }
 
 // Projection, binning, sort and forward rasterisation of tile rows
-// [row0, row1). Fills the workspace; returns nothing.
-// Splits tile rows into `world` contiguous bands of about equal work; returns
-// band `rank` as [*b0, *b1).
-void balanced_band(const std::vector<int64_t>& work, int world, int rank, int* b0, int* b1) {
-    const int ty = (int)work.size();
-    double total = 0;
-    for (int64_t v : work) total += (double)v;
-    auto cut = [&](int r) {  // first row of band r
-        if (r <= 0) return 0;
-        if (r >= world) return ty;
-        const double target = total * r / world;
-        double run = 0;
-        int y = 0;
-        while (y < ty && run + (double)work[y] / 2 < target) run += (double)work[y++];
-        return y;
-    };
-    *b0 = cut(rank);
-    *b1 = cut(rank + 1);
-}
-
-// Projection, binning, sort and forward rasterisation of tile rows
 // [row0, row1). When balance_world > 0 the rows are chosen here instead:
 // band balance_rank of balance_world work-balanced bands, returned in
 // *owned0/*owned1, rendered with a one-tile-row halo.
@@ -269,7 +250,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     w.raw_start.ensure((size_t)T * 8);
     w.tile_bins.ensure((size_t)T * sizeof(int2));
     w.fill.ensure((size_t)T * 4);
-    w.totals.ensure(2 * sizeof(int64_t));
+    w.totals.ensure(4 * sizeof(int64_t));
     w.err.ensure(sizeof(uint32_t));
     w.final_Ts.ensure(P * 3 * 4); w.final_idx.ensure(P * 2 * 4); w.out_img.ensure(P * 3 * 4);
     w.out_depth.ensure(P * 4); w.out_normal.ensure(P * 3 * 4); w.out_alpha.ensure(P * 4);
@@ -296,27 +277,22 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     mark(w, kStProject, s);
     launch_project_forward(pa, s);
     mark(w, kStCounts, s);
+    if (balance_world > 0) w.row_work.ensure((size_t)ty * sizeof(int64_t));
+    launch_tile_counts(w.tile_diff.as<int32_t>(), tx, ty, row0, row1, w.raw_counts.as<int32_t>(),
+                       w.raw_start.as<int64_t>(), w.tile_bins.as<int2>(), w.totals.as<int64_t>(),
+                       balance_world > 0 ? w.row_work.as<int64_t>() : nullptr, s, balance_world, balance_rank);
+    // The one host read of the step: buffer sizes for the intersections (and
+    // the band the kernel chose, when balancing).
+    CK(cudaMemcpyAsync(w.h_totals, w.totals.p, 4 * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
     if (balance_world > 0) {
-        // counts over all rows -> per-row work -> this rank's band (+ halo)
-        w.row_work.ensure((size_t)ty * sizeof(int64_t));
-        launch_tile_counts(w.tile_diff.as<int32_t>(), tx, ty, 0, ty, w.raw_counts.as<int32_t>(),
-                           w.raw_start.as<int64_t>(), w.tile_bins.as<int2>(), w.totals.as<int64_t>(),
-                           w.row_work.as<int64_t>(), s);
-        w.h_row_work.resize(ty);
-        CK(cudaMemcpyAsync(w.h_row_work.data(), w.row_work.p, (size_t)ty * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
-        CK(cudaStreamSynchronize(s));
-        int o0 = 0, o1 = 0;
-        balanced_band(w.h_row_work, balance_world, balance_rank, &o0, &o1);
+        const int o0 = (int)w.h_totals[2], o1 = (int)w.h_totals[3];
+        if (o0 < 0 || o1 > ty || o0 > o1) throw Error(MSPLAT_ERR_CAPACITY, "corrupt band");
         if (owned0) *owned0 = o0;
         if (owned1) *owned1 = o1;
         row0 = o1 > o0 ? std::max(0, o0 - 1) : 0;
         row1 = o1 > o0 ? std::min(ty, o1 + 1) : 0;
     }
-    launch_tile_counts(w.tile_diff.as<int32_t>(), tx, ty, row0, row1, w.raw_counts.as<int32_t>(),
-                       w.raw_start.as<int64_t>(), w.tile_bins.as<int2>(), w.totals.as<int64_t>(), nullptr, s);
-    // The one host read of the step: buffer sizes for the intersections.
-    CK(cudaMemcpyAsync(w.h_totals, w.totals.p, 2 * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
-    CK(cudaStreamSynchronize(s));
     const int64_t raw_total = w.h_totals[0], kept = w.h_totals[1];
     if (raw_total < 0 || kept < 0 || kept > raw_total) throw Error(MSPLAT_ERR_CAPACITY, "corrupt tile totals");
     w.kept = kept;
@@ -609,6 +585,7 @@ int msplat_shard_forward_backward(const MsplatGaussians* g, const MsplatCamera* 
                 CK(cudaMemsetAsync(loss_parts_dev, 0, 3 * sizeof(double), s));
             }
         }
+        mark(w, kStBetweenShardCalls, s);
         CK(cudaGetLastError());
     });
 }

@@ -31,10 +31,28 @@ constexpr int kCountThreads = 1024;
 // fixed per-tile cost (launch, id loads, per-pixel outputs).
 constexpr int kRowWorkPerTile = 64;
 
+// First row of band r of `world` contiguous bands of about equal work
+// (rows are added while less than half of the next row's work overshoots).
+__device__ int band_cut(const int64_t* work, int ty, double total, int r, int world) {
+    if (r <= 0) return 0;
+    if (r >= world) return ty;
+    const double target = total * r / world;
+    double run = 0;
+    int y = 0;
+    while (y < ty && run + (double)work[y] / 2 < target) run += (double)work[y++];
+    return y;
+}
+
+// Per-tile intersection counts from the 2-D difference array, clamped kept
+// counts and both exclusive scans, for tile rows [row0, row1) (other rows get
+// zero counts). With world > 0 the rows are chosen here: band `rank` of
+// `world` work-balanced bands [o0, o1) plus a one-row halo; the band goes to
+// totals[2..3] next to the raw and kept totals (totals[0..1]).
 __global__ void __launch_bounds__(kCountThreads)
 k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int row0, int row1, int32_t* __restrict__ raw_counts,
               int64_t* __restrict__ raw_start, int2* __restrict__ tile_bins, int64_t* __restrict__ totals,
-              int64_t* __restrict__ row_work) {
+              int64_t* __restrict__ row_work, int world, int rank) {
+    __shared__ int s_rows[2];
     const int dw = tx + 1;
     // Column prefix over y (one thread per tile column).
     for (int x = threadIdx.x; x < tx; x += blockDim.x) {
@@ -45,19 +63,42 @@ k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int row0, int ro
         }
     }
     __syncthreads();
-    // Row prefix over x (one thread per tile row); rows outside the band
-    // [row0, row1) get zero counts so that nothing is emitted for them.
+    // Row prefix over x (one thread per tile row) and the work of each row.
     for (int y = threadIdx.x; y < ty; y += blockDim.x) {
         int run = 0;
         int64_t work = 0;
         int32_t* row = raw_counts + (size_t)y * tx;
-        const bool in_band = y >= row0 && y < row1;
         for (int x = 0; x < tx; ++x) {
             run += row[x];
-            row[x] = in_band ? run : 0;
+            row[x] = run;
             work += min(run, kMaxTileElems) + kRowWorkPerTile;
         }
         if (row_work) row_work[y] = work;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int r0 = row0, r1 = row1;
+        if (world > 0 && row_work) {
+            double total = 0;
+            for (int y = 0; y < ty; ++y) total += (double)row_work[y];
+            const int o0 = band_cut(row_work, ty, total, rank, world);
+            const int o1 = band_cut(row_work, ty, total, rank + 1, world);
+            totals[2] = o0;
+            totals[3] = o1;
+            r0 = o1 > o0 ? max(0, o0 - 1) : 0;
+            r1 = o1 > o0 ? min(ty, o1 + 1) : 0;
+        }
+        s_rows[0] = r0;
+        s_rows[1] = r1;
+    }
+    __syncthreads();
+    // Rows outside [row0, row1) get zero counts so that nothing is emitted there.
+    {
+        const int r0 = s_rows[0], r1 = s_rows[1];
+        for (int q = threadIdx.x; q < tx * ty; q += blockDim.x) {
+            const int y = q / tx;
+            if (y < r0 || y >= r1) raw_counts[q] = 0;
+        }
     }
     __syncthreads();
     // Exclusive scans of raw (int64) and kept = min(raw, 2048) (int32).
@@ -385,10 +426,10 @@ k_tile_sort(const int32_t* __restrict__ raw_counts, const int64_t* __restrict__ 
 
 void launch_tile_counts(const int32_t* tile_diff, int tiles_x, int tiles_y, int row0, int row1,
                         int32_t* raw_counts, int64_t* raw_start, int2* tile_bins, int64_t* totals,
-                        int64_t* row_work, cudaStream_t s) {
+                        int64_t* row_work, cudaStream_t s, int world, int rank) {
     note_launches(1);
     k_tile_counts<<<1, kCountThreads, 0, s>>>(tile_diff, tiles_x, tiles_y, row0, row1, raw_counts, raw_start,
-                                              tile_bins, totals, row_work);
+                                              tile_bins, totals, row_work, world, rank);
 }
 
 void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x, int row0, int row1,

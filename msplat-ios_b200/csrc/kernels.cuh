@@ -77,7 +77,8 @@ void launch_project_backward(const ProjBwdArgs& a, cudaStream_t s);
 // rows, for balancing tile-row bands across GPUs.
 void launch_tile_counts(const int32_t* tile_diff, int tiles_x, int tiles_y, int row0, int row1,
                         int32_t* raw_counts, int64_t* raw_start, int2* tile_bins, int64_t* totals,
-                        int64_t* row_work, cudaStream_t s);
+                        int64_t* row_work, cudaStream_t s,
+                        int world = 0, int rank = 0);
 void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x, int row0, int row1,
                       const int64_t* raw_start, int32_t* fill, uint64_t* raw_keys, cudaStream_t s);
 void launch_tile_sort(int tile0, int num_tiles, const int32_t* raw_counts, const int64_t* raw_start,
