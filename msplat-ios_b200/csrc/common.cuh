@@ -57,7 +57,11 @@ __device__ __forceinline__ float det_exp(float x) {
     if (x != x) return x;
     if (x > 88.0f) return __int_as_float(0x7f800000);
     if (x < -86.0f) return 0.0f;
-    float kf = rintf(__fmul_rn(x, 1.44269502f));
+    // k = nearest integer (ties to even) of x log2(e): adding 1.5 * 2^23 puts
+    // the value where the float spacing is 1, so the addition itself rounds
+    // (|x log2 e| <= 127 here); k is read from the bits of the sum.
+    const float shifted = __fadd_rn(__fmul_rn(x, 1.44269502f), 12582912.0f);
+    const float kf = __fsub_rn(shifted, 12582912.0f);
     float r = __fmaf_rn(-kf, 0.693145751953125f, x);
     r = __fmaf_rn(-kf, 1.42860677e-06f, r);
     float p = 1.98412698e-04f;
@@ -68,7 +72,7 @@ __device__ __forceinline__ float det_exp(float x) {
     p = __fmaf_rn(p, r, 0.5f);
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
-    int k = (int)kf;
+    const int k = __float_as_int(shifted) - 0x4B400000;
     return __fmul_rn(p, __int_as_float((k + 127) << 23));
 }
 
