@@ -28,8 +28,12 @@ namespace {
 
 constexpr int kCountThreads = 1024;
 // Work estimate of a tile row for band balancing: kept intersections plus a
-// fixed per-tile cost (launch, id loads, per-pixel outputs).
-constexpr int kRowWorkPerTile = 64;
+// per-tile cost in the same unit. Fitted to per-rank rasteriser + loss times
+// of 8 ranks on the 4946x3286 benchmark scene (time ~ 0.33 ns per kept
+// intersection + 144 ns per tile): per-pixel outputs and the loss cost the
+// same for every tile, and sparse regions carry larger surfels that blend
+// over more pixels per intersection.
+constexpr int kRowWorkPerTile = 430;
 
 // First row of band r of `world` contiguous bands of about equal work
 // (rows are added while less than half of the next row's work overshoots).
@@ -145,9 +149,9 @@ k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int row0, int ro
 
 // One warp per 32 consecutive Gaussians: their clipped tile rectangles are
 // flattened into (Gaussian, tile) pairs by a warp prefix sum of the areas, and
-// every lane takes one pair per round (owner found by a binary search over the
-// lanes' exclusive offsets), so a warp keeps 32 independent slot atomics in
-// flight whatever the rectangle sizes.
+// every lane takes four pairs per round (owners found by a binary search over
+// the lanes' exclusive offsets), so a warp keeps 128 independent slot atomics
+// in flight whatever the rectangle sizes.
 __global__ void __launch_bounds__(256)
 k_emit_keys(int n, const uint2* __restrict__ rects, const float* __restrict__ depths, int tx, int row0, int row1,
             const int64_t* __restrict__ raw_start, int32_t* __restrict__ fill, uint64_t* __restrict__ keys) {
@@ -174,27 +178,46 @@ k_emit_keys(int n, const uint2* __restrict__ rects, const float* __restrict__ de
     }
     const int total = __shfl_sync(full, incl, 31);
     const int excl = incl - area;
-    for (int base = 0; base < total; base += 32) {
-        const int j = base + lane;
-        // owner: the last lane whose exclusive offset is <= j
-        int lo = 0;
+    // kPairsPerLane pairs per lane and round: their slot atomics are issued
+    // back to back, so each lane keeps several round trips in flight
+    constexpr int kPairsPerLane = 4;
+    for (int base = 0; base < total; base += 32 * kPairsPerLane) {
+        int tile[kPairsPerLane];
+        unsigned long long okey[kPairsPerLane];
 #pragma unroll
-        for (int step = 16; step > 0; step >>= 1) {
-            const int e = __shfl_sync(full, excl, lo + step);
-            if (lo + step < 32 && e <= j) lo += step;
+        for (int q = 0; q < kPairsPerLane; ++q) {
+            const int j = base + q * 32 + lane;
+            // owner: the last lane whose exclusive offset is <= j
+            int lo = 0;
+#pragma unroll
+            for (int step = 16; step > 0; step >>= 1) {
+                const int e = __shfl_sync(full, excl, lo + step);
+                if (lo + step < 32 && e <= j) lo += step;
+            }
+            const int o_excl = __shfl_sync(full, excl, lo);
+            const int o_x0 = __shfl_sync(full, x0, lo);
+            const int o_y0 = __shfl_sync(full, y0, lo);
+            const int o_w = __shfl_sync(full, w, lo);
+            okey[q] = __shfl_sync(full, (unsigned long long)key, lo);
+            tile[q] = -1;
+            if (j < total) {
+                const int local = j - o_excl;
+                const int ry = local / o_w;
+                tile[q] = (o_y0 + ry) * tx + o_x0 + (local - ry * o_w);
+            }
         }
-        const int o_excl = __shfl_sync(full, excl, lo);
-        const int o_x0 = __shfl_sync(full, x0, lo);
-        const int o_y0 = __shfl_sync(full, y0, lo);
-        const int o_w = __shfl_sync(full, w, lo);
-        const unsigned long long o_key = __shfl_sync(full, (unsigned long long)key, lo);
-        if (j < total) {
-            const int local = j - o_excl;
-            const int ry = local / o_w;
-            const int t = (o_y0 + ry) * tx + o_x0 + (local - ry * o_w);
-            const int slot = atomicAdd(&fill[t], 1);
-            keys[__ldg(raw_start + t) + slot] = o_key;
+        int slot[kPairsPerLane];
+        int64_t start[kPairsPerLane];
+#pragma unroll
+        for (int q = 0; q < kPairsPerLane; ++q) {
+            if (tile[q] >= 0) {
+                slot[q] = atomicAdd(&fill[tile[q]], 1);
+                start[q] = __ldg(raw_start + tile[q]);
+            }
         }
+#pragma unroll
+        for (int q = 0; q < kPairsPerLane; ++q)
+            if (tile[q] >= 0) keys[start[q] + slot[q]] = okey[q];
     }
 }
 
@@ -411,10 +434,12 @@ k_tile_sort(const int32_t* __restrict__ raw_counts, const int64_t* __restrict__ 
     __syncthreads();
     const int got = s_count;
     if (threadIdx.x == 0 && got != kMaxTileElems && err) atomicOr(err, kErrCapacity);
+    // the selected keys sit in data[] in arbitrary order: any assignment to
+    // threads will do, so read them bank-conflict free
     uint64_t v[8];
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
-        const int e = threadIdx.x * 8 + r;
+        const int e = r * kSortThreads + threadIdx.x;
         v[r] = e < got && e < kMaxTileElems ? data[e] : ~0ull;
     }
     bitonic_blocked<8, kSortThreads>(v, threadIdx.x, data);
