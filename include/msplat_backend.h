@@ -151,6 +151,19 @@ int msplat_shard_forward_backward(const MsplatGaussians* g, const MsplatCamera* 
                                   const float background[3], const float* gt, float lambda_l1, float lambda_dist,
                                   float lambda_dssim, int32_t world, int32_t rank, int32_t* tile_rows,
                                   float* raster_grads_out, double* loss_parts_dev, void* stream);
+/* msplat_shard_forward_backward with the projection split around binning:
+ * with split_color != 0 the geometry (homography, tile rectangles, depth,
+ * opacity) is projected first and the SH colour only after the tile lists
+ * are sorted, after `stream` has waited for features_ready (a cudaEvent_t,
+ * may be NULL). A caller can therefore still be gathering features_dc and
+ * features_rest from the other ranks when it makes this call; only means,
+ * scales, quats and opacities must be in place. Same results as
+ * msplat_shard_forward_backward. */
+int msplat_shard_forward_backward_after(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
+                                        const float background[3], const float* gt, float lambda_l1,
+                                        float lambda_dist, float lambda_dssim, int32_t world, int32_t rank,
+                                        int32_t* tile_rows, float* raster_grads_out, double* loss_parts_dev,
+                                        void* features_ready, int32_t split_color, void* stream);
 int msplat_shard_project_backward_adam(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
                                        const float* raster_grads, int32_t g_begin, int32_t g_end,
                                        const MsplatAdamState* adam, float* xys_grad_norm, float* vis_counts,

@@ -122,13 +122,14 @@ std::vector<Workspace*> g_ws;
 // Stage timing: CUDA events recorded on the launch stream at stage
 // boundaries, read back only when msplat_stage_times() is called.
 enum Stage { kStProject = 0, kStCounts, kStEmit, kStSort, kStRasterFwd, kStLoss, kStRasterBwd, kStProjectBwd,
-             kStBetweenShardCalls, kNumStages };
+             kStBetweenShardCalls, kStColor, kNumStages };
 // between_shard_calls: from the end of msplat_shard_forward_backward to the
 // start of msplat_shard_project_backward_adam on the stream (the caller's
 // reduce-scatter and any wait for slower ranks)
 const char* kStageNames[kNumStages] = {"project_forward", "tile_counts", "emit_keys", "tile_sort",
                                        "rasterize_forward", "loss_ssim", "rasterize_backward",
-                                       "project_backward_adam", "between_shard_calls"};
+                                       "project_backward_adam", "between_shard_calls",
+                                       "project_color"};  // colour pass of a split projection, incl. its wait
 bool g_timing = false;
 double g_stage_ms[kNumStages] = {};
 int64_t g_stage_n[kNumStages] = {};
@@ -226,7 +227,7 @@ CameraDev make_cam(const MsplatCamera* c) {
 void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam, int degrees_to_use,
                    float glob_scale, float clip, const float bg[3], bool ref_outputs, int row0, int row1,
                    cudaStream_t s, int balance_world = 0, int balance_rank = 0, int* owned0 = nullptr,
-                   int* owned1 = nullptr) {
+                   int* owned1 = nullptr, bool split_color = false, cudaEvent_t features_ready = nullptr) {
     const int n = g->num_points;
     const int K = sh_rest_bases(g->sh_degree);
     const int tx = cam.tiles_x, ty = cam.tiles_y, T = tx * ty;
@@ -262,6 +263,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
 
     ProjFwdArgs pa{};
     pa.n = n;
+    pa.pass = split_color ? 1 : 0;
     pa.means = g->means; pa.scales = g->scales; pa.quats = g->quats; pa.opacities = g->opacities;
     pa.f_dc = g->features_dc; pa.f_rest = g->features_rest;
     pa.rest_bases = K; pa.degrees_to_use = degrees_to_use;
@@ -305,6 +307,15 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     mark(w, kStSort, s);
     launch_tile_sort(row0 * tx, (row1 - row0) * tx, w.raw_counts.as<int32_t>(), w.raw_start.as<int64_t>(), w.raw_keys.as<uint64_t>(),
                      w.tile_bins.as<int2>(), w.gaussian_ids.as<int32_t>(), w.err.as<uint32_t>(), s);
+    if (split_color) {
+        // colour after binning: the caller may still be gathering features_dc /
+        // features_rest until features_ready
+        mark(w, kStColor, s);
+        if (features_ready) CK(cudaStreamWaitEvent(s, features_ready, 0));
+        ProjFwdArgs pc = pa;
+        pc.pass = 2;
+        launch_project_forward(pc, s);
+    }
     RasterFwdArgs ra{};
     ra.width = cam.width; ra.height = cam.height; ra.tiles_x = tx; ra.tiles_y = ty;
     ra.tile_row_begin = row0; ra.tile_row_end = row1;
@@ -547,6 +558,16 @@ int msplat_shard_forward_backward(const MsplatGaussians* g, const MsplatCamera* 
                                   const float background[3], const float* gt, float lambda_l1, float lambda_dist,
                                   float lambda_dssim, int32_t world, int32_t rank, int32_t* tile_rows,
                                   float* raster_grads_out, double* loss_parts_dev, void* stream) {
+    return msplat_shard_forward_backward_after(g, cam, degrees_to_use, background, gt, lambda_l1, lambda_dist,
+                                               lambda_dssim, world, rank, tile_rows, raster_grads_out,
+                                               loss_parts_dev, nullptr, 0, stream);
+}
+
+int msplat_shard_forward_backward_after(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
+                                        const float background[3], const float* gt, float lambda_l1,
+                                        float lambda_dist, float lambda_dssim, int32_t world, int32_t rank,
+                                        int32_t* tile_rows, float* raster_grads_out, double* loss_parts_dev,
+                                        void* features_ready, int32_t split_color, void* stream) {
     return guarded([&] {
         check_inputs(g, cam, degrees_to_use);
         if (!background || !gt || !raster_grads_out || !tile_rows) throw Error(MSPLAT_ERR_ARGUMENT, "null pointer");
@@ -561,7 +582,8 @@ int msplat_shard_forward_backward(const MsplatGaussians* g, const MsplatCamera* 
         }
         const int n = g->num_points;
         const int r0 = std::max(0, o0 - 1), r1 = std::min(cd.tiles_y, o1 + 1);
-        stage_forward(w, g, cd, degrees_to_use, 1.0f, 0.01f, background, false, r0, r1, s, world, rank, &o0, &o1);
+        stage_forward(w, g, cd, degrees_to_use, 1.0f, 0.01f, background, false, r0, r1, s, world, rank, &o0, &o1,
+                      split_color != 0, static_cast<cudaEvent_t>(features_ready));
         tile_rows[0] = o0;
         tile_rows[1] = o1;
         const int p0 = std::min(cd.height, o0 * kTile), p1 = std::min(cd.height, o1 * kTile);

@@ -29,6 +29,9 @@ struct CameraDev {
 // ---- projection (project.cu) ------------------------------------------------
 struct ProjFwdArgs {
     int n;
+    // 0: geometry and colour; 1: geometry only (record colour left unset);
+    // 2: colour only, for the Gaussians pass 1 kept (radii > 0)
+    int pass;
     const float* means; const float* scales; const float* quats; const float* opacities;
     const float* f_dc; const float* f_rest;
     int rest_bases;          // K = num_sh_bases(degree) - 1

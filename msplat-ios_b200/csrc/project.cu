@@ -21,6 +21,19 @@
 namespace msplat {
 namespace {
 
+// SH colour of Gaussian i for the camera position: raw colour (reference
+// output) and the clamped colour max(raw + 0.5, 0) the rasteriser blends.
+__device__ __forceinline__ void gaussian_color(const ProjFwdArgs& a, int i, V3 p, float col[3], float rgb[3]) {
+    const CameraDev& cam = a.cam;
+    V3 v = v3(p.x - cam.cam_pos[0], p.y - cam.cam_pos[1], p.z - cam.cam_pos[2]);
+    float inv = 1.0f / sqrtf(dot3(v, v));
+    V3 dir = scale3(v, inv);
+    const int K = a.rest_bases;
+    const float* rest = a.f_rest + (size_t)K * 3 * i;
+    sh_to_color(a.degrees_to_use, dir, a.f_dc + 3 * i, [&](int k) { return __ldg(rest + k); }, col);
+    for (int c = 0; c < 3; ++c) rgb[c] = smax(col[c] + 0.5f, 0.0f);
+}
+
 __global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= a.n) return;
@@ -28,6 +41,16 @@ __global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
     const float* vm = cam.viewmat;
     const float* pm = cam.projmat;
     float4* rec = a.records + (size_t)i * kRecordF4;
+    if (a.pass == 2) {
+        if (a.radii[i] <= 0) return;
+        float col[3], rgb[3];
+        gaussian_color(a, i, v3(a.means[3 * i], a.means[3 * i + 1], a.means[3 * i + 2]), col, rgb);
+        float* r3 = reinterpret_cast<float*>(rec + 3);
+        r3[0] = rgb[0]; r3[1] = rgb[1]; r3[2] = rgb[2];
+        if (a.colors)
+            for (int c = 0; c < 3; ++c) a.colors[3 * i + c] = col[c];
+        return;
+    }
     a.radii[i] = 0;
     a.rects[i] = make_uint2(0u, 0u);
     a.depths[i] = 0.f;
@@ -88,17 +111,10 @@ __global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
     atomicAdd(&a.tile_diff[y1 * dw + x0], -1);
     atomicAdd(&a.tile_diff[y1 * dw + x1], 1);
 
-    V3 v = v3(p.x - cam.cam_pos[0], p.y - cam.cam_pos[1], p.z - cam.cam_pos[2]);
-    float inv = 1.0f / sqrtf(dot3(v, v));
-    V3 dir = scale3(v, inv);
-    const int K = a.rest_bases;
-    const float* rest = a.f_rest + (size_t)K * 3 * i;
-    float col[3];
-    sh_to_color(a.degrees_to_use, dir, a.f_dc + 3 * i, [&](int k) { return __ldg(rest + k); }, col);
+    float col[3] = {0.f, 0.f, 0.f}, rgb[3] = {0.f, 0.f, 0.f};
+    if (a.pass == 0) gaussian_color(a, i, p, col, rgb);
     float opac_raw = a.opacities[i];
     float opac = 1.f / (1.f + det_exp(-opac_raw));
-    float rgb[3];
-    for (int c = 0; c < 3; ++c) rgb[c] = smax(col[c] + 0.5f, 0.0f);
     V3 nrm = R[2];
     rec[0] = make_float4(T0.x, T0.y, T0.z, T1.x);
     rec[1] = make_float4(T1.y, T1.z, T2.x, T2.y);
@@ -112,7 +128,8 @@ __global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
         for (int k = 0; k < 9; ++k) a.transmats[9 * i + k] = tm[k];
         a.normal_opacity[4 * i + 0] = nrm.x; a.normal_opacity[4 * i + 1] = nrm.y;
         a.normal_opacity[4 * i + 2] = nrm.z; a.normal_opacity[4 * i + 3] = opac_raw;
-        for (int c = 0; c < 3; ++c) a.colors[3 * i + c] = col[c];
+        if (a.pass == 0)
+            for (int c = 0; c < 3; ++c) a.colors[3 * i + c] = col[c];
         a.aabb[2 * i] = radius; a.aabb[2 * i + 1] = radius;
     }
 }

@@ -82,6 +82,9 @@ def load():
                                           f, C.POINTER(MsplatAdamState), vp, vp, vp, vp, i32, vp]
     L.msplat_shard_forward_backward.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, fp3, vp,
                                                 f, f, f, i32, i32, C.POINTER(C.c_int32), vp, vp, vp]
+    L.msplat_shard_forward_backward_after.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, fp3,
+                                                      vp, f, f, f, i32, i32, C.POINTER(C.c_int32), vp, vp, vp, i32,
+                                                      vp]
     L.msplat_shard_project_backward_adam.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, vp,
                                                      i32, i32, C.POINTER(MsplatAdamState), vp, vp, vp, vp]
     L.msplat_last_tensor.argtypes = [C.c_char_p, C.POINTER(MsplatTensorRef)]
@@ -104,7 +107,8 @@ def load():
     L.msplat_stage_name.restype = C.c_char_p
     L.msplat_last_error.restype = C.c_char_p
     for name in ("msplat_render", "msplat_train_step_2dgs", "msplat_fused_adam", "msplat_train_step_fused",
-                 "msplat_shard_forward_backward", "msplat_shard_project_backward_adam", "msplat_last_tensor",
+                 "msplat_shard_forward_backward", "msplat_shard_forward_backward_after",
+                 "msplat_shard_project_backward_adam", "msplat_last_tensor",
                  "msplat_densify_plan", "msplat_densify_apply", "msplat_reset_opacity"):
         getattr(L, name).restype = C.c_int
     _lib = L
@@ -239,14 +243,19 @@ def train_step_fused(g: DeviceGaussians, cam: MsplatCamera, degrees_to_use: int,
 
 
 def shard_forward_backward(g, cam, degrees_to_use, background, gt, lambda_l1, lambda_dist, lambda_dssim, raster_grads,
-                           loss_parts, world=0, rank=0, rows=(0, 0), stream=None):
+                           loss_parts, world=0, rank=0, rows=(0, 0), stream=None, features_ready=None,
+                           split_color=False):
     """Part 1 of the sharded step. With world > 0 the library picks a
-    work-balanced band for `rank`; returns the (begin, end) tile rows used."""
+    work-balanced band for `rank`; returns the (begin, end) tile rows used.
+    With split_color the SH colour is projected after binning, once the
+    stream has waited for features_ready (a torch.cuda.Event, may be None)."""
     gs = g.struct()
     tr = (C.c_int32 * 2)(int(rows[0]), int(rows[1]))
-    _check(load().msplat_shard_forward_backward(C.byref(gs), C.byref(cam), degrees_to_use, _bg(background), _ptr(gt),
-                                                lambda_l1, lambda_dist, lambda_dssim, world, rank, tr,
-                                                _ptr(raster_grads), _ptr(loss_parts), _stream(stream)))
+    ev = None if features_ready is None else C.c_void_p(features_ready.cuda_event)
+    _check(load().msplat_shard_forward_backward_after(C.byref(gs), C.byref(cam), degrees_to_use, _bg(background),
+                                                      _ptr(gt), lambda_l1, lambda_dist, lambda_dssim, world, rank,
+                                                      tr, _ptr(raster_grads), _ptr(loss_parts), ev,
+                                                      1 if split_color else 0, _stream(stream)))
     return tr[0], tr[1]
 
 

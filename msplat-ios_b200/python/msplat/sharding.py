@@ -68,7 +68,11 @@ def pad_gaussians(g, padded: int):
     return g
 
 
-def sharded_step(dist, plan: ShardPlan, forward_backward, project_adam, rg, rg_shard, param_fulls, parts):
+COLOR_GROUPS = (3, 4)  # features_dc, features_rest in Model group order
+
+
+def sharded_step(dist, plan: ShardPlan, forward_backward, project_adam, rg, rg_shard, param_fulls, parts,
+                 side_stream=None):
     """One training step across ranks.
 
     forward_backward(plan, rg, parts): fills rg [padded, 16] with this rank's
@@ -78,16 +82,38 @@ def sharded_step(dist, plan: ShardPlan, forward_backward, project_adam, rg, rg_s
         rg_shard [chunk, 16] holding the summed records of Gaussians
         g_begin .. g_end - 1 in its first rows.
     param_fulls: the [padded, ...] parameter buffers to all-gather in place.
+    side_stream: with a CUDA stream, the colour groups (features_dc,
+        features_rest: 48 of the 58 floats per Gaussian) are gathered on it
+        after everything else, and the returned event marks their arrival;
+        the next step's forward_backward binds the geometry while the
+        transfer runs and waits for the event only before its colour pass.
+        Every rank issues the collectives in the same order.
     """
     forward_backward(plan, rg, parts)
     dist.reduce_scatter_tensor(rg_shard, rg, op=dist.ReduceOp.SUM)
     project_adam(plan.g_begin, plan.g_end, rg_shard)
     rows = plan.slice_rows()
-    for full in param_fulls:
+    late = []
+    for k, full in enumerate(param_fulls):
         if full.numel() == 0:
+            continue
+        if side_stream is not None and k in COLOR_GROUPS:
+            late.append(full)
             continue
         dist.all_gather_into_tensor(full, full[rows])
     dist.all_reduce(parts)
+    if not late:
+        return None
+    import torch
+    adam_done = torch.cuda.Event()
+    adam_done.record()
+    side_stream.wait_event(adam_done)
+    ready = torch.cuda.Event()
+    with torch.cuda.stream(side_stream):
+        for full in late:
+            dist.all_gather_into_tensor(full, full[rows])
+        ready.record(side_stream)
+    return ready
 
 
 def loss_from_parts(parts, lambda_dssim: float, width: int, height: int) -> float:
@@ -97,16 +123,21 @@ def loss_from_parts(parts, lambda_dssim: float, width: int, height: int) -> floa
     return l1 + dist_term + lambda_dssim * (1.0 - ssim * inv_num)
 
 
-def gpu_step_fns(B, g, cam, degree, bg, gt, lambda_l1, lambda_dist, lambda_dssim, adam, stats, balance=True):
+def gpu_step_fns(B, g, cam, degree, bg, gt, lambda_l1, lambda_dist, lambda_dssim, adam, stats, balance=True,
+                 features_ready=None, split_color=False):
     """The two callables of sharded_step bound to the C ABI (msplat_shard_*).
-    With balance the library picks work-balanced tile-row bands each step."""
+    With balance the library picks work-balanced tile-row bands each step;
+    with split_color the colour pass waits for features_ready (the event the
+    previous sharded_step returned)."""
     def forward_backward(plan, rg, parts):
+        kw = dict(features_ready=features_ready, split_color=split_color)
         if balance:
             plan.row0, plan.row1 = B.shard_forward_backward(g, cam, degree, bg, gt, lambda_l1, lambda_dist,
-                                                            lambda_dssim, rg, parts, world=plan.world, rank=plan.rank)
+                                                            lambda_dssim, rg, parts, world=plan.world, rank=plan.rank,
+                                                            **kw)
         else:
             B.shard_forward_backward(g, cam, degree, bg, gt, lambda_l1, lambda_dist, lambda_dssim, rg, parts,
-                                     rows=(plan.row0, plan.row1))
+                                     rows=(plan.row0, plan.row1), **kw)
 
     def project_adam(g0, g1, rg_shard):
         # the kernel indexes records by global Gaussian id: offset the base

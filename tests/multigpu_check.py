@@ -1,6 +1,7 @@
 """Launched by tests/test_multigpu.py under torchrun (one process per GPU).
 
-Each rank runs two sharded training steps (msplat/sharding.py over NCCL) on a
+Each rank runs two sharded training steps (msplat/sharding.py over NCCL, with
+the colour groups gathered on a side stream while the next step bins) on a
 small scene; rank 0 also runs the same two steps with the single-GPU fused
 step on a private copy and compares the parameters. Prints "MULTIGPU OK" on
 success (rank 0) and exits non-zero otherwise.
@@ -40,10 +41,15 @@ def main():
     rg = torch.zeros(plan.padded, 16, device=dev)
     rg_shard = torch.zeros(plan.chunk, 16, device=dev)
     parts = torch.zeros(3, dtype=torch.float64, device=dev)
+    # the overlapped schedule the benchmark runs: colour groups gathered on a
+    # side stream while the next step bins its geometry
+    side = torch.cuda.Stream(device=dev)
+    ready = None
     for _ in range(2):
         adam.step += 1
-        fb, pa = sharding.gpu_step_fns(B, g, cam, case.degree, case.bg, gt, 0.8, 0.0, 0.2, adam, None)
-        sharding.sharded_step(dist, plan, fb, pa, rg, rg_shard, g.full, parts)
+        fb, pa = sharding.gpu_step_fns(B, g, cam, case.degree, case.bg, gt, 0.8, 0.0, 0.2, adam, None,
+                                       features_ready=ready, split_color=True)
+        ready = sharding.sharded_step(dist, plan, fb, pa, rg, rg_shard, g.full, parts, side_stream=side)
     torch.cuda.synchronize()
     loss_sh = sharding.loss_from_parts(parts.cpu().numpy(), 0.2, cfg.width, cfg.height)
     got = [t.cpu().numpy() for t in g.groups()]
