@@ -53,6 +53,10 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="nccl", choices=["peers", "nccl"],
+                    help="multi-GPU parameter exchange: NCCL all-gathers with the colour groups overlapped with "
+                         "binning (default), or geometry all-gathered and colour read from its owner over NVLink "
+                         "(CUDA IPC)")
     ap.add_argument("--render-frames", type=int, default=20,
                     help="render-only frames timed after the training steps (single GPU); 0 = skip")
     ap.add_argument("--cameras", type=int, default=0,
@@ -191,7 +195,19 @@ def run_ours(args, ws, rank, local):
     else:
         from msplat import sharding
         plan = sharding.ShardPlan(n, (cfg.height + 15) // 16, ws, rank)
-        sharding.pad_gaussians(g, plan.padded)
+        peers = None
+        exchange = "NCCL all-gather (colour groups overlapped with binning)"
+        if args.exchange == "peers":
+            peers = sharding.PeerParams(B, dist, plan, g)
+            if peers.ok:
+                exchange = ("geometry all-gathered; colour read from its owner over NVLink (CUDA IPC) for the "
+                            "rank's band only")
+            else:
+                exchange += "; peer mapping failed: " + peers.error[:120]
+            adam = B.AdamState(g)
+        else:
+            sharding.pad_gaussians(g, plan.padded)
+        use_peers = peers is not None and peers.ok
         rg = torch.zeros(plan.padded, 16, device=dev)
         rg_shard = torch.zeros(plan.chunk, 16, device=dev)
         parts = torch.zeros(3, dtype=torch.float64, device=dev)
@@ -202,8 +218,10 @@ def run_ours(args, ws, rank, local):
         def step(k):
             adam.step += 1
             fb, pa = sharding.gpu_step_fns(B, g, cams[k % C], cfg.degree, bg, gts[k % C], l1, ld, SSIM_WEIGHT,
-                                           adam, stats, features_ready=pending[0], split_color=True)
-            pending[0] = sharding.sharded_step(dist, plan, fb, pa, rg, rg_shard, g.full, parts, side_stream=side)
+                                           adam, stats, features_ready=pending[0], split_color=not use_peers,
+                                           peers=peers if use_peers else None)
+            pending[0] = sharding.sharded_step(dist, plan, fb, pa, rg, rg_shard, g.full, parts,
+                                               side_stream=None if use_peers else side, skip_color=use_peers)
 
     for k in range(args.warmup):
         step(k)
@@ -357,8 +375,10 @@ def run_ours(args, ws, rank, local):
             stream.wait_event(ready[b])
             adam.step += 1
             fb, pa = sharding.gpu_step_fns(B, g, cams[k % C], cfg.degree, bg, dev_gt[b], l1, ld, SSIM_WEIGHT, adam,
-                                           stats, features_ready=pending[0], split_color=True)
-            pending[0] = sharding.sharded_step(dist, plan, fb, pa, rg, rg_shard, g.full, parts, side_stream=side)
+                                           stats, features_ready=pending[0], split_color=not use_peers,
+                                           peers=peers if use_peers else None)
+            pending[0] = sharding.sharded_step(dist, plan, fb, pa, rg, rg_shard, g.full, parts,
+                                               side_stream=None if use_peers else side, skip_color=use_peers)
             free[b].record(stream)
             if k + 1 < e2e_steps:
                 prefetch(k + 1)
@@ -397,6 +417,7 @@ def run_ours(args, ws, rank, local):
                                        f"{cfg.width}x{cfg.height}, {C} ring cameras",
                            "gaussians": cfg.n, "image": [cfg.width, cfg.height], "sh_degree": cfg.degree,
                            "parallelism": f"tile-row sharding x{ws}" if ws > 1 else "single GPU",
+                           "exchange": exchange if ws > 1 else None,
                            "l2": "inputs larger than L2 (params+Adam state %.1f GB)" % (n * 58 * 12 / 1e9)},
                 "mpix_per_s": round(pixels * value / 1e6, 2),
                 "e2e": e2e, "render": render, "gpu_launches": int(launches), "clocks": clk, "roofline": roof,
@@ -406,6 +427,9 @@ def run_ours(args, ws, rank, local):
             line["ranks"] = ranks
         print(json.dumps(line), flush=True)
     if ws > 1:
+        torch.cuda.synchronize()
+        if peers is not None:
+            peers.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -164,6 +164,45 @@ int msplat_shard_forward_backward_after(const MsplatGaussians* g, const MsplatCa
                                         float lambda_dist, float lambda_dssim, int32_t world, int32_t rank,
                                         int32_t* tile_rows, float* raster_grads_out, double* loss_parts_dev,
                                         void* features_ready, int32_t split_color, void* stream);
+/* Peer colour access (one process per GPU on one node). Each rank keeps the
+ * six parameter groups as [padded, w] device buffers indexed by the global
+ * Gaussian id and owns rows [rank * chunk, (rank + 1) * chunk), which only it
+ * updates (msplat_shard_project_backward_adam). The caller all-gathers the
+ * geometry groups (means, scales, quats, opacities: 10 floats per Gaussian),
+ * which every rank's projection needs for every Gaussian; the colour groups
+ * (features_dc, features_rest: 48 floats) are not gathered: every rank maps
+ * the other ranks' buffers (CUDA IPC) and, after binning, reads the colour
+ * of just the Gaussians whose tile rectangle meets its band from their owner
+ * over NVLink (plain loads, no multicast). Ordering across ranks comes from
+ * the collectives of the step: the owners' Adam updates are complete before
+ * any collective the caller issues after them (the geometry all-gather, the
+ * loss all-reduce), and no owner updates again before every rank has joined
+ * the next reduce-scatter. base[0..2] and base[5] are not read. */
+#define MSPLAT_MAX_PEER_RANKS 16
+typedef struct MsplatPeerParams {
+    int32_t world;  /* ranks, 2..MSPLAT_MAX_PEER_RANKS */
+    int32_t chunk;  /* Gaussians owned per rank */
+    const float* base[6][MSPLAT_MAX_PEER_RANKS]; /* [group][rank]: that rank's buffer, mapped here (Model group order) */
+} MsplatPeerParams;
+
+/* Device buffers that can be shared with other processes: cudaMalloc'd and
+ * zeroed (msplat_device_alloc), their IPC handle (64 bytes), a peer buffer
+ * opened from a handle, and the matching release calls. */
+int msplat_device_alloc(uint64_t bytes, void** ptr);
+int msplat_device_free(void* ptr);
+int msplat_ipc_handle(void* ptr, uint8_t handle[64]);
+int msplat_ipc_open(const uint8_t handle[64], void** ptr);
+int msplat_ipc_close(void* ptr);
+
+/* msplat_shard_forward_backward with the colour coefficients read through
+ * `peers` (Gaussian i from rank i / peers->chunk) and the geometry from g
+ * (this rank's gathered buffers). */
+int msplat_shard_forward_backward_peers(const MsplatGaussians* g, const MsplatPeerParams* peers,
+                                        const MsplatCamera* cam, int32_t degrees_to_use,
+                                        const float background[3], const float* gt, float lambda_l1,
+                                        float lambda_dist, float lambda_dssim, int32_t world, int32_t rank,
+                                        int32_t* tile_rows, float* raster_grads_out, double* loss_parts_dev,
+                                        void* stream);
 int msplat_shard_project_backward_adam(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
                                        const float* raster_grads, int32_t g_begin, int32_t g_end,
                                        const MsplatAdamState* adam, float* xys_grad_norm, float* vis_counts,

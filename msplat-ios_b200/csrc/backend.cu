@@ -227,7 +227,8 @@ CameraDev make_cam(const MsplatCamera* c) {
 void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam, int degrees_to_use,
                    float glob_scale, float clip, const float bg[3], bool ref_outputs, int row0, int row1,
                    cudaStream_t s, int balance_world = 0, int balance_rank = 0, int* owned0 = nullptr,
-                   int* owned1 = nullptr, bool split_color = false, cudaEvent_t features_ready = nullptr) {
+                   int* owned1 = nullptr, bool split_color = false, cudaEvent_t features_ready = nullptr,
+                   const MsplatPeerParams* peers = nullptr) {
     const int n = g->num_points;
     const int K = sh_rest_bases(g->sh_degree);
     const int tx = cam.tiles_x, ty = cam.tiles_y, T = tx * ty;
@@ -264,6 +265,11 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     ProjFwdArgs pa{};
     pa.n = n;
     pa.pass = split_color ? 1 : 0;
+    if (peers) {
+        // colour from the owners' buffers, after binning, for this band only
+        split_color = true;
+        pa.pass = 1;
+    }
     pa.means = g->means; pa.scales = g->scales; pa.quats = g->quats; pa.opacities = g->opacities;
     pa.f_dc = g->features_dc; pa.f_rest = g->features_rest;
     pa.rest_bases = K; pa.degrees_to_use = degrees_to_use;
@@ -314,6 +320,16 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
         if (features_ready) CK(cudaStreamWaitEvent(s, features_ready, 0));
         ProjFwdArgs pc = pa;
         pc.pass = 2;
+        pc.color_row0 = row0;
+        pc.color_row1 = row1;
+        if (peers) {
+            pc.peer_world = peers->world;
+            pc.peer_chunk = peers->chunk;
+            for (int q = 0; q < peers->world; ++q) {
+                pc.peer_dc[q] = peers->base[3][q];
+                pc.peer_rest[q] = peers->base[4][q];
+            }
+        }
         launch_project_forward(pc, s);
     }
     RasterFwdArgs ra{};
@@ -421,6 +437,12 @@ int guarded(F&& f) {
         return MSPLAT_ERR_CUDA;
     }
 }
+
+int shard_forward_backward_impl(const MsplatGaussians* g, const MsplatPeerParams* peers, const MsplatCamera* cam,
+                                int32_t degrees_to_use, const float background[3], const float* gt, float lambda_l1,
+                                float lambda_dist, float lambda_dssim, int32_t world, int32_t rank,
+                                int32_t* tile_rows, float* raster_grads_out, double* loss_parts_dev,
+                                void* features_ready, int32_t split_color, void* stream);
 
 }  // namespace
 }  // namespace msplat
@@ -563,12 +585,46 @@ int msplat_shard_forward_backward(const MsplatGaussians* g, const MsplatCamera* 
                                                loss_parts_dev, nullptr, 0, stream);
 }
 
+int msplat_shard_forward_backward_peers(const MsplatGaussians* g, const MsplatPeerParams* peers,
+                                        const MsplatCamera* cam, int32_t degrees_to_use,
+                                        const float background[3], const float* gt, float lambda_l1,
+                                        float lambda_dist, float lambda_dssim, int32_t world, int32_t rank,
+                                        int32_t* tile_rows, float* raster_grads_out, double* loss_parts_dev,
+                                        void* stream) {
+    return shard_forward_backward_impl(g, peers, cam, degrees_to_use, background, gt, lambda_l1, lambda_dist,
+                                       lambda_dssim, world, rank, tile_rows, raster_grads_out, loss_parts_dev,
+                                       nullptr, 0, stream);
+}
+
 int msplat_shard_forward_backward_after(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
                                         const float background[3], const float* gt, float lambda_l1,
                                         float lambda_dist, float lambda_dssim, int32_t world, int32_t rank,
                                         int32_t* tile_rows, float* raster_grads_out, double* loss_parts_dev,
                                         void* features_ready, int32_t split_color, void* stream) {
+    return shard_forward_backward_impl(g, nullptr, cam, degrees_to_use, background, gt, lambda_l1, lambda_dist,
+                                       lambda_dssim, world, rank, tile_rows, raster_grads_out, loss_parts_dev,
+                                       features_ready, split_color, stream);
+}
+
+}  // extern "C"
+
+namespace msplat {
+namespace {
+int shard_forward_backward_impl(const MsplatGaussians* g, const MsplatPeerParams* peers, const MsplatCamera* cam,
+                                int32_t degrees_to_use, const float background[3], const float* gt, float lambda_l1,
+                                float lambda_dist, float lambda_dssim, int32_t world, int32_t rank,
+                                int32_t* tile_rows, float* raster_grads_out, double* loss_parts_dev,
+                                void* features_ready, int32_t split_color, void* stream) {
     return guarded([&] {
+        if (peers) {
+            if (peers->world < 2 || peers->world > MSPLAT_MAX_PEER_RANKS || peers->chunk <= 0 ||
+                (int64_t)peers->world * peers->chunk < g->num_points)
+                throw Error(MSPLAT_ERR_ARGUMENT, "bad peer parameter view");
+            for (int gi = 0; gi < 6; ++gi)
+                for (int q = 0; q < peers->world; ++q)
+                    if (!peers->base[gi][q] && !(gi == 4 && g->sh_degree == 0))
+                        throw Error(MSPLAT_ERR_ARGUMENT, "null peer buffer");
+        }
         check_inputs(g, cam, degrees_to_use);
         if (!background || !gt || !raster_grads_out || !tile_rows) throw Error(MSPLAT_ERR_ARGUMENT, "null pointer");
         cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -583,7 +639,7 @@ int msplat_shard_forward_backward_after(const MsplatGaussians* g, const MsplatCa
         const int n = g->num_points;
         const int r0 = std::max(0, o0 - 1), r1 = std::min(cd.tiles_y, o1 + 1);
         stage_forward(w, g, cd, degrees_to_use, 1.0f, 0.01f, background, false, r0, r1, s, world, rank, &o0, &o1,
-                      split_color != 0, static_cast<cudaEvent_t>(features_ready));
+                      split_color != 0, static_cast<cudaEvent_t>(features_ready), peers);
         tile_rows[0] = o0;
         tile_rows[1] = o1;
         const int p0 = std::min(cd.height, o0 * kTile), p1 = std::min(cd.height, o1 * kTile);
@@ -609,6 +665,55 @@ int msplat_shard_forward_backward_after(const MsplatGaussians* g, const MsplatCa
         }
         mark(w, kStBetweenShardCalls, s);
         CK(cudaGetLastError());
+    });
+}
+}  // namespace
+}  // namespace msplat
+
+extern "C" {
+
+int msplat_device_alloc(uint64_t bytes, void** ptr) {
+    return guarded([&] {
+        if (!ptr) throw Error(MSPLAT_ERR_ARGUMENT, "null pointer");
+        *ptr = nullptr;
+        void* p = nullptr;
+        CK(cudaMalloc(&p, bytes > 0 ? bytes : 1));
+        CK(cudaMemset(p, 0, bytes > 0 ? bytes : 1));
+        *ptr = p;
+    });
+}
+
+int msplat_device_free(void* ptr) {
+    return guarded([&] {
+        if (ptr) CK(cudaFree(ptr));
+    });
+}
+
+int msplat_ipc_handle(void* ptr, uint8_t handle[64]) {
+    return guarded([&] {
+        if (!ptr || !handle) throw Error(MSPLAT_ERR_ARGUMENT, "null pointer");
+        static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+        cudaIpcMemHandle_t h;
+        CK(cudaIpcGetMemHandle(&h, ptr));
+        std::memcpy(handle, &h, 64);
+    });
+}
+
+int msplat_ipc_open(const uint8_t handle[64], void** ptr) {
+    return guarded([&] {
+        if (!ptr || !handle) throw Error(MSPLAT_ERR_ARGUMENT, "null pointer");
+        *ptr = nullptr;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, handle, 64);
+        void* p = nullptr;
+        CK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+        *ptr = p;
+    });
+}
+
+int msplat_ipc_close(void* ptr) {
+    return guarded([&] {
+        if (ptr) CK(cudaIpcCloseMemHandle(ptr));
     });
 }
 

@@ -27,6 +27,8 @@ struct CameraDev {
 };
 
 // ---- projection (project.cu) ------------------------------------------------
+constexpr int kMaxPeerRanks = 16;
+
 struct ProjFwdArgs {
     int n;
     // 0: geometry and colour; 1: geometry only (record colour left unset);
@@ -47,6 +49,16 @@ struct ProjFwdArgs {
     // optional reference-shaped outputs (may be null)
     float* xys; float* transmats; int32_t* num_tiles_hit; float* normal_opacity;
     float* colors; float* aabb;
+    // multi-GPU: with peer_world > 1, Gaussian i's colour coefficients
+    // (features_dc, features_rest) are read from the buffer of its owner rank
+    // i / peer_chunk (a peer's memory mapped here); the geometry groups are
+    // local (all-gathered by the caller)
+    int peer_world, peer_chunk;
+    const float* peer_dc[kMaxPeerRanks];
+    const float* peer_rest[kMaxPeerRanks];
+    // pass 2: colour only for Gaussians whose tile rectangle meets tile rows
+    // [color_row0, color_row1) (color_row1 <= color_row0: all)
+    int color_row0, color_row1;
 };
 void launch_project_forward(const ProjFwdArgs& a, cudaStream_t s);
 

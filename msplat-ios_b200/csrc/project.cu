@@ -21,16 +21,30 @@
 namespace msplat {
 namespace {
 
+// Parameter pointers for Gaussian i: the local arrays, or with peers the
+// arrays of the owner rank (indexed by the global id either way).
+struct ParamPtrs {
+    const float *means, *scales, *quats, *f_dc, *f_rest, *opacities;
+};
+__device__ __forceinline__ ParamPtrs param_ptrs(const ProjFwdArgs& a, int i) {
+    if (a.peer_world > 1) {
+        const int q = i / a.peer_chunk;
+        return ParamPtrs{a.means, a.scales, a.quats, a.peer_dc[q], a.peer_rest[q], a.opacities};
+    }
+    return ParamPtrs{a.means, a.scales, a.quats, a.f_dc, a.f_rest, a.opacities};
+}
+
 // SH colour of Gaussian i for the camera position: raw colour (reference
 // output) and the clamped colour max(raw + 0.5, 0) the rasteriser blends.
-__device__ __forceinline__ void gaussian_color(const ProjFwdArgs& a, int i, V3 p, float col[3], float rgb[3]) {
+__device__ __forceinline__ void gaussian_color(const ProjFwdArgs& a, const ParamPtrs& pp, int i, V3 p, float col[3],
+                                               float rgb[3]) {
     const CameraDev& cam = a.cam;
     V3 v = v3(p.x - cam.cam_pos[0], p.y - cam.cam_pos[1], p.z - cam.cam_pos[2]);
     float inv = 1.0f / sqrtf(dot3(v, v));
     V3 dir = scale3(v, inv);
     const int K = a.rest_bases;
-    const float* rest = a.f_rest + (size_t)K * 3 * i;
-    sh_to_color(a.degrees_to_use, dir, a.f_dc + 3 * i, [&](int k) { return __ldg(rest + k); }, col);
+    const float* rest = pp.f_rest + (size_t)K * 3 * i;
+    sh_to_color(a.degrees_to_use, dir, pp.f_dc + 3 * i, [&](int k) { return __ldg(rest + k); }, col);
     for (int c = 0; c < 3; ++c) rgb[c] = smax(col[c] + 0.5f, 0.0f);
 }
 
@@ -41,10 +55,15 @@ __global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
     const float* vm = cam.viewmat;
     const float* pm = cam.projmat;
     float4* rec = a.records + (size_t)i * kRecordF4;
+    const ParamPtrs pp = param_ptrs(a, i);
     if (a.pass == 2) {
         if (a.radii[i] <= 0) return;
+        if (a.color_row1 > a.color_row0) {
+            const uint2 rc = a.rects[i];
+            if ((int)(rc.y >> 16) <= a.color_row0 || (int)(rc.x >> 16) >= a.color_row1) return;
+        }
         float col[3], rgb[3];
-        gaussian_color(a, i, v3(a.means[3 * i], a.means[3 * i + 1], a.means[3 * i + 2]), col, rgb);
+        gaussian_color(a, pp, i, v3(pp.means[3 * i], pp.means[3 * i + 1], pp.means[3 * i + 2]), col, rgb);
         float* r3 = reinterpret_cast<float*>(rec + 3);
         r3[0] = rgb[0]; r3[1] = rgb[1]; r3[2] = rgb[2];
         if (a.colors)
@@ -62,12 +81,12 @@ __global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
         for (int k = 0; k < 3; ++k) a.colors[3 * i + k] = 0.f;
         a.aabb[2 * i] = 0.f; a.aabb[2 * i + 1] = 0.f;
     }
-    V3 p = v3(a.means[3 * i], a.means[3 * i + 1], a.means[3 * i + 2]);
+    V3 p = v3(pp.means[3 * i], pp.means[3 * i + 1], pp.means[3 * i + 2]);
     float pvz = vm[8] * p.x + vm[9] * p.y + vm[10] * p.z + vm[11];
     if (pvz <= a.clip_thresh) return;
-    float sx = det_exp(a.scales[2 * i]) * a.glob_scale;
-    float sy = det_exp(a.scales[2 * i + 1]) * a.glob_scale;
-    float q[4] = {a.quats[4 * i], a.quats[4 * i + 1], a.quats[4 * i + 2], a.quats[4 * i + 3]};
+    float sx = det_exp(pp.scales[2 * i]) * a.glob_scale;
+    float sy = det_exp(pp.scales[2 * i + 1]) * a.glob_scale;
+    float q[4] = {pp.quats[4 * i], pp.quats[4 * i + 1], pp.quats[4 * i + 2], pp.quats[4 * i + 3]};
     V3 R[3];
     quat_to_rotmat(q, R);
     V3 tu = scale3(R[0], sx), tv = scale3(R[1], sy);
@@ -112,8 +131,8 @@ __global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
     atomicAdd(&a.tile_diff[y1 * dw + x1], 1);
 
     float col[3] = {0.f, 0.f, 0.f}, rgb[3] = {0.f, 0.f, 0.f};
-    if (a.pass == 0) gaussian_color(a, i, p, col, rgb);
-    float opac_raw = a.opacities[i];
+    if (a.pass == 0) gaussian_color(a, pp, i, p, col, rgb);
+    float opac_raw = pp.opacities[i];
     float opac = 1.f / (1.f + det_exp(-opac_raw));
     V3 nrm = R[2];
     rec[0] = make_float4(T0.x, T0.y, T0.z, T1.x);
@@ -134,12 +153,61 @@ __global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
     }
 }
 
+// Colour pass for ranks that read colour coefficients from their owners
+// (pass 2 with peers): each warp selects, among its 32 Gaussians, those kept
+// by the geometry pass whose tile rectangle meets the band, copies their
+// 3 + 3K coefficients from the owner rank with coalesced loads (all issued
+// before any is used) into shared memory, and each lane then evaluates its
+// own colour with the same SH code as k_project_forward.
+constexpr int kColorCoefs = 48;  // 3 DC + 45 rest for SH degree 3
+__global__ void __launch_bounds__(256) k_project_color_peers(ProjFwdArgs a) {
+    __shared__ float scoef[8][32][kColorCoefs];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int wbase = i - lane;
+    bool need = false;
+    if (i < a.n && a.radii[i] > 0) {
+        const uint2 rc = a.rects[i];
+        need = a.color_row1 <= a.color_row0 ||
+               ((int)(rc.y >> 16) > a.color_row0 && (int)(rc.x >> 16) < a.color_row1);
+    }
+    const unsigned sel = __ballot_sync(0xffffffffu, need);
+    if (sel == 0) return;
+    const int K3 = 3 * a.rest_bases;
+    const int ncoef = 3 + K3;
+    for (unsigned bits = sel; bits; bits &= bits - 1) {
+        const int j = __ffs(bits) - 1;
+        const int g = wbase + j;
+        const int q = g / a.peer_chunk;
+        const float* dc = a.peer_dc[q] + 3 * (size_t)g;
+        const float* rest = a.peer_rest[q] + (size_t)K3 * g;
+        for (int k = lane; k < ncoef; k += 32) scoef[warp][j][k] = k < 3 ? dc[k] : rest[k - 3];
+    }
+    __syncwarp();
+    if (!need) return;
+    const float* mine = scoef[warp][lane];
+    const CameraDev& cam = a.cam;
+    V3 p = v3(a.means[3 * i], a.means[3 * i + 1], a.means[3 * i + 2]);
+    V3 v = v3(p.x - cam.cam_pos[0], p.y - cam.cam_pos[1], p.z - cam.cam_pos[2]);
+    float inv = 1.0f / sqrtf(dot3(v, v));
+    V3 dir = scale3(v, inv);
+    float col[3];
+    sh_to_color(a.degrees_to_use, dir, mine, [&](int k) { return mine[3 + k]; }, col);
+    float* r3 = reinterpret_cast<float*>(a.records + (size_t)i * kRecordF4 + 3);
+    for (int c = 0; c < 3; ++c) r3[c] = smax(col[c] + 0.5f, 0.0f);
+    if (a.colors)
+        for (int c = 0; c < 3; ++c) a.colors[3 * i + c] = col[c];
+}
+
 }  // namespace
 
 void launch_project_forward(const ProjFwdArgs& a, cudaStream_t s) {
     if (a.n <= 0) return;
     note_launches(1);
-    k_project_forward<<<(a.n + 255) / 256, 256, 0, s>>>(a);
+    if (a.pass == 2 && a.peer_world > 1)
+        k_project_color_peers<<<(a.n + 255) / 256, 256, 0, s>>>(a);
+    else
+        k_project_forward<<<(a.n + 255) / 256, 256, 0, s>>>(a);
 }
 
 }  // namespace msplat

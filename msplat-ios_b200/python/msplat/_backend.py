@@ -53,6 +53,13 @@ class MsplatDensifyPlan(C.Structure):
     _fields_ = [("num_splits", C.c_int32), ("num_dups", C.c_int32), ("new_count", C.c_int32)]
 
 
+MAX_PEER_RANKS = 16
+
+
+class MsplatPeerParams(C.Structure):
+    _fields_ = [("world", C.c_int32), ("chunk", C.c_int32), ("base", (C.c_void_p * MAX_PEER_RANKS) * 6)]
+
+
 class MsplatTensorRef(C.Structure):
     _fields_ = [("data", C.c_void_p), ("shape", C.c_int64 * 4), ("ndim", C.c_int32), ("dtype", C.c_int32)]
 
@@ -85,6 +92,14 @@ def load():
     L.msplat_shard_forward_backward_after.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, fp3,
                                                       vp, f, f, f, i32, i32, C.POINTER(C.c_int32), vp, vp, vp, i32,
                                                       vp]
+    L.msplat_shard_forward_backward_peers.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatPeerParams),
+                                                      C.POINTER(MsplatCamera), i32, fp3, vp, f, f, f, i32, i32,
+                                                      C.POINTER(C.c_int32), vp, vp, vp]
+    L.msplat_device_alloc.argtypes = [C.c_uint64, C.POINTER(C.c_void_p)]
+    L.msplat_device_free.argtypes = [vp]
+    L.msplat_ipc_handle.argtypes = [vp, C.c_char * 64]
+    L.msplat_ipc_open.argtypes = [C.c_char * 64, C.POINTER(C.c_void_p)]
+    L.msplat_ipc_close.argtypes = [vp]
     L.msplat_shard_project_backward_adam.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, vp,
                                                      i32, i32, C.POINTER(MsplatAdamState), vp, vp, vp, vp]
     L.msplat_last_tensor.argtypes = [C.c_char_p, C.POINTER(MsplatTensorRef)]
@@ -108,6 +123,8 @@ def load():
     L.msplat_last_error.restype = C.c_char_p
     for name in ("msplat_render", "msplat_train_step_2dgs", "msplat_fused_adam", "msplat_train_step_fused",
                  "msplat_shard_forward_backward", "msplat_shard_forward_backward_after",
+                 "msplat_shard_forward_backward_peers", "msplat_device_alloc", "msplat_device_free",
+                 "msplat_ipc_handle", "msplat_ipc_open", "msplat_ipc_close",
                  "msplat_shard_project_backward_adam", "msplat_last_tensor",
                  "msplat_densify_plan", "msplat_densify_apply", "msplat_reset_opacity"):
         getattr(L, name).restype = C.c_int
@@ -366,3 +383,53 @@ def normal_samples(seed: int, count: int):
 def reset_opacity(opacities, exp_avg, exp_avg_sq, max_logit: float, stream=None):
     _check(load().msplat_reset_opacity(_ptr(opacities), _ptr(exp_avg), _ptr(exp_avg_sq), opacities.numel(),
                                        max_logit, _stream(stream)))
+
+
+def shard_forward_backward_peers(g, peers: MsplatPeerParams, cam, degrees_to_use, background, gt, lambda_l1,
+                                 lambda_dist, lambda_dssim, raster_grads, loss_parts, world=0, rank=0, rows=(0, 0),
+                                 stream=None):
+    """shard_forward_backward with the parameters read from their owner ranks
+    through the peer view (msplat_shard_forward_backward_peers)."""
+    gs = g.struct()
+    tr = (C.c_int32 * 2)(int(rows[0]), int(rows[1]))
+    _check(load().msplat_shard_forward_backward_peers(C.byref(gs), C.byref(peers), C.byref(cam), degrees_to_use,
+                                                      _bg(background), _ptr(gt), lambda_l1, lambda_dist,
+                                                      lambda_dssim, world, rank, tr, _ptr(raster_grads),
+                                                      _ptr(loss_parts), _stream(stream)))
+    return tr[0], tr[1]
+
+
+def device_alloc(nbytes: int) -> int:
+    p = C.c_void_p()
+    _check(load().msplat_device_alloc(nbytes, C.byref(p)))
+    return p.value
+
+
+def device_free(ptr: int):
+    _check(load().msplat_device_free(ptr))
+
+
+def ipc_handle(ptr: int) -> bytes:
+    h = (C.c_char * 64)()
+    _check(load().msplat_ipc_handle(ptr, h))
+    return bytes(h.raw)
+
+
+def ipc_open(handle: bytes) -> int:
+    h = (C.c_char * 64).from_buffer_copy(handle)
+    p = C.c_void_p()
+    _check(load().msplat_ipc_open(h, C.byref(p)))
+    return p.value
+
+
+def ipc_close(ptr: int):
+    _check(load().msplat_ipc_close(ptr))
+
+
+class DeviceArray:
+    """A raw float32 device allocation seen by torch (zero copy) through the
+    CUDA array interface; the owner frees the memory."""
+
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"shape": tuple(int(x) for x in shape), "typestr": "<f4",
+                                         "data": (int(ptr), False), "version": 3, "strides": None}

@@ -71,8 +71,84 @@ def pad_gaussians(g, padded: int):
 COLOR_GROUPS = (3, 4)  # features_dc, features_rest in Model group order
 
 
+class PeerParams:
+    """The parameter groups of a DeviceGaussians re-homed in [padded, ...]
+    buffers that every rank maps through CUDA IPC (msplat_ipc_*): rank q
+    owns and updates rows [q * chunk, (q + 1) * chunk) of its own buffers;
+    the geometry groups are still all-gathered (every rank projects every
+    Gaussian), but the colour groups are read from their owner after binning
+    for just the Gaussians of the rank's band, so they are never gathered. `struct` is the MsplatPeerParams view;
+    when any rank cannot map its peers, `ok` is False on every rank and the
+    buffers remain usable as the [padded, ...] buffers of the NCCL
+    all-gather exchange (g.full). close() must run on every rank (it
+    synchronises and barriers before unmapping and freeing)."""
+
+    def __init__(self, B, dist, plan: ShardPlan, g):
+        import torch
+        if plan.world > B.MAX_PEER_RANKS:
+            raise ValueError("too many ranks for the peer view")
+        self.B, self.dist = B, dist
+        self.own, self.mapped = [], []
+        n, dev = g.n, g.means.device
+        names = ("means", "scales", "quats", "f_dc", "f_rest", "opacities")
+        g.full = []
+        for name in names:
+            t = getattr(g, name)
+            shape = (plan.padded,) + tuple(t.shape[1:])
+            row = 1
+            for d in t.shape[1:]:
+                row *= int(d)
+            ptr = B.device_alloc(plan.padded * max(row, 1) * 4)
+            self.own.append(ptr)
+            full = torch.as_tensor(B.DeviceArray(ptr, shape), device=dev)
+            full[:n].copy_(t)
+            setattr(g, name, full[:n])
+            g.full.append(full)
+        torch.cuda.synchronize()
+        handles = [B.ipc_handle(p) for p in self.own]
+        everyone = [None] * plan.world
+        dist.all_gather_object(everyone, handles)
+        st = B.MsplatPeerParams()
+        st.world, st.chunk = plan.world, plan.chunk
+        self.error = ""
+        try:
+            for q in range(plan.world):
+                for k in range(6):
+                    if q == plan.rank:
+                        ptr = self.own[k]
+                    else:
+                        ptr = B.ipc_open(everyone[q][k])
+                        self.mapped.append(ptr)
+                    st.base[k][q] = ptr
+        except Exception as e:  # e.g. no peer access between these GPUs
+            self.error = str(e)
+        # every rank must agree before anyone reads a peer buffer
+        ok = torch.tensor([0 if self.error else 1], device=dev, dtype=torch.int32)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        self.ok = bool(ok.item())
+        if not self.ok:
+            for p in self.mapped:
+                B.ipc_close(p)
+            self.mapped = []
+            self.error = self.error or "a peer could not map this rank's buffers"
+        self.struct = st if self.ok else None
+        dist.barrier()
+
+    def close(self):
+        import torch
+        torch.cuda.synchronize()
+        self.dist.barrier()  # no rank reads a peer buffer any more
+        for p in self.mapped:
+            self.B.ipc_close(p)
+        self.mapped = []
+        self.dist.barrier()  # no rank maps this rank's buffers any more
+        for p in self.own:
+            self.B.device_free(p)
+        self.own = []
+
+
 def sharded_step(dist, plan: ShardPlan, forward_backward, project_adam, rg, rg_shard, param_fulls, parts,
-                 side_stream=None):
+                 side_stream=None, skip_color=False):
     """One training step across ranks.
 
     forward_backward(plan, rg, parts): fills rg [padded, 16] with this rank's
@@ -87,7 +163,11 @@ def sharded_step(dist, plan: ShardPlan, forward_backward, project_adam, rg, rg_s
         after everything else, and the returned event marks their arrival;
         the next step's forward_backward binds the geometry while the
         transfer runs and waits for the event only before its colour pass.
-        Every rank issues the collectives in the same order.
+    skip_color: the colour groups are not gathered at all (the ranks read
+        them from their owners, PeerParams); the geometry all-gather and the
+        loss all-reduce after Adam order every owner's update before the
+        next step's reads.
+    Every rank issues the collectives in the same order.
     """
     forward_backward(plan, rg, parts)
     dist.reduce_scatter_tensor(rg_shard, rg, op=dist.ReduceOp.SUM)
@@ -95,7 +175,7 @@ def sharded_step(dist, plan: ShardPlan, forward_backward, project_adam, rg, rg_s
     rows = plan.slice_rows()
     late = []
     for k, full in enumerate(param_fulls):
-        if full.numel() == 0:
+        if full.numel() == 0 or (skip_color and k in COLOR_GROUPS):
             continue
         if side_stream is not None and k in COLOR_GROUPS:
             late.append(full)
@@ -124,12 +204,18 @@ def loss_from_parts(parts, lambda_dssim: float, width: int, height: int) -> floa
 
 
 def gpu_step_fns(B, g, cam, degree, bg, gt, lambda_l1, lambda_dist, lambda_dssim, adam, stats, balance=True,
-                 features_ready=None, split_color=False):
+                 features_ready=None, split_color=False, peers=None):
     """The two callables of sharded_step bound to the C ABI (msplat_shard_*).
     With balance the library picks work-balanced tile-row bands each step;
     with split_color the colour pass waits for features_ready (the event the
-    previous sharded_step returned)."""
+    previous sharded_step returned); with peers (a PeerParams) the projection
+    reads every Gaussian from its owner rank."""
     def forward_backward(plan, rg, parts):
+        if peers is not None:
+            plan.row0, plan.row1 = B.shard_forward_backward_peers(g, peers.struct, cam, degree, bg, gt, lambda_l1,
+                                                                  lambda_dist, lambda_dssim, rg, parts,
+                                                                  world=plan.world, rank=plan.rank)
+            return
         kw = dict(features_ready=features_ready, split_color=split_color)
         if balance:
             plan.row0, plan.row1 = B.shard_forward_backward(g, cam, degree, bg, gt, lambda_l1, lambda_dist,

@@ -1,8 +1,10 @@
 """Launched by tests/test_multigpu.py under torchrun (one process per GPU).
 
-Each rank runs two sharded training steps (msplat/sharding.py over NCCL, with
-the colour groups gathered on a side stream while the next step bins) on a
-small scene; rank 0 also runs the same two steps with the single-GPU fused
+Each rank runs two sharded training steps (msplat/sharding.py) on a small
+scene, exchanging parameters either with NCCL all-gathers (colour groups on a
+side stream while the next step bins; MSPLAT_EXCHANGE=nccl) or with the
+geometry all-gathered and the colour read from its owner rank through CUDA
+IPC (MSPLAT_EXCHANGE=peers); rank 0 also runs the same two steps with the single-GPU fused
 step on a private copy and compares the parameters. Prints "MULTIGPU OK" on
 success (rank 0) and exits non-zero otherwise.
 """
@@ -37,22 +39,44 @@ def main():
     g = B.DeviceGaussians(*case.scene.params(), sh_degree=case.degree, device=dev)
     adam = B.AdamState(g)
     plan = sharding.ShardPlan(n, (cfg.height + 15) // 16, ws, rank)
-    sharding.pad_gaussians(g, plan.padded)
+    exchange = os.environ.get("MSPLAT_EXCHANGE", "nccl")
+    peers = None
+    if exchange == "peers":
+        # every rank reads each Gaussian from its owner's buffers (CUDA IPC)
+        peers = sharding.PeerParams(B, dist, plan, g)
+        adam = B.AdamState(g)
+    else:
+        sharding.pad_gaussians(g, plan.padded)
     rg = torch.zeros(plan.padded, 16, device=dev)
     rg_shard = torch.zeros(plan.chunk, 16, device=dev)
     parts = torch.zeros(3, dtype=torch.float64, device=dev)
-    # the overlapped schedule the benchmark runs: colour groups gathered on a
-    # side stream while the next step bins its geometry
+    # the overlapped schedule the benchmark runs with NCCL: colour groups
+    # gathered on a side stream while the next step bins its geometry
     side = torch.cuda.Stream(device=dev)
     ready = None
     for _ in range(2):
         adam.step += 1
         fb, pa = sharding.gpu_step_fns(B, g, cam, case.degree, case.bg, gt, 0.8, 0.0, 0.2, adam, None,
-                                       features_ready=ready, split_color=True)
-        ready = sharding.sharded_step(dist, plan, fb, pa, rg, rg_shard, g.full, parts, side_stream=side)
+                                       features_ready=ready, split_color=peers is None, peers=peers)
+        ready = sharding.sharded_step(dist, plan, fb, pa, rg, rg_shard, g.full, parts,
+                                      side_stream=None if peers else side, skip_color=peers is not None)
     torch.cuda.synchronize()
     loss_sh = sharding.loss_from_parts(parts.cpu().numpy(), 0.2, cfg.width, cfg.height)
-    got = [t.cpu().numpy() for t in g.groups()]
+    if peers is not None:
+        # each rank's colour buffers are current only in the rows it owns:
+        # gather them once to compare the whole parameter set
+        rows = plan.slice_rows()
+        gathered = []
+        for full in g.full:
+            out = torch.empty_like(full)
+            if full.numel():
+                dist.all_gather_into_tensor(out, full[rows].contiguous())
+            gathered.append(out[:n])
+        got = [t.cpu().numpy() for t in gathered]
+        torch.cuda.synchronize()
+        peers.close()
+    else:
+        got = [t.cpu().numpy() for t in g.groups()]
     ok = True
     if rank == 0:
         g1 = B.DeviceGaussians(*case.scene.params(), sh_degree=case.degree, device=dev)

@@ -14,11 +14,12 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def test_two_gpu_sharded_step_matches_single_gpu():
+@pytest.mark.parametrize("exchange", ["nccl", "peers"])
+def test_two_gpu_sharded_step_matches_single_gpu(exchange):
     torch = pytest.importorskip("torch")
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MSPLAT_EXCHANGE=exchange)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29555",
            os.path.join(HERE, "multigpu_check.py")]
