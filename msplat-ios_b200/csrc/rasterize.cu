@@ -415,14 +415,27 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
                         const float dsy = -dL_dG * G * e.v + dL_dz * r1.w;
                         const float dpx = dsx * e.inv_z, dpy = dsy * e.inv_z;
                         const float dpz = -(dpx * e.u + dpy * e.v);
-                        // dk = cross(l, dp), dl = cross(dp, k)
-                        const float dkx = e.ly * dpz - e.lz * dpy, dky = e.lz * dpx - e.lx * dpz, dkz = e.lx * dpy - e.ly * dpx;
-                        const float dlx = dpy * e.kz - dpz * e.ky, dly = dpz * e.kx - dpx * e.kz, dlz = dpx * e.ky - dpy * e.kx;
-                        g[0] = -dkx; g[1] = -dky; g[2] = -dkz;
-                        g[3] = -dlx; g[4] = -dly; g[5] = -dlz;
-                        g[6] = px * dkx + py * dlx + dL_dz * e.u;
-                        g[7] = px * dky + py * dly + dL_dz * e.v;
-                        g[8] = px * dkz + py * dlz + dL_dz;
+                        if constexpr (AUX) {
+                            // dk = cross(l, dp), dl = cross(dp, k)
+                            const float dkx = e.ly * dpz - e.lz * dpy, dky = e.lz * dpx - e.lx * dpz,
+                                        dkz = e.lx * dpy - e.ly * dpx;
+                            const float dlx = dpy * e.kz - dpz * e.ky, dly = dpz * e.kx - dpx * e.kz,
+                                        dlz = dpx * e.ky - dpy * e.kx;
+                            g[0] = -dkx; g[1] = -dky; g[2] = -dkz;
+                            g[3] = -dlx; g[4] = -dly; g[5] = -dlz;
+                            g[6] = px * dkx + py * dlx + dL_dz * e.u;
+                            g[7] = px * dky + py * dly + dL_dz * e.v;
+                            g[8] = px * dkz + py * dlz + dL_dz;
+                        } else {
+                            // k = px Tw - Tu and l = py Tw - Tv are affine in the
+                            // pixel, so the warp's sums of dk = l x dp, dl = dp x k
+                            // and px dk + py dl follow from the sums of dp, px dp and
+                            // py dp; the cross products are taken once per surfel
+                            // when the CTA flushes its accumulator
+                            g[0] = dpx; g[1] = dpy; g[2] = dpz;
+                            g[3] = px * dpx; g[4] = px * dpy; g[5] = px * dpz;
+                            g[6] = py * dpx; g[7] = py * dpy; g[8] = py * dpz;
+                        }
                     } else if (AUX) {
                         g[6] = e.u * dL_dz;
                         g[7] = e.v * dL_dz;
@@ -451,12 +464,45 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
             }
         }
         __syncthreads();
-        for (int q = threadIdx.x; q < total * 4; q += kThreads) {
-            const int s = q >> 2, part = q & 3;
-            const float4 v = make_float4(sacc[s][4 * part], sacc[s][4 * part + 1], sacc[s][4 * part + 2],
-                                         sacc[s][4 * part + 3]);
-            if (v.x != 0.f || v.y != 0.f || v.z != 0.f || v.w != 0.f)
-                atomicAdd(reinterpret_cast<float4*>(a.raster_grads + (size_t)sid[s] * kGradStride) + part, v);
+        if constexpr (AUX) {
+            for (int q = threadIdx.x; q < total * 4; q += kThreads) {
+                const int s = q >> 2, part = q & 3;
+                const float4 v = make_float4(sacc[s][4 * part], sacc[s][4 * part + 1], sacc[s][4 * part + 2],
+                                             sacc[s][4 * part + 3]);
+                if (v.x != 0.f || v.y != 0.f || v.z != 0.f || v.w != 0.f)
+                    atomicAdd(reinterpret_cast<float4*>(a.raster_grads + (size_t)sid[s] * kGradStride) + part, v);
+            }
+        } else {
+            for (int s = threadIdx.x; s < total; s += kThreads) {
+                const float* acc = sacc[s];
+                const float4 r0 = srec[0][s], r1 = srec[1][s], r2 = srec[2][s];
+                const float tux = r0.x, tuy = r0.y, tuz = r0.z, tvx = r0.w, tvy = r1.x, tvz = r1.y;
+                const float twx = r1.z, twy = r1.w, twz = r2.x;
+                const float sx = acc[0], sy = acc[1], sz = acc[2];   // sum dp
+                const float ax = acc[3], ay = acc[4], az = acc[5];   // sum px dp
+                const float bx = acc[6], by = acc[7], bz = acc[8];   // sum py dp
+                // sum dk = Tw x (sum py dp) - Tv x (sum dp)
+                const float dkx = (twy * bz - twz * by) - (tvy * sz - tvz * sy);
+                const float dky = (twz * bx - twx * bz) - (tvz * sx - tvx * sz);
+                const float dkz = (twx * by - twy * bx) - (tvx * sy - tvy * sx);
+                // sum dl = (sum px dp) x Tw - (sum dp) x Tu
+                const float dlx = (ay * twz - az * twy) - (sy * tuz - sz * tuy);
+                const float dly = (az * twx - ax * twz) - (sz * tux - sx * tuz);
+                const float dlz = (ax * twy - ay * twx) - (sx * tuy - sy * tux);
+                // sum (px dk + py dl) = Tu x (sum py dp) - Tv x (sum px dp)
+                const float ex = (tuy * bz - tuz * by) - (tvy * az - tvz * ay);
+                const float ey = (tuz * bx - tux * bz) - (tvz * ax - tvx * az);
+                const float ez = (tux * by - tuy * bx) - (tvx * ay - tvy * ax);
+                float4* dst = reinterpret_cast<float4*>(a.raster_grads + (size_t)sid[s] * kGradStride);
+                const float4 p0 = make_float4(-dkx, -dky, -dkz, -dlx);
+                const float4 p1 = make_float4(-dly, -dlz, ex, ey);
+                const float4 p2 = make_float4(ez, acc[9], acc[10], acc[11]);
+                const float4 p3 = make_float4(acc[12], 0.f, 0.f, 0.f);
+                if (p0.x != 0.f || p0.y != 0.f || p0.z != 0.f || p0.w != 0.f) atomicAdd(dst, p0);
+                if (p1.x != 0.f || p1.y != 0.f || p1.z != 0.f || p1.w != 0.f) atomicAdd(dst + 1, p1);
+                if (p2.x != 0.f || p2.y != 0.f || p2.z != 0.f || p2.w != 0.f) atomicAdd(dst + 2, p2);
+                if (p3.x != 0.f) atomicAdd(dst + 3, p3);
+            }
         }
     }
 }
