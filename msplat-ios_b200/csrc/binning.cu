@@ -67,17 +67,33 @@ k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int row0, int ro
         }
     }
     __syncthreads();
-    // Row prefix over x (one thread per tile row) and the work of each row.
-    for (int y = threadIdx.x; y < ty; y += blockDim.x) {
-        int run = 0;
-        int64_t work = 0;
-        int32_t* row = raw_counts + (size_t)y * tx;
-        for (int x = 0; x < tx; ++x) {
-            run += row[x];
-            row[x] = run;
-            work += min(run, kMaxTileElems) + kRowWorkPerTile;
+    // Row prefix over x (one warp per tile row, 32 columns at a time with a
+    // shuffle scan) and the work of each row.
+    {
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+        for (int y = warp; y < ty; y += nwarps) {
+            int32_t* row = raw_counts + (size_t)y * tx;
+            int carry = 0;
+            int64_t work = 0;
+            for (int x0 = 0; x0 < tx; x0 += 32) {
+                const int x = x0 + lane;
+                int v = x < tx ? row[x] : 0;
+#pragma unroll
+                for (int d = 1; d < 32; d <<= 1) {
+                    const int o = __shfl_up_sync(0xffffffffu, v, d);
+                    if (lane >= d) v += o;
+                }
+                const int run = carry + v;
+                if (x < tx) {
+                    row[x] = run;
+                    work += min(run, kMaxTileElems) + kRowWorkPerTile;
+                }
+                carry = __shfl_sync(0xffffffffu, run, 31);
+            }
+#pragma unroll
+            for (int d = 16; d > 0; d >>= 1) work += __shfl_xor_sync(0xffffffffu, work, d);
+            if (row_work && lane == 0) row_work[y] = work;
         }
-        if (row_work) row_work[y] = work;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -105,45 +121,72 @@ k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int row0, int ro
         }
     }
     __syncthreads();
-    // Exclusive scans of raw (int64) and kept = min(raw, 2048) (int32).
+    // Exclusive scans of raw (int64) and kept = min(raw, 2048) (int32): each
+    // warp scans a contiguous segment of tiles 32 at a time (coalesced), then
+    // the warps' segment totals are scanned and added.
     const int T = tx * ty;
-    const int chunk = (T + blockDim.x - 1) / blockDim.x;
-    const int b = threadIdx.x * chunk;
-    const int e = min(b + chunk, T);
-    int64_t sraw = 0;
-    int32_t skept = 0;
-    for (int t = b; t < e; ++t) {
-        int r = raw_counts[t];
-        sraw += r;
-        skept += min(r, kMaxTileElems);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int seg = ((T + nwarps - 1) / nwarps + 31) & ~31;
+    const int b = min(warp * seg, T), e = min(b + seg, T);
+    __shared__ int64_t s_raw[kCountThreads / 32];
+    __shared__ int32_t s_kept[kCountThreads / 32];
+    int64_t wraw = 0;
+    int32_t wkept = 0;
+    for (int t0 = b; t0 < e; t0 += 32) {
+        const int t = t0 + lane;
+        const int r = t < e ? raw_counts[t] : 0;
+        int64_t vr = r;
+        int32_t vk = min(r, kMaxTileElems);
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) {
+            vr += __shfl_xor_sync(0xffffffffu, vr, d);
+            vk += __shfl_xor_sync(0xffffffffu, vk, d);
+        }
+        wraw += vr;
+        wkept += vk;
     }
-    __shared__ int64_t s_raw[kCountThreads];
-    __shared__ int32_t s_kept[kCountThreads];
-    s_raw[threadIdx.x] = sraw;
-    s_kept[threadIdx.x] = skept;
+    if (lane == 0) {
+        s_raw[warp] = wraw;
+        s_kept[warp] = wkept;
+    }
     __syncthreads();
-    // Hillis-Steele inclusive scan over the per-thread sums.
-    for (int off = 1; off < (int)blockDim.x; off <<= 1) {
-        int64_t vr = threadIdx.x >= off ? s_raw[threadIdx.x - off] : 0;
-        int32_t vk = threadIdx.x >= off ? s_kept[threadIdx.x - off] : 0;
-        __syncthreads();
-        s_raw[threadIdx.x] += vr;
-        s_kept[threadIdx.x] += vk;
-        __syncthreads();
+    int64_t run_raw = 0;
+    int32_t run_kept = 0;
+    for (int w = 0; w < warp; ++w) {
+        run_raw += s_raw[w];
+        run_kept += s_kept[w];
     }
-    int64_t run_raw = s_raw[threadIdx.x] - sraw;
-    int32_t run_kept = s_kept[threadIdx.x] - skept;
-    for (int t = b; t < e; ++t) {
-        int r = raw_counts[t];
-        int k = min(r, kMaxTileElems);
-        raw_start[t] = run_raw;
-        tile_bins[t] = make_int2(run_kept, run_kept + k);
-        run_raw += r;
-        run_kept += k;
+    for (int t0 = b; t0 < e; t0 += 32) {
+        const int t = t0 + lane;
+        const int r = t < e ? raw_counts[t] : 0;
+        const int k = min(r, kMaxTileElems);
+        int64_t ir = r;
+        int32_t ik = k;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int64_t orr = __shfl_up_sync(0xffffffffu, ir, d);
+            const int32_t ok = __shfl_up_sync(0xffffffffu, ik, d);
+            if (lane >= d) {
+                ir += orr;
+                ik += ok;
+            }
+        }
+        if (t < e) {
+            raw_start[t] = run_raw + ir - r;
+            tile_bins[t] = make_int2(run_kept + ik - k, run_kept + ik);
+        }
+        run_raw += __shfl_sync(0xffffffffu, ir, 31);
+        run_kept += __shfl_sync(0xffffffffu, ik, 31);
     }
     if (threadIdx.x == blockDim.x - 1) {
-        totals[0] = s_raw[threadIdx.x];
-        totals[1] = s_kept[threadIdx.x];
+        int64_t tr = 0;
+        int32_t tk = 0;
+        for (int w = 0; w < nwarps; ++w) {
+            tr += s_raw[w];
+            tk += s_kept[w];
+        }
+        totals[0] = tr;
+        totals[1] = tk;
     }
 }
 

@@ -378,7 +378,9 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
                         accum_rec[c3] = last_alpha * last_color[c3] + (1.f - last_alpha) * accum_rec[c3];
                         last_color[c3] = col[c3];
                         dL_dalpha += (col[c3] - accum_rec[c3]) * dpix[c3];
-                        g[10 + c3] = col[c3] > 0.f ? w * dpix[c3] : 0.f;
+                        // the clamp mask (per surfel) is applied at the flush
+                        // in the colour-only kernel
+                        g[10 + c3] = (!AUX || col[c3] > 0.f) ? w * dpix[c3] : 0.f;
                     }
                     float dL_dz = 0.f;
                     if (AUX) {
@@ -441,7 +443,9 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
                         g[7] = e.v * dL_dz;
                         g[8] = dL_dz;
                     }
-                    g[9] = G * dL_dalpha * (opa * (1.0f - opa));
+                    // colour-only kernel: the per-surfel factor o (1 - o) is
+                    // applied at the flush
+                    g[9] = AUX ? G * dL_dalpha * (opa * (1.0f - opa)) : G * dL_dalpha;
                 }
                 // the forward's flags guarantee a contributing lane here: sum
                 // value vi over the warp, lanes 2 vi and 2 vi + 1 each adding
@@ -496,8 +500,11 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
                 float4* dst = reinterpret_cast<float4*>(a.raster_grads + (size_t)sid[s] * kGradStride);
                 const float4 p0 = make_float4(-dkx, -dky, -dkz, -dlx);
                 const float4 p1 = make_float4(-dly, -dlz, ex, ey);
-                const float4 p2 = make_float4(ez, acc[9], acc[10], acc[11]);
-                const float4 p3 = make_float4(acc[12], 0.f, 0.f, 0.f);
+                const float opa = r2.w;
+                const float4 r3 = srec[3][s];
+                const float4 p2 = make_float4(ez, acc[9] * (opa * (1.0f - opa)), r3.x > 0.f ? acc[10] : 0.f,
+                                              r3.y > 0.f ? acc[11] : 0.f);
+                const float4 p3 = make_float4(r3.z > 0.f ? acc[12] : 0.f, 0.f, 0.f, 0.f);
                 if (p0.x != 0.f || p0.y != 0.f || p0.z != 0.f || p0.w != 0.f) atomicAdd(dst, p0);
                 if (p1.x != 0.f || p1.y != 0.f || p1.z != 0.f || p1.w != 0.f) atomicAdd(dst + 1, p1);
                 if (p2.x != 0.f || p2.y != 0.f || p2.z != 0.f || p2.w != 0.f) atomicAdd(dst + 2, p2);
