@@ -71,7 +71,7 @@ struct Buf {
 struct Workspace {
     int device = -1;
     // per Gaussian
-    Buf records, rects, depths, radii, raster_grads;
+    Buf records, cull, rects, depths, radii, raster_grads;
     Buf xys, transmats, num_tiles_hit, normal_opacity, colors, aabb;
     Buf dL_dmean3D, dL_dscale, dL_dquat, dL_dmean2D, dL_dfeatures_dc, dL_dfeatures_rest, dL_dopacity;
     Buf dL_dtransMat, dL_dnormal3D, dL_dcolors;
@@ -97,7 +97,7 @@ struct Workspace {
     bool have_ref_proj = false, have_grads = false, have_pixels = false, have_dimg = false;
 
     void release_all() {
-        Buf* all[] = {&records, &rects, &depths, &radii, &raster_grads, &xys, &transmats, &num_tiles_hit,
+        Buf* all[] = {&records, &cull, &rects, &depths, &radii, &raster_grads, &xys, &transmats, &num_tiles_hit,
                       &normal_opacity, &colors, &aabb, &dL_dmean3D, &dL_dscale, &dL_dquat, &dL_dmean2D,
                       &dL_dfeatures_dc, &dL_dfeatures_rest, &dL_dopacity, &dL_dtransMat, &dL_dnormal3D,
                       &dL_dcolors, &tile_diff, &raw_counts, &raw_start, &tile_bins, &fill, &raw_keys,
@@ -240,6 +240,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     w.have_dimg = false;
     const size_t nn = (size_t)(n > 0 ? n : 1);
     w.records.ensure(nn * kRecordF4 * sizeof(float4));
+    w.cull.ensure(nn * kCullF4 * sizeof(float4));
     w.rects.ensure(nn * sizeof(uint2));
     w.depths.ensure(nn * sizeof(float));
     w.radii.ensure(nn * sizeof(int32_t));
@@ -275,7 +276,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     pa.rest_bases = K; pa.degrees_to_use = degrees_to_use;
     pa.glob_scale = glob_scale; pa.clip_thresh = clip;
     pa.cam = cam;
-    pa.records = w.records.as<float4>(); pa.rects = w.rects.as<uint2>(); pa.depths = w.depths.as<float>();
+    pa.records = w.records.as<float4>(); pa.cull = w.cull.as<float4>(); pa.rects = w.rects.as<uint2>(); pa.depths = w.depths.as<float>();
     pa.radii = w.radii.as<int32_t>(); pa.tile_diff = w.tile_diff.as<int32_t>();
     if (ref_outputs) {
         pa.xys = w.xys.as<float>(); pa.transmats = w.transmats.as<float>();
@@ -337,6 +338,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     ra.tile_row_begin = row0; ra.tile_row_end = row1;
     ra.tile_bins = w.tile_bins.as<int2>(); ra.gaussian_ids = w.gaussian_ids.as<int32_t>();
     ra.records = w.records.as<float4>();
+    ra.cull = w.cull.as<float4>();
     ra.bg[0] = bg[0]; ra.bg[1] = bg[1]; ra.bg[2] = bg[2];
     ra.final_Ts = w.final_Ts.as<float>(); ra.final_idx = w.final_idx.as<int32_t>(); ra.out_img = w.out_img.as<float>();
     ra.out_depth = w.out_depth.as<float>(); ra.out_normal = w.out_normal.as<float>();

@@ -29,6 +29,26 @@ constexpr float kFarN = 100.0f;
 //   r4 = (normal.y, normal.z, rmax, 0)   rmax = reject_rho(sigmoid(opacity))
 constexpr int kRecordF4 = 5;
 
+// Per-Gaussian cull record written by the projection and read by the forward
+// rasteriser to skip pixel blocks a surfel cannot reach: 2 x float4 = 32 bytes.
+//   c0 = (centre.x, centre.y, s1, t1)
+//   c1 = (s2, -E.xy / E.yy, -E.xy / E.xx, rd2)
+// The pixels where rho3d <= rmax * kCullRhoScale form a conic; when it is an
+// ellipse, d^T E d <= 1 inside it (d = pixel - centre), with E factored as
+// d^T E d = (s1 d.x + t1 d.y)^2 + (s2 d.y)^2, a sum of squares that float
+// arithmetic evaluates without cancellation however thin the ellipse.
+// Otherwise (not an ellipse, or thinner than kCullMaxAspect) s1 = t1 = s2 = 0
+// and every block passes. rd2 is the squared radius of the 2-D filter disc
+// 2 d^2 <= rmax around xy, grown by the margin; -1 when the surfel never
+// reaches alpha 1/255.
+constexpr int kCullF4 = 2;
+constexpr float kCullRhoScale = 1.002f;  // rmax growth covering float rounding of rho
+constexpr float kCullMargin = 0.25f;     // pixel margin around each tested block
+// Screen ellipses with an axis ratio above this come from surfels seen almost
+// edge-on, where the rasteriser's own float rho3d loses relative accuracy;
+// they are never culled.
+constexpr double kCullMaxAspect = 1.0e4;
+
 // Rho above which a surfel of opacity o is certainly skipped by the 1/255
 // alpha cut: o * exp(-rho/2) < 1/255 for rho > 2 ln(255 o); the +0.01 margin
 // covers the rounding of det_exp and of this bound. Negative for o < 1/255.

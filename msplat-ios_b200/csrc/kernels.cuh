@@ -42,6 +42,7 @@ struct ProjFwdArgs {
     CameraDev cam;
     // product outputs
     float4* records;         // [N, 5] float4
+    float4* cull;            // [N, 2] float4 cull record (written with the geometry)
     uint2* rects;            // [N] packed tile rect (x0 | y0 << 16, x1 | y1 << 16)
     float* depths;           // [N] view-space depth (sort key)
     int32_t* radii;          // [N]
@@ -105,6 +106,7 @@ struct RasterFwdArgs {
     int width, height, tiles_x, tiles_y;
     int tile_row_begin, tile_row_end;   // tile rows rendered by this launch
     const int2* tile_bins; const int32_t* gaussian_ids; const float4* records;
+    const float4* cull;                 // [N, 2] cull records of the projection
     float bg[3];
     float* final_Ts; int32_t* final_idx; float* out_img; float* out_depth; float* out_normal;
     float* out_alpha; float* out_median_depth; float* out_distortion;

@@ -48,6 +48,52 @@ __device__ __forceinline__ void gaussian_color(const ProjFwdArgs& a, const Param
     for (int c = 0; c < 3; ++c) rgb[c] = smax(col[c] + 0.5f, 0.0f);
 }
 
+// Cull record of one surfel (layout in common.cuh). With k = x Tw - Tu and
+// l = y Tw - Tv, the ray/plane intersection before the division is
+// p = k x l = M (x, y, 1) with columns m0 = Tv x Tw, m1 = Tw x Tu,
+// m2 = Tu x Tv, so rho3d = (p.x^2 + p.y^2) / p.z^2 <= r is the conic
+// Q(x, y) = p.x^2 + p.y^2 - r p.z^2 <= 0 with 2x2 part A (entries m_i^T W m_j,
+// W = diag(1, 1, -r)). Since T M = det(T) I for T = (Tu; Tv; Tw), its centre
+// (the pole of the line at infinity) is (Tu . w, Tv . w) / dd with
+// w = (r Tw.x, r Tw.y, -Tw.z) and dd = Tw . w, det A = det(T)^2 (-dd), and its
+// minimum Q(centre) = det(Q) / det(A) = r det(T)^2 / dd. These closed forms
+// avoid the cancellation of evaluating Q at a rounded centre. It is an
+// ellipse when dd < 0; the record stores the factors of E = A / -Q(centre):
+// s1 = sqrt(E.xx), t1 = E.xy / s1, s2 = sqrt(det E / E.xx). Computed in double
+// from the float rows (products of two floats are exact in double);
+// (tr A)^2 / det A bounds the squared axis ratio.
+__device__ void cull_record(V3 tu, V3 tv, V3 tw, float rmax, float4* out) {
+    if (!(rmax > 0.f)) {
+        out[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+        out[1] = make_float4(0.f, 0.f, 0.f, -1.f);
+        return;
+    }
+    const double r = (double)rmax * (double)kCullRhoScale;
+    const double ux = tu.x, uy = tu.y, uz = tu.z, vx = tv.x, vy = tv.y, vz = tv.z, wx = tw.x, wy = tw.y, wz = tw.z;
+    const double m0x = vy * wz - vz * wy, m0y = vz * wx - vx * wz, m0z = vx * wy - vy * wx;
+    const double m1x = wy * uz - wz * uy, m1y = wz * ux - wx * uz, m1z = wx * uy - wy * ux;
+    const double qa = m0x * m0x + m0y * m0y - r * m0z * m0z;
+    const double qb = m0x * m1x + m0y * m1y - r * m0z * m1z;
+    const double qc = m1x * m1x + m1y * m1y - r * m1z * m1z;
+    const double det_t = ux * m0x + uy * m0y + uz * m0z;
+    const double dd = r * (wx * wx + wy * wy) - wz * wz;
+    const double det_a = det_t * det_t * -dd;
+    const float rd = sqrtf(0.5f * rmax * kCullRhoScale) + kCullMargin;
+    float4 c0 = make_float4(0.f, 0.f, 0.f, 0.f), c1 = make_float4(0.f, 0.f, 0.f, rd * rd);
+    if (dd < 0.0 && det_t != 0.0 && qa > 0.0 && (qa + qc) * (qa + qc) <= kCullMaxAspect * kCullMaxAspect * det_a) {
+        const double cx = (r * (ux * wx + uy * wy) - uz * wz) / dd;
+        const double cy = (r * (vx * wx + vy * wy) - vz * wz) / dd;
+        const double sc = -dd / (r * det_t * det_t);   // -1 / Q(centre)
+        const double s1 = sqrt(qa * sc);
+        c0 = make_float4((float)cx, (float)cy, (float)s1, (float)(qb * sc / s1));
+        c1.x = (float)sqrt(det_a * sc / qa);
+        c1.y = (float)(-qb / qc);
+        c1.z = (float)(-qb / qa);
+    }
+    out[0] = c0;
+    out[1] = c1;
+}
+
 __global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= a.n) return;
@@ -139,7 +185,9 @@ __global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
     rec[1] = make_float4(T1.y, T1.z, T2.x, T2.y);
     rec[2] = make_float4(T2.z, cxp, cyp, opac);
     rec[3] = make_float4(rgb[0], rgb[1], rgb[2], nrm.x);
-    rec[4] = make_float4(nrm.y, nrm.z, reject_rho(opac), 0.f);
+    const float rmax = reject_rho(opac);
+    rec[4] = make_float4(nrm.y, nrm.z, rmax, 0.f);
+    cull_record(T0, T1, T2, rmax, a.cull + (size_t)i * kCullF4);
     if (a.num_tiles_hit) {
         a.num_tiles_hit[i] = area;
         a.xys[2 * i] = cxp; a.xys[2 * i + 1] = cyp;

@@ -13,9 +13,11 @@
 // 8x8 groups per tile, each re-reading the tile list); the tile's surfels are
 // streamed in batches of 256: ids are read coalesced, the 80-byte per-Gaussian
 // records (written once by the projection) are gathered into shared memory
-// structure-of-arrays. Each warp owns an 8x4 pixel block: it tests 32 surfel
-// boxes at a time (one per lane), and walks only the surfels whose box meets
-// its block. The forward records, per tile-list entry, which warps blended
+// structure-of-arrays. Each warp owns an 8x4 pixel block: it tests 32
+// surfels at a time (one per lane) against its block with the exact
+// screen-space conic of rho3d <= rmax and the 2-D filter disc (32-byte cull
+// records from the projection), and walks only the surfels that can reach
+// the block. The forward records, per tile-list entry, which warps blended
 // the surfel (one bit per warp); the backward drops entries no warp blended
 // and each warp visits only its own, so pairs that were rejected in the
 // forward are not evaluated again. In the backward the per-(pixel, surfel)
@@ -77,40 +79,26 @@ __device__ __forceinline__ bool eval_pair(float px, float py, float4 r0, float4 
 __device__ __forceinline__ int tile_lx(int t) { return ((t >> 5) & 1) * 8 + (t & 7); }
 __device__ __forceinline__ int tile_ly(int t) { return (t >> 6) * 4 + ((t >> 3) & 3); }
 
-__device__ __forceinline__ int to_pix(float v) {
-    return (int)fminf(fmaxf(v, -1.0e9f), 1.0e9f);
-}
-
-// Conservative inclusive pixel box (x0, y0, x1, y1) outside which the surfel
-// cannot reach alpha >= 1/255: the union of the 2-D filter disc
-// 2 d^2 <= rmax around the centre and the screen bounds of the projected disc
-// u^2 + v^2 <= rmax. The latter is the axis-aligned box of a conic computed
-// from its dual (T diag(rmax, rmax, -1) T^T), valid when the disc lies wholly
-// in front of the camera (d < 0); otherwise the box is unbounded. A 2-pixel
-// margin covers the rounding of this float computation. Empty (x0 > x1) when
-// the surfel can never reach 1/255.
-__device__ __forceinline__ int4 surfel_box(float4 r0, float4 r1, float4 r2, float rmax) {
-    const int4 everything = make_int4(-1000000000, -1000000000, 1000000000, 1000000000);
-    if (!(rmax > 0.f)) return (rmax == rmax) ? make_int4(1, 1, 0, 0) : everything;
-    const float r2d = sqrtf(0.5f * rmax) + 2.0f;
-    float x0 = r2.y - r2d, x1 = r2.y + r2d, y0 = r2.z - r2d, y1 = r2.z + r2d;
-    const float t0x = r0.x, t0y = r0.y, t0z = r0.z;   // row Tu
-    const float t1x = r0.w, t1y = r1.x, t1z = r1.y;   // row Tv
-    const float t2x = r1.z, t2y = r1.w, t2z = r2.x;   // row Tw
-    const float d = rmax * (t2x * t2x + t2y * t2y) - t2z * t2z;
-    if (!(d < 0.f)) return everything;
-    const float fa = rmax / d, fc = -1.0f / d;
-    const float cx = fa * (t0x * t2x + t0y * t2y) + fc * (t0z * t2z);
-    const float cy = fa * (t1x * t2x + t1y * t2y) + fc * (t1z * t2z);
-    const float hx = sqrtf(fmaxf(0.f, cx * cx - (fa * (t0x * t0x + t0y * t0y) + fc * (t0z * t0z))));
-    const float hy = sqrtf(fmaxf(0.f, cy * cy - (fa * (t1x * t1x + t1y * t1y) + fc * (t1z * t1z))));
-    const float mx = 2.0f + 1e-3f * (fabsf(cx) + hx), my = 2.0f + 1e-3f * (fabsf(cy) + hy);
-    x0 = fminf(x0, cx - hx - mx);
-    x1 = fmaxf(x1, cx + hx + mx);
-    y0 = fminf(y0, cy - hy - my);
-    y1 = fmaxf(y1, cy + hy + my);
-    if (!(x0 <= x1) || !(y0 <= y1)) return everything;
-    return make_int4(to_pix(floorf(x0)), to_pix(floorf(y0)), to_pix(ceilf(x1)), to_pix(ceilf(y1)));
+// Whether a surfel can reach alpha >= 1/255 anywhere in the pixel rectangle
+// [x0, x1] x [y0, y1] (bounds already grown by kCullMargin), from its cull
+// record (common.cuh) and its 2-D centre m: the filter disc
+// |p - m|^2 <= rd2 meets the rectangle, or the minimum of d^T E d over the
+// rectangle (d = p - centre), evaluated as the sum of squares
+// (s1 d.x + t1 d.y)^2 + (s2 d.y)^2, is at most 1. For a convex quadratic whose
+// minimum lies outside the rectangle, the minimum over the rectangle is on
+// the edge x = clamp(centre.x) or on the edge y = clamp(centre.y); along
+// each, the best other coordinate is the clamped unconstrained one.
+__device__ __forceinline__ bool block_hit(float4 c0, float4 c1, float mx, float my, float x0, float x1, float y0,
+                                          float y1) {
+    const float ddx = fmaxf(0.f, fmaxf(x0 - mx, mx - x1)), ddy = fmaxf(0.f, fmaxf(y0 - my, my - y1));
+    const float lox = x0 - c0.x, hix = x1 - c0.x, loy = y0 - c0.y, hiy = y1 - c0.y;
+    const float dx = fminf(fmaxf(0.f, lox), hix), dy = fminf(fmaxf(0.f, loy), hiy);
+    const float dy1 = fminf(fmaxf(c1.y * dx, loy), hiy);
+    const float dx2 = fminf(fmaxf(c1.z * dy, lox), hix);
+    const float h1 = fmaf(c0.z, dx, c0.w * dy1), g1 = c1.x * dy1;
+    const float h2 = fmaf(c0.z, dx2, c0.w * dy), g2 = c1.x * dy;
+    const float q1 = fmaf(h1, h1, g1 * g1), q2 = fmaf(h2, h2, g2 * g2);
+    return c1.w >= 0.f && (fminf(q1, q2) <= 1.f || fmaf(ddx, ddx, ddy * ddy) <= c1.w);
 }
 
 // Packs the per-warp blend flags of batch entry threadIdx.x (one byte per
@@ -128,15 +116,16 @@ __device__ __forceinline__ void flush_blend_flags(uint8_t* mask, const uint2* sf
 
 __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
     __shared__ float4 srec[kRecordF4][kThreads];
-    __shared__ int4 sbox[kThreads];
+    __shared__ float4 scull[kCullF4][kThreads];
     __shared__ uint2 sflag[kThreads];  // per batch entry: byte w set when warp w blended it
     constexpr unsigned full = 0xffffffffu;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int tile = (a.tile_row_begin + blockIdx.y) * a.tiles_x + blockIdx.x;
     const int lx = tile_lx(threadIdx.x), ly = tile_ly(threadIdx.x);
-    // this warp's 8x4 pixel block
-    const int wx0 = blockIdx.x * kTile + (warp & 1) * 8, wx1 = wx0 + 7;
-    const int wy0 = (a.tile_row_begin + blockIdx.y) * kTile + (warp >> 1) * 4, wy1 = wy0 + 3;
+    // this warp's 8x4 pixel block, grown by the cull margin
+    const float wx0 = (float)(blockIdx.x * kTile + (warp & 1) * 8) - kCullMargin, wx1 = wx0 + (7.f + 2.f * kCullMargin);
+    const float wy0 = (float)((a.tile_row_begin + blockIdx.y) * kTile + (warp >> 1) * 4) - kCullMargin,
+                wy1 = wy0 + (3.f + 2.f * kCullMargin);
     const int j = blockIdx.x * kTile + lx;
     const int i = (a.tile_row_begin + blockIdx.y) * kTile + ly;
     const bool inside = (i < a.height) && (j < a.width);
@@ -161,10 +150,11 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
         if (idx < range.y) {
             const int g = a.gaussian_ids[idx];
             const float4* r = a.records + (size_t)g * kRecordF4;
-            float4 q[kRecordF4];
+            const float4* cr = a.cull + (size_t)g * kCullF4;
 #pragma unroll
-            for (int k = 0; k < kRecordF4; ++k) srec[k][threadIdx.x] = q[k] = __ldg(r + k);
-            sbox[threadIdx.x] = surfel_box(q[0], q[1], q[2], q[4].z);
+            for (int k = 0; k < kRecordF4; ++k) srec[k][threadIdx.x] = __ldg(r + k);
+#pragma unroll
+            for (int k = 0; k < kCullF4; ++k) scull[k][threadIdx.x] = __ldg(cr + k);
         }
         sflag[threadIdx.x] = make_uint2(0u, 0u);
         __syncthreads();
@@ -172,22 +162,23 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
         if (__all_sync(full, done)) continue;
         const int bs = min(kThreads, range.y - b0);
         const int base = b0 - range.x + 1;  // 1-based position of surfel 0 of this batch in the tile list
-        // 32 surfels at a time: one box test per lane, then the warp walks
-        // the surfels whose box meets its 8x4 pixel block
+        // 32 surfels at a time: one cull test per lane, then the warp walks
+        // the surfels that can reach its 8x4 pixel block
         for (int c = 0; c < bs; c += 32) {
             bool hit = false;
             if (c + lane < bs) {
-                const int4 box = sbox[c + lane];
-                hit = !(box.x > wx1 || box.z < wx0 || box.y > wy1 || box.w < wy0);
+                const int q = c + lane;
+                const float4 r2 = srec[2][q];
+                hit = block_hit(scull[0][q], scull[1][q], r2.y, r2.z, wx0, wx1, wy0, wy1);
             }
             unsigned bits = __ballot_sync(full, hit);
             while (bits) {
                 const int s = c + __ffs(bits) - 1;
                 bits &= bits - 1;
                 if (done) continue;
-                // no per-pixel box test: the box meets this warp's block, so
-                // the warp evaluates the surfel anyway, and eval_pair's exact
-                // early rejection covers the pixels outside the box
+                // no per-pixel cull test: the surfel can reach this warp's
+                // block, so the warp evaluates it anyway, and eval_pair's
+                // exact early rejection covers the pixels it cannot reach
                 Pair e;
                 if (!eval_pair(px, py, srec[0][s], srec[1][s], srec[2][s], srec[4][s].z, e)) continue;
                 contributor = base + s;

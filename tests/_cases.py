@@ -21,6 +21,11 @@ def case_config(name: str) -> S.SceneConfig:
         # big surfels on a small image: most tiles exceed the 2048 cap
         return S.small_config(24_000, 2, 96, 80, focal=90.0, num_cameras=1,
                               log_scale_mean=math.log(0.08), log_scale_std=0.3)
+    if name == "thin":
+        # strongly anisotropic surfels in every orientation: thin, grazing
+        # ellipses exercise the rasteriser's conic cull at its boundary
+        return S.small_config(12_000, 1, 256, 192, focal=230.0, num_cameras=2,
+                              log_scale_mean=math.log(0.02), log_scale_std=1.6)
     if name == "cfg1":
         return S.CONFIGS[1]
     raise KeyError(name)

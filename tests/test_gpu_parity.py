@@ -40,7 +40,7 @@ def _device_scene(case):
     return B.DeviceGaussians(*case.scene.params(), sh_degree=case.degree)
 
 
-CASES = ["cfg0", "sh3_small", "sh1_odd", "overflow"]
+CASES = ["cfg0", "sh3_small", "sh1_odd", "overflow", "thin"]
 
 
 @pytest.mark.parametrize("name", CASES)
