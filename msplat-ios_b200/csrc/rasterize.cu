@@ -24,9 +24,9 @@
 // gradients are summed across the warp through a per-warp transpose buffer in
 // shared memory (13 stores, four 16-byte loads and one shuffle per lane),
 // across warps in shared memory, and leave the CTA as four float4 atomics per
-// surfel. The replayed pair evaluation uses
-// the forward's exact operation sequence; the gradient arithmetic after it
-// uses fast reciprocals.
+// surfel. The replayed pair evaluation follows the forward's operation
+// sequence with the hardware reciprocal and exponential; the gradient
+// arithmetic after it uses fast reciprocals.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -41,11 +41,16 @@ struct Pair {
 };
 
 
-// Per-(pixel, surfel) evaluation with a pinned IEEE operation sequence
-// (identical in the forward and the backward replay, and in the CPU checker).
-// Before the exact sequence, a pair whose 2-D and 3-D falloff both exceed
-// rmax is rejected without the division and the exponential; such a pair
-// would fail the alpha >= 1/255 test anyway, so results are unchanged.
+// Per-(pixel, surfel) evaluation. EXACT (the forward): a pinned IEEE
+// operation sequence, identical in the CPU checker, with the IEEE reciprocal
+// and the deterministic exponential. The backward replay uses the hardware
+// reciprocal and exponential instead (a few ulp apart): its gradients are
+// compared within a tolerance, and a pair whose alpha lies within those ulp
+// of 1/255 is the only one whose decision can differ from the forward's.
+// Before either sequence, a pair whose 2-D and 3-D falloff both exceed rmax
+// is rejected without the division and the exponential; such a pair would
+// fail the alpha >= 1/255 test anyway, so results are unchanged.
+template <bool EXACT>
 __device__ __forceinline__ bool eval_pair(float px, float py, float4 r0, float4 r1, float4 r2, float rmax, Pair& e) {
     // Tu = r0.xyz, Tv = (r0.w, r1.x, r1.y), Tw = (r1.z, r1.w, r2.x), xy = r2.yz, opacity = r2.w
     const float dx = fsub(r2.y, px), dy = fsub(r2.z, py);
@@ -57,7 +62,7 @@ __device__ __forceinline__ bool eval_pair(float px, float py, float4 r0, float4 
     const float p_z = ffma(kx, ly, -fmul(ky, lx));
     if (rho2d > rmax && p_x * p_x + p_y * p_y > (rmax * 1.0001f) * (p_z * p_z)) return false;
     if (p_z == 0.0f) return false;
-    const float inv_z = __frcp_rn(p_z);
+    const float inv_z = EXACT ? __frcp_rn(p_z) : __fdividef(1.0f, p_z);
     const float u = fmul(p_x, inv_z), v = fmul(p_y, inv_z);
     const float rho3d = ffma(u, u, fmul(v, v));
     const float rho = (rho2d < rho3d) ? rho2d : rho3d;
@@ -65,7 +70,7 @@ __device__ __forceinline__ bool eval_pair(float px, float py, float4 r0, float4 
     if (depth < kNearN) return false;
     const float power = fmul(-0.5f, rho);
     if (power > 0.0f) return false;
-    const float G = det_exp(power);
+    const float G = EXACT ? det_exp(power) : __expf(power);
     const float og = fmul(r2.w, G);
     const float alpha = (og < 0.99f) ? og : 0.99f;
     if (alpha < 1.0f / 255.0f) return false;
@@ -180,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
                 // block, so the warp evaluates it anyway, and eval_pair's
                 // exact early rejection covers the pixels it cannot reach
                 Pair e;
-                if (!eval_pair(px, py, srec[0][s], srec[1][s], srec[2][s], srec[4][s].z, e)) continue;
+                if (!eval_pair<true>(px, py, srec[0][s], srec[1][s], srec[2][s], srec[4][s].z, e)) continue;
                 contributor = base + s;
                 const float next_T = fmul(T, fsub(1.0f, e.alpha));
                 if (next_T <= 1e-4f) {
@@ -356,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
                 for (int k = 0; k < 16; ++k) g[k] = 0.f;
                 Pair e;
                 const float4 r0 = srec[0][s], r1 = srec[1][s], r2 = srec[2][s];
-                if (rel < last_c && eval_pair(px, py, r0, r1, r2, srec[4][s].z, e)) {
+                if (rel < last_c && eval_pair<false>(px, py, r0, r1, r2, srec[4][s].z, e)) {
                     const float4 r3 = srec[3][s], r4 = srec[4][s];
                     const float alpha = e.alpha, G = e.G, opa = r2.w;
                     const float r1ma = __fdividef(1.0f, 1.0f - alpha);
