@@ -96,6 +96,29 @@ __device__ __forceinline__ float det_exp(float x) {
     return __fmul_rn(p, __int_as_float((k + 127) << 23));
 }
 
+// det_exp for arguments known to lie in [-86, 0] (or NaN): the same sequence
+// without the two range tests, so the results are identical there. The
+// rasteriser's falloff exp(-rho/2) is only evaluated for rho within the
+// surfel's rejection bound (at most 2 ln 255 + 0.01 plus rounding), i.e. for
+// arguments in [-5.6, 0].
+__device__ __forceinline__ float det_exp_nonpos(float x) {
+    if (x != x) return x;
+    const float shifted = __fadd_rn(__fmul_rn(x, 1.44269502f), 12582912.0f);
+    const float kf = __fsub_rn(shifted, 12582912.0f);
+    float r = __fmaf_rn(-kf, 0.693145751953125f, x);
+    r = __fmaf_rn(-kf, 1.42860677e-06f, r);
+    float p = 1.98412698e-04f;
+    p = __fmaf_rn(p, r, 1.38888889e-03f);
+    p = __fmaf_rn(p, r, 8.33333377e-03f);
+    p = __fmaf_rn(p, r, 4.16666679e-02f);
+    p = __fmaf_rn(p, r, 1.66666672e-01f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    const int k = __float_as_int(shifted) - 0x4B400000;
+    return __fmul_rn(p, __int_as_float((k + 127) << 23));
+}
+
 // Device-side error word: kernels OR bits into it instead of trapping; the
 // host reads it after the step.
 enum : uint32_t {

@@ -70,7 +70,8 @@ __device__ __forceinline__ bool eval_pair(float px, float py, float4 r0, float4 
     if (depth < kNearN) return false;
     const float power = fmul(-0.5f, rho);
     if (power > 0.0f) return false;
-    const float G = EXACT ? det_exp(power) : __expf(power);
+    // power is in [-5.6, 0] here (rho passed the rejection bound) or NaN
+    const float G = EXACT ? det_exp_nonpos(power) : __expf(power);
     const float og = fmul(r2.w, G);
     const float alpha = (og < 0.99f) ? og : 0.99f;
     if (alpha < 1.0f / 255.0f) return false;
