@@ -47,9 +47,9 @@ struct Pair {
 // reciprocal and exponential instead (a few ulp apart): its gradients are
 // compared within a tolerance, and a pair whose alpha lies within those ulp
 // of 1/255 is the only one whose decision can differ from the forward's.
-// Before either sequence, a pair whose 2-D and 3-D falloff both exceed rmax
-// is rejected without the division and the exponential; such a pair would
-// fail the alpha >= 1/255 test anyway, so results are unchanged.
+// In the forward, a pair whose 2-D and 3-D falloff both exceed rmax is
+// rejected before the division and the exponential; such a pair would fail
+// the alpha >= 1/255 test anyway, so results are unchanged.
 template <bool EXACT>
 __device__ __forceinline__ bool eval_pair(float px, float py, float4 r0, float4 r1, float4 r2, float rmax, Pair& e) {
     // Tu = r0.xyz, Tv = (r0.w, r1.x, r1.y), Tw = (r1.z, r1.w, r2.x), xy = r2.yz, opacity = r2.w
@@ -60,7 +60,9 @@ __device__ __forceinline__ bool eval_pair(float px, float py, float4 r0, float4 
     const float p_x = ffma(ky, lz, -fmul(kz, ly));
     const float p_y = ffma(kz, lx, -fmul(kx, lz));
     const float p_z = ffma(kx, ly, -fmul(ky, lx));
-    if (rho2d > rmax && p_x * p_x + p_y * p_y > (rmax * 1.0001f) * (p_z * p_z)) return false;
+    // (the backward visits only warps with a blending lane, so there the test
+    // would save nothing: its lanes fail the alpha test below instead)
+    if (EXACT && rho2d > rmax && p_x * p_x + p_y * p_y > (rmax * 1.0001f) * (p_z * p_z)) return false;
     if (p_z == 0.0f) return false;
     const float inv_z = EXACT ? __frcp_rn(p_z) : __fdividef(1.0f, p_z);
     const float u = fmul(p_x, inv_z), v = fmul(p_y, inv_z);
