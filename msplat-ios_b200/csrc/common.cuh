@@ -97,12 +97,13 @@ __device__ __forceinline__ float det_exp(float x) {
 }
 
 // det_exp for arguments known to lie in [-86, 0] (or NaN): the same sequence
-// without the two range tests, so the results are identical there. The
-// rasteriser's falloff exp(-rho/2) is only evaluated for rho within the
-// surfel's rejection bound (at most 2 ln 255 + 0.01 plus rounding), i.e. for
-// arguments in [-5.6, 0].
+// without the range tests, so the results are identical there (a NaN
+// propagates through the polynomial). The rasteriser's falloff exp(-rho/2)
+// is used only for rho within the surfel's rejection bound (at most
+// 2 ln 255 + 0.01 plus rounding), i.e. for arguments in [-5.6, 0]; lanes whose
+// result is discarded may pass anything, so the exponent is assembled in
+// unsigned arithmetic, defined for every input.
 __device__ __forceinline__ float det_exp_nonpos(float x) {
-    if (x != x) return x;
     const float shifted = __fadd_rn(__fmul_rn(x, 1.44269502f), 12582912.0f);
     const float kf = __fsub_rn(shifted, 12582912.0f);
     float r = __fmaf_rn(-kf, 0.693145751953125f, x);
@@ -115,8 +116,8 @@ __device__ __forceinline__ float det_exp_nonpos(float x) {
     p = __fmaf_rn(p, r, 0.5f);
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
-    const int k = __float_as_int(shifted) - 0x4B400000;
-    return __fmul_rn(p, __int_as_float((k + 127) << 23));
+    const unsigned k = __float_as_uint(shifted) - 0x4B400000u;
+    return __fmul_rn(p, __uint_as_float((k + 127u) << 23));
 }
 
 // Device-side error word: kernels OR bits into it instead of trapping; the

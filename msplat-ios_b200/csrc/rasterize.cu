@@ -38,48 +38,52 @@ constexpr int kThreads = 256;
 struct Pair {
     float u, v, inv_z, rho3d, rho2d, depth, G, alpha;
     float kx, ky, kz, lx, ly, lz;
+    float p_x, p_y, p_z;
 };
 
-
-// Per-(pixel, surfel) evaluation. EXACT (the forward): a pinned IEEE
-// operation sequence, identical in the CPU checker, with the IEEE reciprocal
-// and the deterministic exponential. The backward replay uses the hardware
-// reciprocal and exponential instead (a few ulp apart): its gradients are
-// compared within a tolerance, and a pair whose alpha lies within those ulp
-// of 1/255 is the only one whose decision can differ from the forward's.
-// In the forward, a pair whose 2-D and 3-D falloff both exceed rmax is
-// rejected before the division and the exponential; such a pair would fail
-// the alpha >= 1/255 test anyway, so results are unchanged.
-template <bool EXACT>
-__device__ __forceinline__ bool eval_pair(float px, float py, float4 r0, float4 r1, float4 r2, float rmax, Pair& e) {
+// Per-(pixel, surfel) evaluation in two stages, both straight-line (every
+// test is folded into the returned predicate, so that the lanes of a warp do
+// not diverge inside them).
+//
+// Stage 1: the 2-D falloff, k = px Tw - Tu, l = py Tw - Tv and p = k x l.
+// Returns false when both falloffs certainly exceed rmax: such a pair fails
+// the alpha >= 1/255 test of stage 2 anyway. The forward uses it to skip a
+// surfel for the whole warp when no lane passes.
+__device__ __forceinline__ bool pair_stage1(float px, float py, float4 r0, float4 r1, float4 r2, float rmax, Pair& e) {
     // Tu = r0.xyz, Tv = (r0.w, r1.x, r1.y), Tw = (r1.z, r1.w, r2.x), xy = r2.yz, opacity = r2.w
     const float dx = fsub(r2.y, px), dy = fsub(r2.z, py);
-    const float rho2d = fmul(kFilterInvSq, ffma(dx, dx, fmul(dy, dy)));
-    const float kx = ffma(px, r1.z, -r0.x), ky = ffma(px, r1.w, -r0.y), kz = ffma(px, r2.x, -r0.z);
-    const float lx = ffma(py, r1.z, -r0.w), ly = ffma(py, r1.w, -r1.x), lz = ffma(py, r2.x, -r1.y);
-    const float p_x = ffma(ky, lz, -fmul(kz, ly));
-    const float p_y = ffma(kz, lx, -fmul(kx, lz));
-    const float p_z = ffma(kx, ly, -fmul(ky, lx));
-    // (the backward visits only warps with a blending lane, so there the test
-    // would save nothing: its lanes fail the alpha test below instead)
-    if (EXACT && rho2d > rmax && p_x * p_x + p_y * p_y > (rmax * 1.0001f) * (p_z * p_z)) return false;
-    if (p_z == 0.0f) return false;
-    const float inv_z = EXACT ? __frcp_rn(p_z) : __fdividef(1.0f, p_z);
-    const float u = fmul(p_x, inv_z), v = fmul(p_y, inv_z);
+    e.rho2d = fmul(kFilterInvSq, ffma(dx, dx, fmul(dy, dy)));
+    e.kx = ffma(px, r1.z, -r0.x); e.ky = ffma(px, r1.w, -r0.y); e.kz = ffma(px, r2.x, -r0.z);
+    e.lx = ffma(py, r1.z, -r0.w); e.ly = ffma(py, r1.w, -r1.x); e.lz = ffma(py, r2.x, -r1.y);
+    e.p_x = ffma(e.ky, e.lz, -fmul(e.kz, e.ly));
+    e.p_y = ffma(e.kz, e.lx, -fmul(e.kx, e.lz));
+    e.p_z = ffma(e.kx, e.ly, -fmul(e.ky, e.lx));
+    return !(e.rho2d > rmax && e.p_x * e.p_x + e.p_y * e.p_y > (rmax * 1.0001f) * (e.p_z * e.p_z));
+}
+
+// Stage 2: ray/plane intersection, falloff, depth and alpha; returns whether
+// the pair is blended (p.z != 0, depth >= near, alpha >= 1/255). EXACT (the
+// forward): a pinned IEEE operation sequence, identical in the CPU checker,
+// with the IEEE reciprocal and the deterministic exponential. The backward
+// replay uses the hardware reciprocal and exponential instead (a few ulp
+// apart): its gradients are compared within a tolerance, and a pair whose
+// alpha lies within those ulp of 1/255 is the only one whose decision can
+// differ from the forward's. Lanes whose result is discarded may evaluate
+// out-of-range arguments here; every operation stays defined for them.
+template <bool EXACT>
+__device__ __forceinline__ bool pair_stage2(float4 r1, float4 r2, Pair& e) {
+    const float inv_z = EXACT ? __frcp_rn(e.p_z) : __fdividef(1.0f, e.p_z);
+    const float u = fmul(e.p_x, inv_z), v = fmul(e.p_y, inv_z);
     const float rho3d = ffma(u, u, fmul(v, v));
-    const float rho = (rho2d < rho3d) ? rho2d : rho3d;
+    const float rho = (e.rho2d < rho3d) ? e.rho2d : rho3d;
     const float depth = ffma(u, r1.z, ffma(v, r1.w, r2.x));
-    if (depth < kNearN) return false;
     const float power = fmul(-0.5f, rho);
-    if (power > 0.0f) return false;
-    // power is in [-5.6, 0] here (rho passed the rejection bound) or NaN
+    // for a lane that passed stage 1, power is in [-5.6, 0] or NaN
     const float G = EXACT ? det_exp_nonpos(power) : __expf(power);
     const float og = fmul(r2.w, G);
     const float alpha = (og < 0.99f) ? og : 0.99f;
-    if (alpha < 1.0f / 255.0f) return false;
-    e.u = u; e.v = v; e.inv_z = inv_z; e.rho3d = rho3d; e.rho2d = rho2d; e.depth = depth; e.G = G; e.alpha = alpha;
-    e.kx = kx; e.ky = ky; e.kz = kz; e.lx = lx; e.ly = ly; e.lz = lz;
-    return true;
+    e.u = u; e.v = v; e.inv_z = inv_z; e.rho3d = rho3d; e.depth = depth; e.G = G; e.alpha = alpha;
+    return (e.p_z != 0.0f) & !(depth < kNearN) & !(power > 0.0f) & !(alpha < 1.0f / 255.0f);
 }
 
 // Pixel of thread t inside its 16x16 tile: each warp covers an 8x4 block, so
@@ -183,12 +187,14 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
             while (bits) {
                 const int s = c + __ffs(bits) - 1;
                 bits &= bits - 1;
-                if (done) continue;
                 // no per-pixel cull test: the surfel can reach this warp's
-                // block, so the warp evaluates it anyway, and eval_pair's
-                // exact early rejection covers the pixels it cannot reach
+                // block; stage 1's rejection bound covers the pixels it
+                // cannot reach, and the warp moves on when no lane is left
                 Pair e;
-                if (!eval_pair<true>(px, py, srec[0][s], srec[1][s], srec[2][s], srec[4][s].z, e)) continue;
+                const float4 q1 = srec[1][s], q2 = srec[2][s];
+                const bool cand = (!done) & pair_stage1(px, py, srec[0][s], q1, q2, srec[4][s].z, e);
+                if (!__any_sync(full, cand)) continue;
+                if (!(pair_stage2<true>(q1, q2, e) & cand)) continue;
                 contributor = base + s;
                 const float next_T = fmul(T, fsub(1.0f, e.alpha));
                 if (next_T <= 1e-4f) {
@@ -364,7 +370,8 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
                 for (int k = 0; k < 16; ++k) g[k] = 0.f;
                 Pair e;
                 const float4 r0 = srec[0][s], r1 = srec[1][s], r2 = srec[2][s];
-                if (rel < last_c && eval_pair<false>(px, py, r0, r1, r2, srec[4][s].z, e)) {
+                pair_stage1(px, py, r0, r1, r2, 0.f, e);
+                if ((rel < last_c) & pair_stage2<false>(r1, r2, e)) {
                     const float4 r3 = srec[3][s], r4 = srec[4][s];
                     const float alpha = e.alpha, G = e.G, opa = r2.w;
                     const float r1ma = __fdividef(1.0f, 1.0f - alpha);
