@@ -252,7 +252,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     w.raw_counts.ensure((size_t)T * 4);
     w.raw_start.ensure((size_t)T * 8);
     w.tile_bins.ensure((size_t)T * sizeof(int2));
-    w.fill.ensure((size_t)T * 4);
+    w.fill.ensure((size_t)T * 8);
     w.totals.ensure(4 * sizeof(int64_t));
     w.err.ensure(sizeof(uint32_t));
     w.final_Ts.ensure(P * 3 * 4); w.final_idx.ensure(P * 2 * 4); w.out_img.ensure(P * 3 * 4);
@@ -260,7 +260,6 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     w.out_median.ensure(P * 4); w.out_dist.ensure(P * 4);
 
     CK(cudaMemsetAsync(w.tile_diff.p, 0, (size_t)(tx + 1) * (ty + 1) * 4, s));
-    CK(cudaMemsetAsync(w.fill.p, 0, (size_t)T * 4, s));
     CK(cudaMemsetAsync(w.err.p, 0, sizeof(uint32_t), s));
 
     ProjFwdArgs pa{};
@@ -288,7 +287,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     mark(w, kStCounts, s);
     if (balance_world > 0) w.row_work.ensure((size_t)ty * sizeof(int64_t));
     launch_tile_counts(w.tile_diff.as<int32_t>(), tx, ty, row0, row1, w.raw_counts.as<int32_t>(),
-                       w.raw_start.as<int64_t>(), w.tile_bins.as<int2>(), w.totals.as<int64_t>(),
+                       w.raw_start.as<int64_t>(), w.fill.as<uint64_t>(), w.tile_bins.as<int2>(), w.totals.as<int64_t>(),
                        balance_world > 0 ? w.row_work.as<int64_t>() : nullptr, s, balance_world, balance_rank);
     // The one host read of the step: buffer sizes for the intersections (and
     // the band the kernel chose, when balancing).
@@ -309,8 +308,8 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     w.gaussian_ids.ensure((size_t)(kept > 0 ? kept : 1) * sizeof(int32_t));
     w.blend_mask.ensure((size_t)(kept > 0 ? kept : 1));
     mark(w, kStEmit, s);
-    launch_emit_keys(n, w.rects.as<uint2>(), w.depths.as<float>(), tx, row0, row1, w.raw_start.as<int64_t>(),
-                     w.fill.as<int32_t>(), w.raw_keys.as<uint64_t>(), s);
+    launch_emit_keys(n, w.rects.as<uint2>(), w.depths.as<float>(), tx, row0, row1, w.fill.as<uint64_t>(),
+                     w.raw_keys.as<uint64_t>(), s);
     mark(w, kStSort, s);
     launch_tile_sort(row0 * tx, (row1 - row0) * tx, w.raw_counts.as<int32_t>(), w.raw_start.as<int64_t>(), w.raw_keys.as<uint64_t>(),
                      w.tile_bins.as<int2>(), w.gaussian_ids.as<int32_t>(), w.err.as<uint32_t>(), s);

@@ -54,8 +54,8 @@ __device__ int band_cut(const int64_t* work, int ty, double total, int r, int wo
 // totals[2..3] next to the raw and kept totals (totals[0..1]).
 __global__ void __launch_bounds__(kCountThreads)
 k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int row0, int row1, int32_t* __restrict__ raw_counts,
-              int64_t* __restrict__ raw_start, int2* __restrict__ tile_bins, int64_t* __restrict__ totals,
-              int64_t* __restrict__ row_work, int world, int rank) {
+              int64_t* __restrict__ raw_start, unsigned long long* __restrict__ fill, int2* __restrict__ tile_bins,
+              int64_t* __restrict__ totals, int64_t* __restrict__ row_work, int world, int rank) {
     __shared__ int s_rows[2];
     const int dw = tx + 1;
     // Column prefix over y (one thread per tile column).
@@ -173,6 +173,7 @@ k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int row0, int ro
         }
         if (t < e) {
             raw_start[t] = run_raw + ir - r;
+            fill[t] = (unsigned long long)(run_raw + ir - r);
             tile_bins[t] = make_int2(run_kept + ik - k, run_kept + ik);
         }
         run_raw += __shfl_sync(0xffffffffu, ir, 31);
@@ -197,7 +198,7 @@ k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int row0, int ro
 // in flight whatever the rectangle sizes.
 __global__ void __launch_bounds__(256)
 k_emit_keys(int n, const uint2* __restrict__ rects, const float* __restrict__ depths, int tx, int row0, int row1,
-            const int64_t* __restrict__ raw_start, int32_t* __restrict__ fill, uint64_t* __restrict__ keys) {
+            unsigned long long* __restrict__ fill, uint64_t* __restrict__ keys) {
     constexpr unsigned full = 0xffffffffu;
     const int lane = threadIdx.x & 31;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -249,18 +250,15 @@ k_emit_keys(int n, const uint2* __restrict__ rects, const float* __restrict__ de
                 tile[q] = (o_y0 + ry) * tx + o_x0 + (local - ry * o_w);
             }
         }
-        int slot[kPairsPerLane];
-        int64_t start[kPairsPerLane];
-#pragma unroll
-        for (int q = 0; q < kPairsPerLane; ++q) {
-            if (tile[q] >= 0) {
-                slot[q] = atomicAdd(&fill[tile[q]], 1);
-                start[q] = __ldg(raw_start + tile[q]);
-            }
-        }
+        // fill[t] starts at the tile's first key position (k_tile_counts),
+        // so the atomic returns the key's position directly
+        unsigned long long pos[kPairsPerLane];
 #pragma unroll
         for (int q = 0; q < kPairsPerLane; ++q)
-            if (tile[q] >= 0) keys[start[q] + slot[q]] = okey[q];
+            if (tile[q] >= 0) pos[q] = atomicAdd(&fill[tile[q]], 1ull);
+#pragma unroll
+        for (int q = 0; q < kPairsPerLane; ++q)
+            if (tile[q] >= 0) keys[pos[q]] = okey[q];
     }
 }
 
@@ -493,18 +491,20 @@ k_tile_sort(const int32_t* __restrict__ raw_counts, const int64_t* __restrict__ 
 }  // namespace
 
 void launch_tile_counts(const int32_t* tile_diff, int tiles_x, int tiles_y, int row0, int row1,
-                        int32_t* raw_counts, int64_t* raw_start, int2* tile_bins, int64_t* totals,
+                        int32_t* raw_counts, int64_t* raw_start, uint64_t* fill, int2* tile_bins, int64_t* totals,
                         int64_t* row_work, cudaStream_t s, int world, int rank) {
     note_launches(1);
     k_tile_counts<<<1, kCountThreads, 0, s>>>(tile_diff, tiles_x, tiles_y, row0, row1, raw_counts, raw_start,
-                                              tile_bins, totals, row_work, world, rank);
+                                              reinterpret_cast<unsigned long long*>(fill), tile_bins, totals,
+                                              row_work, world, rank);
 }
 
 void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x, int row0, int row1,
-                      const int64_t* raw_start, int32_t* fill, uint64_t* raw_keys, cudaStream_t s) {
+                      uint64_t* fill, uint64_t* raw_keys, cudaStream_t s) {
     if (n <= 0) return;
     note_launches(1);
-    k_emit_keys<<<(n + 255) / 256, 256, 0, s>>>(n, rects, depths, tiles_x, row0, row1, raw_start, fill, raw_keys);
+    k_emit_keys<<<(n + 255) / 256, 256, 0, s>>>(n, rects, depths, tiles_x, row0, row1,
+                                                reinterpret_cast<unsigned long long*>(fill), raw_keys);
 }
 
 void launch_tile_sort(int tile0, int num_tiles, const int32_t* raw_counts, const int64_t* raw_start,

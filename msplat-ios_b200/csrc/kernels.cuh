@@ -87,16 +87,17 @@ void launch_project_backward(const ProjBwdArgs& a, cudaStream_t s);
 
 // ---- binning (binning.cu) ---------------------------------------------------
 // Tile counts from the difference array, kept counts, exclusive scans and the
-// two totals. totals[0] = raw intersections (int64), totals[1] = kept. Only
+// two totals. totals[0] = raw intersections (int64), totals[1] = kept.
+// fill[t] receives raw_start[t]: the key counter of k_emit_keys. Only
 // tile rows [row0, row1) are binned; the other rows get empty ranges.
 // row_work (optional, [tiles_y]) receives a per-row work estimate over all
 // rows, for balancing tile-row bands across GPUs.
 void launch_tile_counts(const int32_t* tile_diff, int tiles_x, int tiles_y, int row0, int row1,
-                        int32_t* raw_counts, int64_t* raw_start, int2* tile_bins, int64_t* totals,
+                        int32_t* raw_counts, int64_t* raw_start, uint64_t* fill, int2* tile_bins, int64_t* totals,
                         int64_t* row_work, cudaStream_t s,
                         int world = 0, int rank = 0);
 void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x, int row0, int row1,
-                      const int64_t* raw_start, int32_t* fill, uint64_t* raw_keys, cudaStream_t s);
+                      uint64_t* fill, uint64_t* raw_keys, cudaStream_t s);
 void launch_tile_sort(int tile0, int num_tiles, const int32_t* raw_counts, const int64_t* raw_start,
                       const uint64_t* raw_keys, const int2* tile_bins, int32_t* gaussian_ids,
                       uint32_t* err, cudaStream_t s);
