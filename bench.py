@@ -53,10 +53,11 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--exchange", default="nccl", choices=["peers", "nccl"],
-                    help="multi-GPU parameter exchange: NCCL all-gathers with the colour groups overlapped with "
-                         "binning (default), or geometry all-gathered and colour read from its owner over NVLink "
-                         "(CUDA IPC)")
+    ap.add_argument("--exchange", default="rgb", choices=["peers", "nccl", "rgb"],
+                    help="multi-GPU parameter exchange: geometry all-gathered and the owners' colours for the "
+                         "next camera all-gathered instead of the colour coefficients (rgb, default); NCCL "
+                         "all-gathers of all groups with the colour groups overlapped with binning (nccl); or "
+                         "geometry all-gathered and colour read from its owner over NVLink (CUDA IPC, peers)")
     ap.add_argument("--render-frames", type=int, default=20,
                     help="render-only frames timed after the training steps (single GPU); 0 = skip")
     ap.add_argument("--cameras", type=int, default=0,
@@ -213,15 +214,38 @@ def run_ours(args, ws, rank, local):
         parts = torch.zeros(3, dtype=torch.float64, device=dev)
 
         side = torch.cuda.Stream(device=dev)
-        pending = [None]  # event: colour groups of the last step gathered
+        pending = [None]  # event: colour groups (or colours) of the last step gathered
+        rgb_full = None
+        if args.exchange == "rgb":
+            rgb_full = torch.zeros(plan.padded, 3, device=dev)
+            exchange = ("geometry all-gathered; each owner's clamped colours for the next camera all-gathered "
+                        "(12 B per Gaussian) instead of the colour coefficients")
+        have_rgb = [False]
+
+        def mstep(cam, gt, cam_next):
+            adam.step += 1
+            fb, pa = sharding.gpu_step_fns(B, g, cam, cfg.degree, bg, gt, l1, ld, SSIM_WEIGHT, adam, stats,
+                                           features_ready=pending[0], split_color=not use_peers,
+                                           peers=peers if use_peers else None,
+                                           rgb=rgb_full if have_rgb[0] else None)
+            colors_next = None if rgb_full is None else sharding.colors_fn(B, g, cam_next, cfg.degree, rgb_full)
+            pending[0] = sharding.sharded_step(dist, plan, fb, pa, rg, rg_shard, g.full, parts,
+                                               side_stream=None if use_peers else side,
+                                               skip_color=use_peers or rgb_full is not None,
+                                               colors_next=colors_next, rgb_full=rgb_full)
+            have_rgb[0] = rgb_full is not None
+
+        def prime_rgb(cam):
+            # colours for `cam` from the owners' current coefficients
+            torch.cuda.synchronize()
+            sharding.colors_fn(B, g, cam, cfg.degree, rgb_full)(plan.g_begin, plan.g_end)
+            rows = plan.slice_rows()
+            dist.all_gather_into_tensor(rgb_full, rgb_full[rows])
+            pending[0] = None
+            have_rgb[0] = True
 
         def step(k):
-            adam.step += 1
-            fb, pa = sharding.gpu_step_fns(B, g, cams[k % C], cfg.degree, bg, gts[k % C], l1, ld, SSIM_WEIGHT,
-                                           adam, stats, features_ready=pending[0], split_color=not use_peers,
-                                           peers=peers if use_peers else None)
-            pending[0] = sharding.sharded_step(dist, plan, fb, pa, rg, rg_shard, g.full, parts,
-                                               side_stream=None if use_peers else side, skip_color=use_peers)
+            mstep(cams[k % C], gts[k % C], cams[(k + 1) % C])
 
     for k in range(args.warmup):
         step(k)
@@ -367,18 +391,16 @@ def run_ours(args, ws, rank, local):
                 dev_gt[b].copy_(host_gt[k % len(host_gt)], non_blocking=True)
                 ready[b].record(copy_stream)
 
+        H = len(host_gt)
+        if rgb_full is not None:
+            prime_rgb(cams[0])
         dist.barrier()
         t0 = time.perf_counter()
         prefetch(0)
         for k in range(e2e_steps):
             b = k % 2
             stream.wait_event(ready[b])
-            adam.step += 1
-            fb, pa = sharding.gpu_step_fns(B, g, cams[k % C], cfg.degree, bg, dev_gt[b], l1, ld, SSIM_WEIGHT, adam,
-                                           stats, features_ready=pending[0], split_color=not use_peers,
-                                           peers=peers if use_peers else None)
-            pending[0] = sharding.sharded_step(dist, plan, fb, pa, rg, rg_shard, g.full, parts,
-                                               side_stream=None if use_peers else side, skip_color=use_peers)
+            mstep(cams[k % H], dev_gt[b], cams[(k + 1) % H])
             free[b].record(stream)
             if k + 1 < e2e_steps:
                 prefetch(k + 1)

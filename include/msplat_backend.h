@@ -207,6 +207,26 @@ int msplat_shard_project_backward_adam(const MsplatGaussians* g, const MsplatCam
                                        const float* raster_grads, int32_t g_begin, int32_t g_end,
                                        const MsplatAdamState* adam, float* xys_grad_norm, float* vis_counts,
                                        float* max_2d_size, void* stream);
+/* Colour exchange by clamped colour instead of SH coefficients (no
+ * reference counterpart; the colour evaluation is sh_coeffs_to_color,
+ * core/metal/msplat_metal.metal:756-823, as in the projection). The colour a
+ * Gaussian contributes to a step depends only on its own parameters and the
+ * camera, so the owner of a slice, right after its Adam update, evaluates the
+ * clamped colours max(SH + 0.5, 0) of its Gaussians [g_begin, g_end) for the
+ * NEXT step's camera into rgb[3 i .. 3 i + 2] (msplat_shard_colors); the ranks
+ * all-gather that [N, 3] buffer (12 B per Gaussian instead of 192 B of
+ * coefficients at SH degree 3) and the next step copies it
+ * (msplat_shard_forward_backward_rgb, after rgb_ready when non-null) where it
+ * would evaluate the SH. The copied colours are bit-identical to the
+ * evaluated ones. The colour coefficients then stay current only on their
+ * owner: gather them before exporting or checkpointing. */
+int msplat_shard_colors(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use, int32_t g_begin,
+                        int32_t g_end, float* rgb, void* stream);
+int msplat_shard_forward_backward_rgb(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
+                                      const float background[3], const float* gt, float lambda_l1,
+                                      float lambda_dist, float lambda_dssim, int32_t world, int32_t rank,
+                                      int32_t* tile_rows, float* raster_grads_out, double* loss_parts_dev,
+                                      const float* rgb, void* rgb_ready, void* stream);
 
 /* Densification: replaces msplat_densify (core/metal/bindings.h:143-157, impl
  * core/metal/msplat_metal.mm:1339-1594, kernels core/metal/msplat_metal.metal:

@@ -228,7 +228,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
                    float glob_scale, float clip, const float bg[3], bool ref_outputs, int row0, int row1,
                    cudaStream_t s, int balance_world = 0, int balance_rank = 0, int* owned0 = nullptr,
                    int* owned1 = nullptr, bool split_color = false, cudaEvent_t features_ready = nullptr,
-                   const MsplatPeerParams* peers = nullptr) {
+                   const MsplatPeerParams* peers = nullptr, const float* rgb_in = nullptr) {
     const int n = g->num_points;
     const int K = sh_rest_bases(g->sh_degree);
     const int tx = cam.tiles_x, ty = cam.tiles_y, T = tx * ty;
@@ -322,6 +322,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
         pc.pass = 2;
         pc.color_row0 = row0;
         pc.color_row1 = row1;
+        pc.rgb_in = rgb_in;
         if (peers) {
             pc.peer_world = peers->world;
             pc.peer_chunk = peers->chunk;
@@ -443,7 +444,8 @@ int shard_forward_backward_impl(const MsplatGaussians* g, const MsplatPeerParams
                                 int32_t degrees_to_use, const float background[3], const float* gt, float lambda_l1,
                                 float lambda_dist, float lambda_dssim, int32_t world, int32_t rank,
                                 int32_t* tile_rows, float* raster_grads_out, double* loss_parts_dev,
-                                void* features_ready, int32_t split_color, void* stream);
+                                void* features_ready, int32_t split_color, void* stream,
+                                const float* rgb_in);
 
 }  // namespace
 }  // namespace msplat
@@ -581,9 +583,9 @@ int msplat_shard_forward_backward(const MsplatGaussians* g, const MsplatCamera* 
                                   const float background[3], const float* gt, float lambda_l1, float lambda_dist,
                                   float lambda_dssim, int32_t world, int32_t rank, int32_t* tile_rows,
                                   float* raster_grads_out, double* loss_parts_dev, void* stream) {
-    return msplat_shard_forward_backward_after(g, cam, degrees_to_use, background, gt, lambda_l1, lambda_dist,
-                                               lambda_dssim, world, rank, tile_rows, raster_grads_out,
-                                               loss_parts_dev, nullptr, 0, stream);
+    return shard_forward_backward_impl(g, nullptr, cam, degrees_to_use, background, gt, lambda_l1, lambda_dist,
+                                       lambda_dssim, world, rank, tile_rows, raster_grads_out, loss_parts_dev,
+                                       nullptr, 0, stream, nullptr);
 }
 
 int msplat_shard_forward_backward_peers(const MsplatGaussians* g, const MsplatPeerParams* peers,
@@ -594,7 +596,7 @@ int msplat_shard_forward_backward_peers(const MsplatGaussians* g, const MsplatPe
                                         void* stream) {
     return shard_forward_backward_impl(g, peers, cam, degrees_to_use, background, gt, lambda_l1, lambda_dist,
                                        lambda_dssim, world, rank, tile_rows, raster_grads_out, loss_parts_dev,
-                                       nullptr, 0, stream);
+                                       nullptr, 0, stream, nullptr);
 }
 
 int msplat_shard_forward_backward_after(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
@@ -604,7 +606,39 @@ int msplat_shard_forward_backward_after(const MsplatGaussians* g, const MsplatCa
                                         void* features_ready, int32_t split_color, void* stream) {
     return shard_forward_backward_impl(g, nullptr, cam, degrees_to_use, background, gt, lambda_l1, lambda_dist,
                                        lambda_dssim, world, rank, tile_rows, raster_grads_out, loss_parts_dev,
-                                       features_ready, split_color, stream);
+                                       features_ready, split_color, stream, nullptr);
+}
+
+int msplat_shard_forward_backward_rgb(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
+                                      const float background[3], const float* gt, float lambda_l1,
+                                      float lambda_dist, float lambda_dssim, int32_t world, int32_t rank,
+                                      int32_t* tile_rows, float* raster_grads_out, double* loss_parts_dev,
+                                      const float* rgb, void* rgb_ready, void* stream) {
+    if (!rgb) {
+        msplat::set_last_error("null rgb");
+        return MSPLAT_ERR_ARGUMENT;
+    }
+    return shard_forward_backward_impl(g, nullptr, cam, degrees_to_use, background, gt, lambda_l1, lambda_dist,
+                                       lambda_dssim, world, rank, tile_rows, raster_grads_out, loss_parts_dev,
+                                       rgb_ready, 1, stream, rgb);
+}
+
+int msplat_shard_colors(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use, int32_t g_begin,
+                        int32_t g_end, float* rgb, void* stream) {
+    return guarded([&] {
+        check_inputs(g, cam, degrees_to_use);
+        if (!rgb) throw Error(MSPLAT_ERR_ARGUMENT, "null rgb");
+        if (g_begin < 0 || g_end > g->num_points || g_begin > g_end) throw Error(MSPLAT_ERR_ARGUMENT, "bad slice");
+        ProjFwdArgs pa{};
+        pa.n = g->num_points;
+        pa.means = g->means; pa.scales = g->scales; pa.quats = g->quats; pa.opacities = g->opacities;
+        pa.f_dc = g->features_dc; pa.f_rest = g->features_rest;
+        pa.rest_bases = sh_rest_bases(g->sh_degree);
+        pa.degrees_to_use = degrees_to_use;
+        pa.cam = make_cam(cam);
+        launch_shard_colors(pa, g_begin, g_end, rgb, static_cast<cudaStream_t>(stream));
+        CK(cudaGetLastError());
+    });
 }
 
 }  // extern "C"
@@ -615,7 +649,8 @@ int shard_forward_backward_impl(const MsplatGaussians* g, const MsplatPeerParams
                                 int32_t degrees_to_use, const float background[3], const float* gt, float lambda_l1,
                                 float lambda_dist, float lambda_dssim, int32_t world, int32_t rank,
                                 int32_t* tile_rows, float* raster_grads_out, double* loss_parts_dev,
-                                void* features_ready, int32_t split_color, void* stream) {
+                                void* features_ready, int32_t split_color, void* stream,
+                                const float* rgb_in) {
     return guarded([&] {
         if (peers) {
             if (peers->world < 2 || peers->world > MSPLAT_MAX_PEER_RANKS || peers->chunk <= 0 ||
@@ -640,7 +675,7 @@ int shard_forward_backward_impl(const MsplatGaussians* g, const MsplatPeerParams
         const int n = g->num_points;
         const int r0 = std::max(0, o0 - 1), r1 = std::min(cd.tiles_y, o1 + 1);
         stage_forward(w, g, cd, degrees_to_use, 1.0f, 0.01f, background, false, r0, r1, s, world, rank, &o0, &o1,
-                      split_color != 0, static_cast<cudaEvent_t>(features_ready), peers);
+                      split_color != 0, static_cast<cudaEvent_t>(features_ready), peers, rgb_in);
         tile_rows[0] = o0;
         tile_rows[1] = o1;
         const int p0 = std::min(cd.height, o0 * kTile), p1 = std::min(cd.height, o1 * kTile);

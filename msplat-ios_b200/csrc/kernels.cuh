@@ -60,8 +60,15 @@ struct ProjFwdArgs {
     // pass 2: colour only for Gaussians whose tile rectangle meets tile rows
     // [color_row0, color_row1) (color_row1 <= color_row0: all)
     int color_row0, color_row1;
+    // pass 2: with rgb_in ([N, 3], the clamped colours for this camera,
+    // computed by launch_shard_colors on the owners and all-gathered) the
+    // colour is copied instead of evaluated; raw colours are not available
+    const float* rgb_in;
 };
 void launch_project_forward(const ProjFwdArgs& a, cudaStream_t s);
+// Clamped colours max(SH + 0.5, 0) of Gaussians [g0, g1) for a.cam into
+// rgb_out[3 i .. 3 i + 2], with the SH code of the forward (bit-identical).
+void launch_shard_colors(const ProjFwdArgs& a, int g0, int g1, float* rgb_out, cudaStream_t s);
 
 struct ProjBwdArgs {
     int g_begin, g_end;      // Gaussians handled by this launch (a shard)

@@ -108,6 +108,11 @@ __global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
             const uint2 rc = a.rects[i];
             if ((int)(rc.y >> 16) <= a.color_row0 || (int)(rc.x >> 16) >= a.color_row1) return;
         }
+        if (a.rgb_in) {
+            float* r3 = reinterpret_cast<float*>(rec + 3);
+            r3[0] = a.rgb_in[3 * i]; r3[1] = a.rgb_in[3 * i + 1]; r3[2] = a.rgb_in[3 * i + 2];
+            return;
+        }
         float col[3], rgb[3];
         gaussian_color(a, pp, i, v3(pp.means[3 * i], pp.means[3 * i + 1], pp.means[3 * i + 2]), col, rgb);
         float* r3 = reinterpret_cast<float*>(rec + 3);
@@ -247,7 +252,27 @@ __global__ void __launch_bounds__(256) k_project_color_peers(ProjFwdArgs a) {
         for (int c = 0; c < 3; ++c) a.colors[3 * i + c] = col[c];
 }
 
+// Colours of an owner's slice for the next step's camera (multi-GPU): the
+// same evaluation as the forward's colour pass, for every Gaussian of the
+// slice (culled ones included; the forward copies only what it needs).
+__global__ void __launch_bounds__(256) k_shard_colors(ProjFwdArgs a, int g0, int g1, float* __restrict__ rgb_out) {
+    const int i = g0 + blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= g1) return;
+    const ParamPtrs pp = param_ptrs(a, i);
+    float col[3], rgb[3];
+    gaussian_color(a, pp, i, v3(pp.means[3 * i], pp.means[3 * i + 1], pp.means[3 * i + 2]), col, rgb);
+    rgb_out[3 * i] = rgb[0];
+    rgb_out[3 * i + 1] = rgb[1];
+    rgb_out[3 * i + 2] = rgb[2];
+}
+
 }  // namespace
+
+void launch_shard_colors(const ProjFwdArgs& a, int g0, int g1, float* rgb_out, cudaStream_t s) {
+    if (g1 <= g0) return;
+    note_launches(1);
+    k_shard_colors<<<(g1 - g0 + 255) / 256, 256, 0, s>>>(a, g0, g1, rgb_out);
+}
 
 void launch_project_forward(const ProjFwdArgs& a, cudaStream_t s) {
     if (a.n <= 0) return;

@@ -95,6 +95,10 @@ def load():
     L.msplat_shard_forward_backward_peers.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatPeerParams),
                                                       C.POINTER(MsplatCamera), i32, fp3, vp, f, f, f, i32, i32,
                                                       C.POINTER(C.c_int32), vp, vp, vp]
+    L.msplat_shard_forward_backward_rgb.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, fp3,
+                                                    vp, f, f, f, i32, i32, C.POINTER(C.c_int32), vp, vp, vp, vp,
+                                                    vp]
+    L.msplat_shard_colors.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, i32, i32, vp, vp]
     L.msplat_device_alloc.argtypes = [C.c_uint64, C.POINTER(C.c_void_p)]
     L.msplat_device_free.argtypes = [vp]
     L.msplat_ipc_handle.argtypes = [vp, C.c_char * 64]
@@ -123,7 +127,8 @@ def load():
     L.msplat_last_error.restype = C.c_char_p
     for name in ("msplat_render", "msplat_train_step_2dgs", "msplat_fused_adam", "msplat_train_step_fused",
                  "msplat_shard_forward_backward", "msplat_shard_forward_backward_after",
-                 "msplat_shard_forward_backward_peers", "msplat_device_alloc", "msplat_device_free",
+                 "msplat_shard_forward_backward_peers", "msplat_shard_forward_backward_rgb", "msplat_shard_colors",
+                 "msplat_device_alloc", "msplat_device_free",
                  "msplat_ipc_handle", "msplat_ipc_open", "msplat_ipc_close",
                  "msplat_shard_project_backward_adam", "msplat_last_tensor",
                  "msplat_densify_plan", "msplat_densify_apply", "msplat_reset_opacity"):
@@ -274,6 +279,30 @@ def shard_forward_backward(g, cam, degrees_to_use, background, gt, lambda_l1, la
                                                       tr, _ptr(raster_grads), _ptr(loss_parts), ev,
                                                       1 if split_color else 0, _stream(stream)))
     return tr[0], tr[1]
+
+
+def shard_forward_backward_rgb(g, cam, degrees_to_use, background, gt, lambda_l1, lambda_dist, lambda_dssim,
+                               raster_grads, loss_parts, rgb, world=0, rank=0, rows=(0, 0), stream=None,
+                               rgb_ready=None):
+    """shard_forward_backward with the colours copied from rgb ([N, 3], the
+    clamped colours for this camera that the owners computed with
+    shard_colors and the ranks all-gathered), after rgb_ready (a
+    torch.cuda.Event, may be None)."""
+    gs = g.struct()
+    tr = (C.c_int32 * 2)(int(rows[0]), int(rows[1]))
+    ev = None if rgb_ready is None else C.c_void_p(rgb_ready.cuda_event)
+    _check(load().msplat_shard_forward_backward_rgb(C.byref(gs), C.byref(cam), degrees_to_use, _bg(background),
+                                                    _ptr(gt), lambda_l1, lambda_dist, lambda_dssim, world, rank,
+                                                    tr, _ptr(raster_grads), _ptr(loss_parts), _ptr(rgb), ev,
+                                                    _stream(stream)))
+    return tr[0], tr[1]
+
+
+def shard_colors(g, cam, degrees_to_use, g0, g1, rgb, stream=None):
+    """Clamped SH colours of Gaussians [g0, g1) for camera cam into rows g0..g1
+    of rgb (an [>= g1, 3] float tensor): msplat_shard_colors."""
+    gs = g.struct()
+    _check(load().msplat_shard_colors(C.byref(gs), C.byref(cam), degrees_to_use, g0, g1, _ptr(rgb), _stream(stream)))
 
 
 def shard_project_backward_adam(g, cam, degrees_to_use, raster_grads, g0, g1, adam: AdamState, stats=None,

@@ -148,7 +148,7 @@ class PeerParams:
 
 
 def sharded_step(dist, plan: ShardPlan, forward_backward, project_adam, rg, rg_shard, param_fulls, parts,
-                 side_stream=None, skip_color=False):
+                 side_stream=None, skip_color=False, colors_next=None, rgb_full=None):
     """One training step across ranks.
 
     forward_backward(plan, rg, parts): fills rg [padded, 16] with this rank's
@@ -164,16 +164,24 @@ def sharded_step(dist, plan: ShardPlan, forward_backward, project_adam, rg, rg_s
         the next step's forward_backward binds the geometry while the
         transfer runs and waits for the event only before its colour pass.
     skip_color: the colour groups are not gathered at all (the ranks read
-        them from their owners, PeerParams); the geometry all-gather and the
-        loss all-reduce after Adam order every owner's update before the
-        next step's reads.
+        them from their owners, PeerParams, or exchange colours instead,
+        below); the geometry all-gather and the loss all-reduce after Adam
+        order every owner's update before the next step's reads.
+    colors_next(g_begin, g_end), rgb_full [padded, 3]: colour exchange. After
+        Adam the owner writes the clamped colours of its slice for the next
+        step's camera into rgb_full (msplat_shard_colors); rgb_full is
+        all-gathered on side_stream (12 B per Gaussian instead of the 192 B of
+        colour coefficients) and the returned event marks its arrival. Use
+        with skip_color=True.
     Every rank issues the collectives in the same order.
     """
     forward_backward(plan, rg, parts)
     dist.reduce_scatter_tensor(rg_shard, rg, op=dist.ReduceOp.SUM)
     project_adam(plan.g_begin, plan.g_end, rg_shard)
     rows = plan.slice_rows()
-    late = []
+    if colors_next is not None:
+        colors_next(plan.g_begin, plan.g_end)
+    late = [rgb_full] if rgb_full is not None else []
     for k, full in enumerate(param_fulls):
         if full.numel() == 0 or (skip_color and k in COLOR_GROUPS):
             continue
@@ -183,6 +191,10 @@ def sharded_step(dist, plan: ShardPlan, forward_backward, project_adam, rg, rg_s
         dist.all_gather_into_tensor(full, full[rows])
     dist.all_reduce(parts)
     if not late:
+        return None
+    if side_stream is None:
+        for full in late:
+            dist.all_gather_into_tensor(full, full[rows])
         return None
     import torch
     adam_done = torch.cuda.Event()
@@ -204,13 +216,21 @@ def loss_from_parts(parts, lambda_dssim: float, width: int, height: int) -> floa
 
 
 def gpu_step_fns(B, g, cam, degree, bg, gt, lambda_l1, lambda_dist, lambda_dssim, adam, stats, balance=True,
-                 features_ready=None, split_color=False, peers=None):
+                 features_ready=None, split_color=False, peers=None, rgb=None):
     """The two callables of sharded_step bound to the C ABI (msplat_shard_*).
     With balance the library picks work-balanced tile-row bands each step;
     with split_color the colour pass waits for features_ready (the event the
     previous sharded_step returned); with peers (a PeerParams) the projection
-    reads every Gaussian from its owner rank."""
+    reads every Gaussian from its owner rank; with rgb ([padded, 3], gathered
+    colours for this camera) the colour pass copies them, after
+    features_ready."""
     def forward_backward(plan, rg, parts):
+        if rgb is not None:
+            kw = dict(world=plan.world, rank=plan.rank) if balance else dict(rows=(plan.row0, plan.row1))
+            plan.row0, plan.row1 = B.shard_forward_backward_rgb(g, cam, degree, bg, gt, lambda_l1, lambda_dist,
+                                                                lambda_dssim, rg, parts, rgb, rgb_ready=features_ready,
+                                                                **kw)
+            return
         if peers is not None:
             plan.row0, plan.row1 = B.shard_forward_backward_peers(g, peers.struct, cam, degree, bg, gt, lambda_l1,
                                                                   lambda_dist, lambda_dssim, rg, parts,
@@ -231,3 +251,11 @@ def gpu_step_fns(B, g, cam, degree, bg, gt, lambda_l1, lambda_dist, lambda_dssim
                                       stats=stats, count_step=False)
 
     return forward_backward, project_adam
+
+
+def colors_fn(B, g, cam_next, degree, rgb_full):
+    """The colors_next callable of sharded_step: the clamped colours of the
+    owner's slice for the next step's camera (msplat_shard_colors)."""
+    def colors_next(g0, g1):
+        B.shard_colors(g, cam_next, degree, g0, g1, rgb_full)
+    return colors_next

@@ -2,9 +2,12 @@
 
 Each rank runs two sharded training steps (msplat/sharding.py) on a small
 scene, exchanging parameters either with NCCL all-gathers (colour groups on a
-side stream while the next step bins; MSPLAT_EXCHANGE=nccl) or with the
+side stream while the next step bins; MSPLAT_EXCHANGE=nccl), with the
 geometry all-gathered and the colour read from its owner rank through CUDA
-IPC (MSPLAT_EXCHANGE=peers); rank 0 also runs the same two steps with the single-GPU fused
+IPC (MSPLAT_EXCHANGE=peers), or with the geometry all-gathered and the
+owners' clamped colours for the next camera all-gathered instead of the
+colour coefficients (MSPLAT_EXCHANGE=rgb); rank 0 also runs the same two
+steps with the single-GPU fused
 step on a private copy and compares the parameters. Prints "MULTIGPU OK" on
 success (rank 0) and exits non-zero otherwise.
 """
@@ -47,6 +50,7 @@ def main():
         adam = B.AdamState(g)
     else:
         sharding.pad_gaussians(g, plan.padded)
+    rgb_full = torch.zeros(plan.padded, 3, device=dev) if exchange == "rgb" else None
     rg = torch.zeros(plan.padded, 16, device=dev)
     rg_shard = torch.zeros(plan.chunk, 16, device=dev)
     parts = torch.zeros(3, dtype=torch.float64, device=dev)
@@ -54,15 +58,19 @@ def main():
     # gathered on a side stream while the next step bins its geometry
     side = torch.cuda.Stream(device=dev)
     ready = None
-    for _ in range(2):
+    for step in range(2):
         adam.step += 1
         fb, pa = sharding.gpu_step_fns(B, g, cam, case.degree, case.bg, gt, 0.8, 0.0, 0.2, adam, None,
-                                       features_ready=ready, split_color=peers is None, peers=peers)
+                                       features_ready=ready, split_color=peers is None, peers=peers,
+                                       rgb=rgb_full if (rgb_full is not None and step > 0) else None)
+        colors_next = None if rgb_full is None else sharding.colors_fn(B, g, cam, case.degree, rgb_full)
         ready = sharding.sharded_step(dist, plan, fb, pa, rg, rg_shard, g.full, parts,
-                                      side_stream=None if peers else side, skip_color=peers is not None)
+                                      side_stream=None if peers else side,
+                                      skip_color=peers is not None or rgb_full is not None,
+                                      colors_next=colors_next, rgb_full=rgb_full)
     torch.cuda.synchronize()
     loss_sh = sharding.loss_from_parts(parts.cpu().numpy(), 0.2, cfg.width, cfg.height)
-    if peers is not None:
+    if peers is not None or rgb_full is not None:
         # each rank's colour buffers are current only in the rows it owns:
         # gather them once to compare the whole parameter set
         rows = plan.slice_rows()
@@ -74,7 +82,8 @@ def main():
             gathered.append(out[:n])
         got = [t.cpu().numpy() for t in gathered]
         torch.cuda.synchronize()
-        peers.close()
+        if peers is not None:
+            peers.close()
     else:
         got = [t.cpu().numpy() for t in g.groups()]
     ok = True

@@ -5,7 +5,9 @@ with NCCL. Here two gloo ranks run it with the CPU oracle standing in for the
 CUDA kernels: each rank back-propagates only its own tile rows, the raster
 gradients are reduce-scattered, each rank applies the projection VJP and Adam
 to its slice, and the parameters are all-gathered. The result must equal one
-single-process oracle step.
+single-process oracle step. The colour exchange (mode "rgb") gathers each
+owner's clamped colours for the next camera instead of the colour
+coefficients; those must equal the oracle's colours of the updated scene.
 """
 import os
 import socket
@@ -34,7 +36,7 @@ def _free_port():
     return port
 
 
-def _rank_main(rank, ws, port, out_path):
+def _rank_main(rank, ws, port, out_path, mode="coeffs"):
     import torch
     import torch.distributed as dist
 
@@ -94,8 +96,20 @@ def _rank_main(rank, ws, port, out_path):
     rg = torch.zeros(plan.padded, sharding.GRAD_STRIDE)
     rg_shard = torch.zeros(plan.chunk, sharding.GRAD_STRIDE)
     parts = torch.zeros(3, dtype=torch.float64)
-    sharding.sharded_step(dist, plan, forward_backward, project_adam, rg, rg_shard, fulls, parts)
-    np.savez(out_path + f".{rank}.npz", *[f[:n].numpy() for f in fulls], parts=parts.numpy())
+    colors_next, rgb_full = None, None
+    if mode == "rgb":
+        rgb_full = torch.zeros(plan.padded, 3)
+        cam_next = Case("sh3_small", cam_index=1).ocam
+
+        def colors_next(g0, g1):
+            sl = slice(g0, g1)
+            pn = O.project_forward(params[0][sl], params[1][sl], params[2][sl], params[5][sl], params[3][sl],
+                                   params[4][sl], deg, deg, cam_next)
+            rgb_full[sl] = torch.from_numpy(np.maximum(pn["colors"] + np.float32(0.5), np.float32(0.0)))
+    sharding.sharded_step(dist, plan, forward_backward, project_adam, rg, rg_shard, fulls, parts,
+                          skip_color=mode == "rgb", colors_next=colors_next, rgb_full=rgb_full)
+    extra = {} if rgb_full is None else {"rgb": rgb_full[:n].numpy(), "g_begin": plan.g_begin, "g_end": plan.g_end}
+    np.savez(out_path + f".{rank}.npz", *[f[:n].numpy() for f in fulls], parts=parts.numpy(), **extra)
     dist.destroy_process_group()
 
 
@@ -122,3 +136,35 @@ def test_two_gloo_ranks_equal_one_oracle_step(tmp_path):
         assert ok.mean() > 0.9995, (k, ok.mean())
     l1_total = 0.8 * np.abs(ref["out_img"] - case.gt).astype(np.float64).sum() / ref["out_img"].size
     assert abs(res[0]["parts"][0] - l1_total) < 1e-9
+
+
+def test_two_gloo_ranks_exchange_next_camera_colours(tmp_path):
+    """Mode rgb: the colour coefficients stay with their owners and every rank
+    ends the step holding the clamped colours of all Gaussians for the next
+    camera, equal to the oracle's colours of the updated scene."""
+    import torch.multiprocessing as mp
+
+    from _cases import Case
+    from oracle import oracle as O
+    ws = 2
+    out = str(tmp_path / "shard_rgb")
+    mp.start_processes(_rank_main, args=(ws, _free_port(), out, "rgb"), nprocs=ws, start_method="spawn")
+    res = [np.load(out + f".{r}.npz") for r in range(ws)]
+    case = Case("sh3_small")
+    tr = O.OracleTrainer(case.scene.params(), case.degree)
+    tr.step(case.ocam, case.gt, case.bg)
+    nxt = Case("sh3_small", cam_index=1).ocam
+    pn = O.project_forward(tr.means, tr.scales, tr.quats, tr.opac, tr.f_dc, tr.f_rest, case.degree, case.degree, nxt)
+    want = np.maximum(pn["colors"] + np.float32(0.5), np.float32(0.0))
+    assert np.array_equal(res[0]["rgb"], res[1]["rgb"]), "gathered colours differ between ranks"
+    ok = np.isclose(res[0]["rgb"], want, rtol=1e-5, atol=1e-6)
+    assert ok.mean() > 0.999, ok.mean()
+    init = [case.scene.f_dc, case.scene.f_rest]
+    for r in range(ws):
+        g0, g1 = int(res[r]["g_begin"]), int(res[r]["g_end"])
+        for k, a0 in ((3, init[0]), (4, init[1])):
+            got = res[r][f"arr_{k}"]
+            others = np.ones(got.shape[0], bool)
+            others[g0:g1] = False
+            assert np.array_equal(got[others], np.asarray(a0, np.float32)[others]), "colour groups were gathered"
+            assert not np.array_equal(got[g0:g1], np.asarray(a0, np.float32)[g0:g1]), "owner slice not updated"
