@@ -195,8 +195,10 @@ int sh_rest_bases(int degree) { return (degree + 1) * (degree + 1) - 1; }
 
 void check_inputs(const MsplatGaussians* g, const MsplatCamera* cam, int degrees_to_use) {
     if (!g || !cam) throw Error(MSPLAT_ERR_ARGUMENT, "null gaussians or camera");
-    if (g->num_points < 0 || g->num_points > (1 << 24))
-        throw Error(MSPLAT_ERR_ARGUMENT, "num_points must be in [0, 2^24]");
+    // ids take 25 bits at most (the overfull-tile select reads 32-bit ids in
+    // three digits; per-Gaussian int offsets stay below 2^31 up to 2^25)
+    if (g->num_points < 0 || g->num_points > (1 << 25))
+        throw Error(MSPLAT_ERR_ARGUMENT, "num_points must be in [0, 2^25]");
     if (g->sh_degree < 0 || g->sh_degree > 3) throw Error(MSPLAT_ERR_ARGUMENT, "sh_degree must be 0..3");
     if (degrees_to_use < 0 || degrees_to_use > g->sh_degree)
         throw Error(MSPLAT_ERR_ARGUMENT, "degrees_to_use must be in [0, sh_degree]");
@@ -312,7 +314,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
                      w.raw_keys.as<uint64_t>(), s);
     mark(w, kStSort, s);
     launch_tile_sort(row0 * tx, (row1 - row0) * tx, w.raw_counts.as<int32_t>(), w.raw_start.as<int64_t>(), w.raw_keys.as<uint64_t>(),
-                     w.tile_bins.as<int2>(), w.gaussian_ids.as<int32_t>(), w.err.as<uint32_t>(), s);
+                     w.tile_bins.as<int2>(), w.gaussian_ids.as<int32_t>(), w.err.as<uint32_t>(), n, s);
     if (split_color) {
         // colour after binning: the caller may still be gathering features_dc /
         // features_rest until features_ready

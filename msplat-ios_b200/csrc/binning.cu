@@ -425,7 +425,7 @@ __device__ __forceinline__ void find_digit(const int* hist, int need, int* s_dig
 __global__ void __launch_bounds__(kSortThreads)
 k_tile_sort(const int32_t* __restrict__ raw_counts, const int64_t* __restrict__ raw_start,
             const uint64_t* __restrict__ keys, const int2* __restrict__ tile_bins,
-            int32_t* __restrict__ gaussian_ids, int tile0, uint32_t* err) {
+            int32_t* __restrict__ gaussian_ids, int tile0, uint32_t* err, int num_ids) {
     __shared__ uint64_t data[kMaxTileElems];
     __shared__ int hist[kSelectBins];
     __shared__ uint32_t s_prefix;
@@ -442,25 +442,31 @@ k_tile_sort(const int32_t* __restrict__ raw_counts, const int64_t* __restrict__ 
             sort_and_store<8, kSortThreads>(src, count, threadIdx.x, data, dst, count);
         return;
     }
-    // Radix select on the 24-bit Gaussian id (two 12-bit digits): find theta
-    // such that exactly 2048 ids of this tile are <= theta.
+    // Radix select on the Gaussian id, most significant digit first: bits
+    // 24..31 (only when there are more than 2^24 Gaussians), 12..23, 0..11.
+    // Each pass histograms the ids that share the digits chosen so far and
+    // picks the digit below which fewer than `need` ids remain; the result
+    // theta is the id such that exactly 2048 ids of this tile are <= theta.
     if (threadIdx.x == 0 && err) atomicOr(err, kErrTileOverflow);
-    for (int q = threadIdx.x; q < kSelectBins; q += kSortThreads) hist[q] = 0;
-    __syncthreads();
-    for (int q = threadIdx.x; q < count; q += kSortThreads) atomicAdd(&hist[((uint32_t)src[q] >> 12) & 4095], 1);
-    __syncthreads();
-    find_digit(hist, kMaxTileElems, &s_digit, &s_need);
-    const uint32_t hi_digit = (uint32_t)s_digit;
-    const int need2 = s_need;
-    for (int q = threadIdx.x; q < kSelectBins; q += kSortThreads) hist[q] = 0;
-    __syncthreads();
-    for (int q = threadIdx.x; q < count; q += kSortThreads) {
-        const uint32_t id = (uint32_t)src[q];
-        if (((id >> 12) & 4095) == hi_digit) atomicAdd(&hist[id & 4095], 1);
+    uint32_t prefix = 0;  // digits chosen so far
+    int need = kMaxTileElems;
+    for (int level = num_ids > (1 << 24) ? 0 : 1; level < 3; ++level) {
+        const int shift = level == 0 ? 24 : (level == 1 ? 12 : 0);
+        const uint32_t mask = level == 0 ? 255u : 4095u;
+        const int above = shift + (level == 0 ? 8 : 12);  // bits above this digit: fixed by prefix
+        for (int q = threadIdx.x; q < kSelectBins; q += kSortThreads) hist[q] = 0;
+        __syncthreads();
+        for (int q = threadIdx.x; q < count; q += kSortThreads) {
+            const uint32_t id = (uint32_t)src[q];
+            if (((uint64_t)id >> above) == prefix) atomicAdd(&hist[(id >> shift) & mask], 1);
+        }
+        __syncthreads();
+        find_digit(hist, need, &s_digit, &s_need);
+        prefix = (prefix << (level == 0 ? 8 : 12)) | (uint32_t)s_digit;
+        need = s_need;
+        __syncthreads();
     }
-    __syncthreads();
-    find_digit(hist, need2, &s_digit, &s_need);
-    if (threadIdx.x == 0) s_prefix = (hi_digit << 12) | (uint32_t)s_digit;
+    if (threadIdx.x == 0) s_prefix = prefix;
     __syncthreads();
     const uint32_t theta = s_prefix;
     if (threadIdx.x == 0) s_count = 0;
@@ -509,7 +515,7 @@ void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_
 
 void launch_tile_sort(int tile0, int num_tiles, const int32_t* raw_counts, const int64_t* raw_start,
                       const uint64_t* raw_keys, const int2* tile_bins, int32_t* gaussian_ids, uint32_t* err,
-                      cudaStream_t s) {
+                      int num_gaussians, cudaStream_t s) {
     if (num_tiles <= 0) return;
     note_launches(2);
     const int warps = kSortThreads / 32;
@@ -517,7 +523,7 @@ void launch_tile_sort(int tile0, int num_tiles, const int32_t* raw_counts, const
                                                                               tile_bins, gaussian_ids, tile0,
                                                                               num_tiles);
     k_tile_sort<<<num_tiles, kSortThreads, 0, s>>>(raw_counts, raw_start, raw_keys, tile_bins, gaussian_ids, tile0,
-                                                    err);
+                                                    err, num_gaussians);
 }
 
 }  // namespace msplat

@@ -105,9 +105,11 @@ void launch_tile_counts(const int32_t* tile_diff, int tiles_x, int tiles_y, int 
                         int world = 0, int rank = 0);
 void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x, int row0, int row1,
                       uint64_t* fill, uint64_t* raw_keys, cudaStream_t s);
+// num_gaussians bounds the ids (the overfull-tile select needs a third digit
+// pass above 2^24 Gaussians).
 void launch_tile_sort(int tile0, int num_tiles, const int32_t* raw_counts, const int64_t* raw_start,
                       const uint64_t* raw_keys, const int2* tile_bins, int32_t* gaussian_ids,
-                      uint32_t* err, cudaStream_t s);
+                      uint32_t* err, int num_gaussians, cudaStream_t s);
 
 // ---- rasterisation (rasterize.cu) -------------------------------------------
 struct RasterFwdArgs {

@@ -80,3 +80,23 @@ def test_training_step_on_an_empty_scene():
     img = np.broadcast_to(np.float32(S.BACKGROUND), gt.shape).copy()
     want = O.loss_ssim(img, gt, np.zeros(gt.shape[:2], np.float32), 0.8, 0.0, 0.2)["loss"]
     assert abs(float(loss.cpu()[0]) - want) <= 1e-5 * abs(want)
+
+
+def test_overfull_tiles_with_more_than_2_24_gaussians():
+    """Ids above 2^24 take part in the overfull-tile selection (the 2048 lowest
+    ids of a tile): a third radix digit keeps them from aliasing lower ids."""
+    B = _B()
+    n = 16_900_000  # > 2^24 = 16,777,216
+    cfg = S.small_config(n, 0, 32, 32, num_cameras=1)
+    sc = S.make_scene(cfg, seed=3)
+    fx, fy, cx, cy = sc.intrinsics
+    ocam = O.prepare_cam(sc.cam_to_world[0], fx, fy, cx, cy, 32, 32)
+    p = O.project_forward(*sc.params(), 0, 0, ocam)
+    bins = O.bin_and_sort(p, ocam)
+    assert bins["raw_counts"].min() > 2048 and (p["radii"][1 << 24:] > 0).any()
+    g = B.DeviceGaussians(*sc.params(), sh_degree=0)
+    B.render(g, B.camera_from_oracle(ocam), 0, S.BACKGROUND)
+    torch.cuda.synchronize()
+    assert B.last_num_intersections() == bins["kept"]
+    np.testing.assert_array_equal(B.last_tensor("tile_bins").cpu().numpy(), bins["tile_bins"])
+    np.testing.assert_array_equal(B.last_tensor("gaussian_ids").cpu().numpy(), bins["gaussian_ids"])
