@@ -76,7 +76,8 @@ struct Workspace {
     Buf dL_dmean3D, dL_dscale, dL_dquat, dL_dmean2D, dL_dfeatures_dc, dL_dfeatures_rest, dL_dopacity;
     Buf dL_dtransMat, dL_dnormal3D, dL_dcolors;
     // per tile / intersection
-    Buf tile_diff, raw_counts, raw_start, tile_bins, fill, raw_keys, gaussian_ids, blend_mask;
+    Buf tile_diff, chunk_counts, raw_true, id_limit, raw_counts, raw_start, tile_bins, fill, raw_keys, gaussian_ids,
+        blend_mask;
     // per pixel
     Buf final_Ts, final_idx, out_img, out_depth, out_normal, out_alpha, out_median, out_dist, dL_dout_img;
     // scalars
@@ -100,7 +101,7 @@ struct Workspace {
         Buf* all[] = {&records, &cull, &rects, &depths, &radii, &raster_grads, &xys, &transmats, &num_tiles_hit,
                       &normal_opacity, &colors, &aabb, &dL_dmean3D, &dL_dscale, &dL_dquat, &dL_dmean2D,
                       &dL_dfeatures_dc, &dL_dfeatures_rest, &dL_dopacity, &dL_dtransMat, &dL_dnormal3D,
-                      &dL_dcolors, &tile_diff, &raw_counts, &raw_start, &tile_bins, &fill, &raw_keys,
+                      &dL_dcolors, &tile_diff, &chunk_counts, &raw_true, &id_limit, &raw_counts, &raw_start, &tile_bins, &fill, &raw_keys,
                       &gaussian_ids, &blend_mask, &final_Ts, &final_idx, &out_img, &out_depth, &out_normal, &out_alpha,
                       &out_median, &out_dist, &dL_dout_img, &loss_partials, &loss_out, &loss_f, &err, &totals, &row_work};
         for (Buf* b : all) b->release();
@@ -250,7 +251,11 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
         w.xys.ensure(nn * 2 * 4); w.transmats.ensure(nn * 9 * 4); w.num_tiles_hit.ensure(nn * 4);
         w.normal_opacity.ensure(nn * 4 * 4); w.colors.ensure(nn * 3 * 4); w.aabb.ensure(nn * 2 * 4);
     }
-    w.tile_diff.ensure((size_t)(tx + 1) * (ty + 1) * 4);
+    const size_t diff_bytes = (size_t)kIdChunks * (tx + 1) * (ty + 1) * 4;
+    w.tile_diff.ensure(diff_bytes);
+    w.chunk_counts.ensure((size_t)kIdChunks * T * 4);
+    w.raw_true.ensure((size_t)T * 4);
+    w.id_limit.ensure((size_t)T * 4);
     w.raw_counts.ensure((size_t)T * 4);
     w.raw_start.ensure((size_t)T * 8);
     w.tile_bins.ensure((size_t)T * sizeof(int2));
@@ -261,7 +266,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     w.out_depth.ensure(P * 4); w.out_normal.ensure(P * 3 * 4); w.out_alpha.ensure(P * 4);
     w.out_median.ensure(P * 4); w.out_dist.ensure(P * 4);
 
-    CK(cudaMemsetAsync(w.tile_diff.p, 0, (size_t)(tx + 1) * (ty + 1) * 4, s));
+    CK(cudaMemsetAsync(w.tile_diff.p, 0, diff_bytes, s));
     CK(cudaMemsetAsync(w.err.p, 0, sizeof(uint32_t), s));
 
     ProjFwdArgs pa{};
@@ -279,6 +284,8 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     pa.cam = cam;
     pa.records = w.records.as<float4>(); pa.cull = w.cull.as<float4>(); pa.rects = w.rects.as<uint2>(); pa.depths = w.depths.as<float>();
     pa.radii = w.radii.as<int32_t>(); pa.tile_diff = w.tile_diff.as<int32_t>();
+    const int id_chunk = std::max(1, (n + kIdChunks - 1) / kIdChunks);
+    pa.id_chunk = id_chunk;
     if (ref_outputs) {
         pa.xys = w.xys.as<float>(); pa.transmats = w.transmats.as<float>();
         pa.num_tiles_hit = w.num_tiles_hit.as<int32_t>(); pa.normal_opacity = w.normal_opacity.as<float>();
@@ -288,9 +295,11 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     launch_project_forward(pa, s);
     mark(w, kStCounts, s);
     if (balance_world > 0) w.row_work.ensure((size_t)ty * sizeof(int64_t));
-    launch_tile_counts(w.tile_diff.as<int32_t>(), tx, ty, row0, row1, w.raw_counts.as<int32_t>(),
+    launch_tile_counts(w.tile_diff.as<int32_t>(), id_chunk, w.chunk_counts.as<int32_t>(), w.raw_true.as<int32_t>(),
+                       w.id_limit.as<int32_t>(), tx, ty, row0, row1, w.raw_counts.as<int32_t>(),
                        w.raw_start.as<int64_t>(), w.fill.as<uint64_t>(), w.tile_bins.as<int2>(), w.totals.as<int64_t>(),
-                       balance_world > 0 ? w.row_work.as<int64_t>() : nullptr, s, balance_world, balance_rank);
+                       balance_world > 0 ? w.row_work.as<int64_t>() : nullptr, w.err.as<uint32_t>(), s, balance_world,
+                       balance_rank);
     // The one host read of the step: buffer sizes for the intersections (and
     // the band the kernel chose, when balancing).
     CK(cudaMemcpyAsync(w.h_totals, w.totals.p, 4 * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
@@ -310,8 +319,8 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     w.gaussian_ids.ensure((size_t)(kept > 0 ? kept : 1) * sizeof(int32_t));
     w.blend_mask.ensure((size_t)(kept > 0 ? kept : 1));
     mark(w, kStEmit, s);
-    launch_emit_keys(n, w.rects.as<uint2>(), w.depths.as<float>(), tx, row0, row1, w.fill.as<uint64_t>(),
-                     w.raw_keys.as<uint64_t>(), s);
+    launch_emit_keys(n, w.rects.as<uint2>(), w.depths.as<float>(), tx, row0, row1, w.id_limit.as<int32_t>(),
+                     w.fill.as<uint64_t>(), w.raw_keys.as<uint64_t>(), s);
     mark(w, kStSort, s);
     launch_tile_sort(row0 * tx, (row1 - row0) * tx, w.raw_counts.as<int32_t>(), w.raw_start.as<int64_t>(), w.raw_keys.as<uint64_t>(),
                      w.tile_bins.as<int2>(), w.gaussian_ids.as<int32_t>(), w.err.as<uint32_t>(), n, s);
@@ -804,7 +813,7 @@ int msplat_last_tensor(const char* name, MsplatTensorRef* out) {
         else if (nm == "radii") set(w.radii, 1, {n}, px);
         else if (nm == "depths") set(w.depths, 0, {n}, px);
         else if (nm == "tile_bins") set(w.tile_bins, 1, {T, 2}, px);
-        else if (nm == "raw_tile_counts") set(w.raw_counts, 1, {T}, px);
+        else if (nm == "raw_tile_counts") set(w.raw_true, 1, {T}, px);
         else if (nm == "gaussian_ids") set(w.gaussian_ids, 1, {w.kept}, px);
         else if (nm == "xys") set(w.xys, 0, {n, 2}, rp);
         else if (nm == "transMats") set(w.transmats, 0, {n, 9}, rp);

@@ -20,6 +20,8 @@
 //      per tile up to 512 keys, one CTA above that; for an overfull tile the
 //      CTA first keeps the 2048 lowest Gaussian ids (a three-pass radix select
 //      on the id bits). Output: the sorted Gaussian ids.
+#include <climits>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -47,52 +49,95 @@ __device__ int band_cut(const int64_t* work, int ty, double total, int r, int wo
     return y;
 }
 
-// Per-tile intersection counts from the 2-D difference array, clamped kept
-// counts and both exclusive scans, for tile rows [row0, row1) (other rows get
-// zero counts). With world > 0 the rows are chosen here: band `rank` of
-// `world` work-balanced bands [o0, o1) plus a one-row halo; the band goes to
-// totals[2..3] next to the raw and kept totals (totals[0..1]).
+// Per-tile intersection counts of one id chunk (blockIdx.x) from its 2-D
+// difference array: column prefix over y (one thread per tile column), then
+// row prefix over x (one warp per tile row, 32 columns at a time with a
+// shuffle scan).
 __global__ void __launch_bounds__(kCountThreads)
-k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int row0, int row1, int32_t* __restrict__ raw_counts,
-              int64_t* __restrict__ raw_start, unsigned long long* __restrict__ fill, int2* __restrict__ tile_bins,
-              int64_t* __restrict__ totals, int64_t* __restrict__ row_work, int world, int rank) {
-    __shared__ int s_rows[2];
+k_chunk_counts(const int32_t* __restrict__ diff, int tx, int ty, int32_t* __restrict__ chunk_counts) {
     const int dw = tx + 1;
-    // Column prefix over y (one thread per tile column).
+    const int32_t* d = diff + (size_t)blockIdx.x * dw * (ty + 1);
+    int32_t* out = chunk_counts + (size_t)blockIdx.x * tx * ty;
     for (int x = threadIdx.x; x < tx; x += blockDim.x) {
         int run = 0;
         for (int y = 0; y < ty; ++y) {
-            run += diff[y * dw + x];
-            raw_counts[y * tx + x] = run;
+            run += d[y * dw + x];
+            out[y * tx + x] = run;
         }
     }
     __syncthreads();
-    // Row prefix over x (one warp per tile row, 32 columns at a time with a
-    // shuffle scan) and the work of each row.
-    {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    for (int y = warp; y < ty; y += nwarps) {
+        int32_t* row = out + (size_t)y * tx;
+        int carry = 0;
+        for (int x0 = 0; x0 < tx; x0 += 32) {
+            const int x = x0 + lane;
+            int v = x < tx ? row[x] : 0;
+#pragma unroll
+            for (int dd = 1; dd < 32; dd <<= 1) {
+                const int o = __shfl_up_sync(0xffffffffu, v, dd);
+                if (lane >= dd) v += o;
+            }
+            const int run = carry + v;
+            if (x < tx) row[x] = run;
+            carry = __shfl_sync(0xffffffffu, run, 31);
+        }
+    }
+}
+
+// Per tile: the raw count (sum over the id chunks) and, for a tile over the
+// 2048 cap, the first chunk k at which the cumulative count reaches 2048.
+// The 2048 lowest ids of the tile (the ones it keeps) all lie in chunks
+// 0..k, so only those chunks' intersections are emitted: emit_count[t] is
+// their number and id_limit[t] = (k + 1) * id_chunk the exclusive id bound
+// (INT_MAX for tiles within the cap, which emit everything).
+__global__ void __launch_bounds__(256)
+k_tile_select(const int32_t* __restrict__ chunk_counts, int num_tiles, int num_chunks, int id_chunk,
+              int32_t* __restrict__ raw_true, int32_t* __restrict__ emit_count, int32_t* __restrict__ id_limit,
+              uint32_t* err) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= num_tiles) return;
+    int64_t cum = 0;
+    int cut = -1, emitted = 0;
+    for (int c = 0; c < num_chunks; ++c) {
+        cum += chunk_counts[(size_t)c * num_tiles + t];
+        if (cut < 0 && cum >= kMaxTileElems) {
+            cut = c;
+            emitted = (int)cum;
+        }
+    }
+    const int raw = (int)min(cum, (int64_t)INT_MAX);
+    raw_true[t] = raw;
+    if (raw > kMaxTileElems) {
+        emit_count[t] = emitted;
+        id_limit[t] = (int)min((int64_t)(cut + 1) * id_chunk, (int64_t)INT_MAX);
+        if (err) atomicOr(err, kErrTileOverflow);
+    } else {
+        emit_count[t] = raw;
+        id_limit[t] = INT_MAX;
+    }
+}
+
+// From the per-tile emitted counts (k_tile_select): the row work, clamped
+// kept counts and both exclusive scans, for tile rows [row0, row1) (other
+// rows get zero counts). With world > 0 the rows are chosen here: band `rank`
+// of `world` work-balanced bands [o0, o1) plus a one-row halo; the band goes
+// to totals[2..3] next to the emitted and kept totals (totals[0..1]).
+__global__ void __launch_bounds__(kCountThreads)
+k_tile_counts(int tx, int ty, int row0, int row1, int32_t* __restrict__ raw_counts,
+              int64_t* __restrict__ raw_start, unsigned long long* __restrict__ fill, int2* __restrict__ tile_bins,
+              int64_t* __restrict__ totals, int64_t* __restrict__ row_work, int world, int rank) {
+    __shared__ int s_rows[2];
+    // The work of each row (one warp per tile row).
+    if (row_work) {
         const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
         for (int y = warp; y < ty; y += nwarps) {
-            int32_t* row = raw_counts + (size_t)y * tx;
-            int carry = 0;
+            const int32_t* row = raw_counts + (size_t)y * tx;
             int64_t work = 0;
-            for (int x0 = 0; x0 < tx; x0 += 32) {
-                const int x = x0 + lane;
-                int v = x < tx ? row[x] : 0;
-#pragma unroll
-                for (int d = 1; d < 32; d <<= 1) {
-                    const int o = __shfl_up_sync(0xffffffffu, v, d);
-                    if (lane >= d) v += o;
-                }
-                const int run = carry + v;
-                if (x < tx) {
-                    row[x] = run;
-                    work += min(run, kMaxTileElems) + kRowWorkPerTile;
-                }
-                carry = __shfl_sync(0xffffffffu, run, 31);
-            }
+            for (int x = lane; x < tx; x += 32) work += min(row[x], kMaxTileElems) + kRowWorkPerTile;
 #pragma unroll
             for (int d = 16; d > 0; d >>= 1) work += __shfl_xor_sync(0xffffffffu, work, d);
-            if (row_work && lane == 0) row_work[y] = work;
+            if (lane == 0) row_work[y] = work;
         }
     }
     __syncthreads();
@@ -198,7 +243,7 @@ k_tile_counts(const int32_t* __restrict__ diff, int tx, int ty, int row0, int ro
 // in flight whatever the rectangle sizes.
 __global__ void __launch_bounds__(256)
 k_emit_keys(int n, const uint2* __restrict__ rects, const float* __restrict__ depths, int tx, int row0, int row1,
-            unsigned long long* __restrict__ fill, uint64_t* __restrict__ keys) {
+            const int32_t* __restrict__ id_limit, unsigned long long* __restrict__ fill, uint64_t* __restrict__ keys) {
     constexpr unsigned full = 0xffffffffu;
     const int lane = threadIdx.x & 31;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -248,6 +293,8 @@ k_emit_keys(int n, const uint2* __restrict__ rects, const float* __restrict__ de
                 const int local = j - o_excl;
                 const int ry = local / o_w;
                 tile[q] = (o_y0 + ry) * tx + o_x0 + (local - ry * o_w);
+                // past the tile's id limit: not among its 2048 lowest ids
+                if ((int)(uint32_t)okey[q] >= __ldg(id_limit + tile[q])) tile[q] = -1;
             }
         }
         // fill[t] starts at the tile's first key position (k_tile_counts),
@@ -496,20 +543,25 @@ k_tile_sort(const int32_t* __restrict__ raw_counts, const int64_t* __restrict__ 
 
 }  // namespace
 
-void launch_tile_counts(const int32_t* tile_diff, int tiles_x, int tiles_y, int row0, int row1,
+void launch_tile_counts(const int32_t* tile_diff, int id_chunk, int32_t* chunk_counts, int32_t* raw_true,
+                        int32_t* id_limit, int tiles_x, int tiles_y, int row0, int row1,
                         int32_t* raw_counts, int64_t* raw_start, uint64_t* fill, int2* tile_bins, int64_t* totals,
-                        int64_t* row_work, cudaStream_t s, int world, int rank) {
-    note_launches(1);
-    k_tile_counts<<<1, kCountThreads, 0, s>>>(tile_diff, tiles_x, tiles_y, row0, row1, raw_counts, raw_start,
+                        int64_t* row_work, uint32_t* err, cudaStream_t s, int world, int rank) {
+    const int T = tiles_x * tiles_y;
+    note_launches(3);
+    k_chunk_counts<<<kIdChunks, kCountThreads, 0, s>>>(tile_diff, tiles_x, tiles_y, chunk_counts);
+    k_tile_select<<<(T + 255) / 256, 256, 0, s>>>(chunk_counts, T, kIdChunks, id_chunk, raw_true, raw_counts,
+                                                  id_limit, err);
+    k_tile_counts<<<1, kCountThreads, 0, s>>>(tiles_x, tiles_y, row0, row1, raw_counts, raw_start,
                                               reinterpret_cast<unsigned long long*>(fill), tile_bins, totals,
                                               row_work, world, rank);
 }
 
 void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x, int row0, int row1,
-                      uint64_t* fill, uint64_t* raw_keys, cudaStream_t s) {
+                      const int32_t* id_limit, uint64_t* fill, uint64_t* raw_keys, cudaStream_t s) {
     if (n <= 0) return;
     note_launches(1);
-    k_emit_keys<<<(n + 255) / 256, 256, 0, s>>>(n, rects, depths, tiles_x, row0, row1,
+    k_emit_keys<<<(n + 255) / 256, 256, 0, s>>>(n, rects, depths, tiles_x, row0, row1, id_limit,
                                                 reinterpret_cast<unsigned long long*>(fill), raw_keys);
 }
 

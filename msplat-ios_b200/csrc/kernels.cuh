@@ -28,6 +28,10 @@ struct CameraDev {
 
 // ---- projection (project.cu) ------------------------------------------------
 constexpr int kMaxPeerRanks = 16;
+// Gaussian ids are split into this many contiguous chunks for the per-tile
+// counts, so that a tile over the 2048 cap emits only the chunks that can hold
+// its 2048 lowest ids.
+constexpr int kIdChunks = 32;
 
 struct ProjFwdArgs {
     int n;
@@ -46,7 +50,8 @@ struct ProjFwdArgs {
     uint2* rects;            // [N] packed tile rect (x0 | y0 << 16, x1 | y1 << 16)
     float* depths;           // [N] view-space depth (sort key)
     int32_t* radii;          // [N]
-    int32_t* tile_diff;      // [(tiles_y+1) * (tiles_x+1)] 2-D difference array (+=)
+    int32_t* tile_diff;      // [kIdChunks][(tiles_y+1) * (tiles_x+1)] 2-D difference arrays (+=)
+    int id_chunk;            // Gaussian i counts into difference array i / id_chunk
     // optional reference-shaped outputs (may be null)
     float* xys; float* transmats; int32_t* num_tiles_hit; float* normal_opacity;
     float* colors; float* aabb;
@@ -93,18 +98,23 @@ struct ProjBwdArgs {
 void launch_project_backward(const ProjBwdArgs& a, cudaStream_t s);
 
 // ---- binning (binning.cu) ---------------------------------------------------
-// Tile counts from the difference array, kept counts, exclusive scans and the
-// two totals. totals[0] = raw intersections (int64), totals[1] = kept.
+// Tile counts from the per-chunk difference arrays (chunk_counts: scratch of
+// kIdChunks * tiles), the true raw counts (raw_true), the emitted counts
+// (raw_counts: all intersections of a tile within the cap, the chunks up to
+// the one holding its 2048th lowest id otherwise) with the id bound of each
+// tile (id_limit), kept counts, exclusive scans and the two totals.
+// totals[0] = emitted intersections (int64), totals[1] = kept.
 // fill[t] receives raw_start[t]: the key counter of k_emit_keys. Only
 // tile rows [row0, row1) are binned; the other rows get empty ranges.
 // row_work (optional, [tiles_y]) receives a per-row work estimate over all
 // rows, for balancing tile-row bands across GPUs.
-void launch_tile_counts(const int32_t* tile_diff, int tiles_x, int tiles_y, int row0, int row1,
+void launch_tile_counts(const int32_t* tile_diff, int id_chunk, int32_t* chunk_counts, int32_t* raw_true,
+                        int32_t* id_limit, int tiles_x, int tiles_y, int row0, int row1,
                         int32_t* raw_counts, int64_t* raw_start, uint64_t* fill, int2* tile_bins, int64_t* totals,
-                        int64_t* row_work, cudaStream_t s,
+                        int64_t* row_work, uint32_t* err, cudaStream_t s,
                         int world = 0, int rank = 0);
 void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x, int row0, int row1,
-                      uint64_t* fill, uint64_t* raw_keys, cudaStream_t s);
+                      const int32_t* id_limit, uint64_t* fill, uint64_t* raw_keys, cudaStream_t s);
 // num_gaussians bounds the ids (the overfull-tile select needs a third digit
 // pass above 2^24 Gaussians).
 void launch_tile_sort(int tile0, int num_tiles, const int32_t* raw_counts, const int64_t* raw_start,

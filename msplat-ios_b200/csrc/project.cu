@@ -176,10 +176,11 @@ __global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
     a.depths[i] = pvz;
     a.rects[i] = make_uint2((uint32_t)x0 | ((uint32_t)y0 << 16), (uint32_t)x1 | ((uint32_t)y1 << 16));
     const int dw = cam.tiles_x + 1;
-    atomicAdd(&a.tile_diff[y0 * dw + x0], 1);
-    atomicAdd(&a.tile_diff[y0 * dw + x1], -1);
-    atomicAdd(&a.tile_diff[y1 * dw + x0], -1);
-    atomicAdd(&a.tile_diff[y1 * dw + x1], 1);
+    int32_t* diff = a.tile_diff + (size_t)(i / a.id_chunk) * dw * (cam.tiles_y + 1);
+    atomicAdd(&diff[y0 * dw + x0], 1);
+    atomicAdd(&diff[y0 * dw + x1], -1);
+    atomicAdd(&diff[y1 * dw + x0], -1);
+    atomicAdd(&diff[y1 * dw + x1], 1);
 
     float col[3] = {0.f, 0.f, 0.f}, rgb[3] = {0.f, 0.f, 0.f};
     if (a.pass == 0) gaussian_color(a, pp, i, p, col, rgb);
