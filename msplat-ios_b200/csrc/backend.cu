@@ -76,7 +76,7 @@ struct Workspace {
     Buf dL_dmean3D, dL_dscale, dL_dquat, dL_dmean2D, dL_dfeatures_dc, dL_dfeatures_rest, dL_dopacity;
     Buf dL_dtransMat, dL_dnormal3D, dL_dcolors;
     // per tile / intersection
-    Buf tile_diff, chunk_counts, raw_true, id_limit, raw_counts, raw_start, tile_bins, fill, raw_keys, gaussian_ids,
+    Buf tile_diff, chunk_counts, raw_true, id_limit, block_max, raw_counts, raw_start, tile_bins, fill, raw_keys, gaussian_ids,
         blend_mask;
     // per pixel
     Buf final_Ts, final_idx, out_img, out_depth, out_normal, out_alpha, out_median, out_dist, dL_dout_img;
@@ -101,7 +101,7 @@ struct Workspace {
         Buf* all[] = {&records, &cull, &rects, &depths, &radii, &raster_grads, &xys, &transmats, &num_tiles_hit,
                       &normal_opacity, &colors, &aabb, &dL_dmean3D, &dL_dscale, &dL_dquat, &dL_dmean2D,
                       &dL_dfeatures_dc, &dL_dfeatures_rest, &dL_dopacity, &dL_dtransMat, &dL_dnormal3D,
-                      &dL_dcolors, &tile_diff, &chunk_counts, &raw_true, &id_limit, &raw_counts, &raw_start, &tile_bins, &fill, &raw_keys,
+                      &dL_dcolors, &tile_diff, &chunk_counts, &raw_true, &id_limit, &block_max, &raw_counts, &raw_start, &tile_bins, &fill, &raw_keys,
                       &gaussian_ids, &blend_mask, &final_Ts, &final_idx, &out_img, &out_depth, &out_normal, &out_alpha,
                       &out_median, &out_dist, &dL_dout_img, &loss_partials, &loss_out, &loss_f, &err, &totals, &row_work};
         for (Buf* b : all) b->release();
@@ -256,6 +256,9 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     w.chunk_counts.ensure((size_t)kIdChunks * T * 4);
     w.raw_true.ensure((size_t)T * 4);
     w.id_limit.ensure((size_t)T * 4);
+    const size_t bmax_bytes =
+        (size_t)((tx + kLimitBlock - 1) / kLimitBlock) * ((ty + kLimitBlock - 1) / kLimitBlock) * 4;
+    w.block_max.ensure(bmax_bytes);
     w.raw_counts.ensure((size_t)T * 4);
     w.raw_start.ensure((size_t)T * 8);
     w.tile_bins.ensure((size_t)T * sizeof(int2));
@@ -267,6 +270,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     w.out_median.ensure(P * 4); w.out_dist.ensure(P * 4);
 
     CK(cudaMemsetAsync(w.tile_diff.p, 0, diff_bytes, s));
+    CK(cudaMemsetAsync(w.block_max.p, 0, bmax_bytes, s));
     CK(cudaMemsetAsync(w.err.p, 0, sizeof(uint32_t), s));
 
     ProjFwdArgs pa{};
@@ -296,7 +300,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     mark(w, kStCounts, s);
     if (balance_world > 0) w.row_work.ensure((size_t)ty * sizeof(int64_t));
     launch_tile_counts(w.tile_diff.as<int32_t>(), id_chunk, w.chunk_counts.as<int32_t>(), w.raw_true.as<int32_t>(),
-                       w.id_limit.as<int32_t>(), tx, ty, row0, row1, w.raw_counts.as<int32_t>(),
+                       w.id_limit.as<int32_t>(), w.block_max.as<int32_t>(), tx, ty, row0, row1, w.raw_counts.as<int32_t>(),
                        w.raw_start.as<int64_t>(), w.fill.as<uint64_t>(), w.tile_bins.as<int2>(), w.totals.as<int64_t>(),
                        balance_world > 0 ? w.row_work.as<int64_t>() : nullptr, w.err.as<uint32_t>(), s, balance_world,
                        balance_rank);
@@ -320,7 +324,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     w.blend_mask.ensure((size_t)(kept > 0 ? kept : 1));
     mark(w, kStEmit, s);
     launch_emit_keys(n, w.rects.as<uint2>(), w.depths.as<float>(), tx, row0, row1, w.id_limit.as<int32_t>(),
-                     w.fill.as<uint64_t>(), w.raw_keys.as<uint64_t>(), s);
+                     w.block_max.as<int32_t>(), w.fill.as<uint64_t>(), w.raw_keys.as<uint64_t>(), s);
     mark(w, kStSort, s);
     launch_tile_sort(row0 * tx, (row1 - row0) * tx, w.raw_counts.as<int32_t>(), w.raw_start.as<int64_t>(), w.raw_keys.as<uint64_t>(),
                      w.tile_bins.as<int2>(), w.gaussian_ids.as<int32_t>(), w.err.as<uint32_t>(), n, s);

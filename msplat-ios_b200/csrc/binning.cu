@@ -90,13 +90,17 @@ k_chunk_counts(const int32_t* __restrict__ diff, int tx, int ty, int32_t* __rest
 // The 2048 lowest ids of the tile (the ones it keeps) all lie in chunks
 // 0..k, so only those chunks' intersections are emitted: emit_count[t] is
 // their number and id_limit[t] = (k + 1) * id_chunk the exclusive id bound
-// (INT_MAX for tiles within the cap, which emit everything).
+// (INT_MAX for tiles within the cap, which emit everything). block_max
+// (zeroed by the caller) receives the largest id_limit of each
+// kLimitBlock x kLimitBlock block of tiles.
 __global__ void __launch_bounds__(256)
-k_tile_select(const int32_t* __restrict__ chunk_counts, int num_tiles, int num_chunks, int id_chunk,
+k_tile_select(const int32_t* __restrict__ chunk_counts, int num_tiles, int tx, int num_chunks, int id_chunk,
               int32_t* __restrict__ raw_true, int32_t* __restrict__ emit_count, int32_t* __restrict__ id_limit,
-              uint32_t* err) {
+              int32_t* __restrict__ block_max, uint32_t* err) {
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= num_tiles) return;
+    const int bxn = (tx + kLimitBlock - 1) / kLimitBlock;
+    int32_t* bmax = block_max + ((t / tx) / kLimitBlock) * bxn + (t % tx) / kLimitBlock;
     int64_t cum = 0;
     int cut = -1, emitted = 0;
     for (int c = 0; c < num_chunks; ++c) {
@@ -108,14 +112,16 @@ k_tile_select(const int32_t* __restrict__ chunk_counts, int num_tiles, int num_c
     }
     const int raw = (int)min(cum, (int64_t)INT_MAX);
     raw_true[t] = raw;
+    int limit = INT_MAX;
     if (raw > kMaxTileElems) {
         emit_count[t] = emitted;
-        id_limit[t] = (int)min((int64_t)(cut + 1) * id_chunk, (int64_t)INT_MAX);
+        limit = (int)min((int64_t)(cut + 1) * id_chunk, (int64_t)INT_MAX);
         if (err) atomicOr(err, kErrTileOverflow);
     } else {
         emit_count[t] = raw;
-        id_limit[t] = INT_MAX;
     }
+    id_limit[t] = limit;
+    atomicMax(bmax, limit);
 }
 
 // From the per-tile emitted counts (k_tile_select): the row work, clamped
@@ -243,7 +249,8 @@ k_tile_counts(int tx, int ty, int row0, int row1, int32_t* __restrict__ raw_coun
 // in flight whatever the rectangle sizes.
 __global__ void __launch_bounds__(256)
 k_emit_keys(int n, const uint2* __restrict__ rects, const float* __restrict__ depths, int tx, int row0, int row1,
-            const int32_t* __restrict__ id_limit, unsigned long long* __restrict__ fill, uint64_t* __restrict__ keys) {
+            const int32_t* __restrict__ id_limit, const int32_t* __restrict__ block_max,
+            unsigned long long* __restrict__ fill, uint64_t* __restrict__ keys) {
     constexpr unsigned full = 0xffffffffu;
     const int lane = threadIdx.x & 31;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -258,6 +265,19 @@ k_emit_keys(int n, const uint2* __restrict__ rects, const float* __restrict__ de
         w = x1 - x0;
         if (w > 0 && y1 > y0) area = w * (y1 - y0);
         key = ((uint64_t)__float_as_uint(depths[i]) << 32) | (uint64_t)(uint32_t)i;
+        // a Gaussian at or past the id bound of every tile block it touches
+        // emits nothing (those tiles keep lower ids only)
+        if (area > 0) {
+            const int bxn = (tx + kLimitBlock - 1) / kLimitBlock;
+            bool any = false;
+            for (int by = y0 / kLimitBlock; by <= (y1 - 1) / kLimitBlock && !any; ++by)
+                for (int bx = x0 / kLimitBlock; bx <= (x1 - 1) / kLimitBlock; ++bx)
+                    if (__ldg(block_max + by * bxn + bx) > i) {
+                        any = true;
+                        break;
+                    }
+            if (!any) area = 0;
+        }
     }
     int incl = area;
 #pragma unroll
@@ -544,24 +564,25 @@ k_tile_sort(const int32_t* __restrict__ raw_counts, const int64_t* __restrict__ 
 }  // namespace
 
 void launch_tile_counts(const int32_t* tile_diff, int id_chunk, int32_t* chunk_counts, int32_t* raw_true,
-                        int32_t* id_limit, int tiles_x, int tiles_y, int row0, int row1,
+                        int32_t* id_limit, int32_t* block_max, int tiles_x, int tiles_y, int row0, int row1,
                         int32_t* raw_counts, int64_t* raw_start, uint64_t* fill, int2* tile_bins, int64_t* totals,
                         int64_t* row_work, uint32_t* err, cudaStream_t s, int world, int rank) {
     const int T = tiles_x * tiles_y;
     note_launches(3);
     k_chunk_counts<<<kIdChunks, kCountThreads, 0, s>>>(tile_diff, tiles_x, tiles_y, chunk_counts);
-    k_tile_select<<<(T + 255) / 256, 256, 0, s>>>(chunk_counts, T, kIdChunks, id_chunk, raw_true, raw_counts,
-                                                  id_limit, err);
+    k_tile_select<<<(T + 255) / 256, 256, 0, s>>>(chunk_counts, T, tiles_x, kIdChunks, id_chunk, raw_true,
+                                                  raw_counts, id_limit, block_max, err);
     k_tile_counts<<<1, kCountThreads, 0, s>>>(tiles_x, tiles_y, row0, row1, raw_counts, raw_start,
                                               reinterpret_cast<unsigned long long*>(fill), tile_bins, totals,
                                               row_work, world, rank);
 }
 
 void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x, int row0, int row1,
-                      const int32_t* id_limit, uint64_t* fill, uint64_t* raw_keys, cudaStream_t s) {
+                      const int32_t* id_limit, const int32_t* block_max, uint64_t* fill, uint64_t* raw_keys,
+                      cudaStream_t s) {
     if (n <= 0) return;
     note_launches(1);
-    k_emit_keys<<<(n + 255) / 256, 256, 0, s>>>(n, rects, depths, tiles_x, row0, row1, id_limit,
+    k_emit_keys<<<(n + 255) / 256, 256, 0, s>>>(n, rects, depths, tiles_x, row0, row1, id_limit, block_max,
                                                 reinterpret_cast<unsigned long long*>(fill), raw_keys);
 }
 

@@ -32,6 +32,10 @@ constexpr int kMaxPeerRanks = 16;
 // counts, so that a tile over the 2048 cap emits only the chunks that can hold
 // its 2048 lowest ids.
 constexpr int kIdChunks = 32;
+// Side of the square blocks of tiles over which the largest id bound is kept
+// (block_max), letting key emission skip a Gaussian whose id is past the
+// bounds of all the blocks it touches.
+constexpr int kLimitBlock = 8;
 
 struct ProjFwdArgs {
     int n;
@@ -109,12 +113,13 @@ void launch_project_backward(const ProjBwdArgs& a, cudaStream_t s);
 // row_work (optional, [tiles_y]) receives a per-row work estimate over all
 // rows, for balancing tile-row bands across GPUs.
 void launch_tile_counts(const int32_t* tile_diff, int id_chunk, int32_t* chunk_counts, int32_t* raw_true,
-                        int32_t* id_limit, int tiles_x, int tiles_y, int row0, int row1,
+                        int32_t* id_limit, int32_t* block_max, int tiles_x, int tiles_y, int row0, int row1,
                         int32_t* raw_counts, int64_t* raw_start, uint64_t* fill, int2* tile_bins, int64_t* totals,
                         int64_t* row_work, uint32_t* err, cudaStream_t s,
                         int world = 0, int rank = 0);
 void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x, int row0, int row1,
-                      const int32_t* id_limit, uint64_t* fill, uint64_t* raw_keys, cudaStream_t s);
+                      const int32_t* id_limit, const int32_t* block_max, uint64_t* fill, uint64_t* raw_keys,
+                      cudaStream_t s);
 // num_gaussians bounds the ids (the overfull-tile select needs a third digit
 // pass above 2^24 Gaussians).
 void launch_tile_sort(int tile0, int num_tiles, const int32_t* raw_counts, const int64_t* raw_start,
