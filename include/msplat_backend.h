@@ -52,7 +52,7 @@ typedef struct MsplatCamera {
 
 /* Gaussian parameters, device pointers in the reference layout. */
 typedef struct MsplatGaussians {
-    int32_t num_points;
+    int32_t num_points; /* 0 .. 2^25 (MSPLAT_ERR_ARGUMENT above) */
     int32_t sh_degree; /* degree of the stored coefficients, 0..3 */
     float* means;
     float* scales;
