@@ -8,18 +8,24 @@
 // The reference scatters into fixed 2048-slot bins with atomics, so which
 // intersections survive in an overfull tile depends on the atomic race. Here
 // every step is deterministic:
-//   1. the projection adds each Gaussian's tile rectangle into a 2-D
-//      difference array (4 atomics per Gaussian instead of one per tile);
-//   2. one CTA integrates it into exact per-tile counts, clamps them to 2048
-//      and scans both the raw and the kept counts;
-//   3. each (Gaussian, tile) pair appends the key (depth_bits << 32) | id into
-//      its tile's raw segment (slot order is irrelevant, the set is exact);
+//   1. the projection adds each Gaussian's tile rectangle into the 2-D
+//      difference array of its id chunk (32 contiguous id ranges; 4 atomics
+//      per Gaussian instead of one per tile);
+//   2. one CTA per chunk integrates its array into per-tile counts; per tile,
+//      the raw count and, for a tile over the 2048 cap, the id bound below
+//      which its 2048 lowest ids lie (the end of the chunk where the
+//      cumulative count reaches 2048); one CTA then clamps the emitted counts
+//      to 2048 and scans both the emitted and the kept counts;
+//   3. each (Gaussian, tile) pair under the tile's id bound appends the key
+//      (depth_bits << 32) | id into its tile's segment (slot order is
+//      irrelevant, the set is exact); Gaussians past the bounds of every
+//      8x8-tile block they touch are skipped whole;
 //   4. per tile, the kept keys are sorted ascending with a register-blocked
 //      bitonic network (keys in registers; partners in the same warp reached
 //      by shuffles, only cross-warp partners through shared memory): one warp
 //      per tile up to 512 keys, one CTA above that; for an overfull tile the
-//      CTA first keeps the 2048 lowest Gaussian ids (a three-pass radix select
-//      on the id bits). Output: the sorted Gaussian ids.
+//      CTA first keeps the 2048 lowest Gaussian ids among the emitted ones (a
+//      radix select on the id bits). Output: the sorted Gaussian ids.
 #include <climits>
 
 #include "common.cuh"
