@@ -123,9 +123,8 @@ def build_scene(cfg_id: int):
 
 
 def cameras(B, S, cfg, scene):
-    from msplat import camera_setup
     fx, fy, cx, cy = scene.intrinsics
-    return [camera_setup.prepare_cam(B, scene.cam_to_world[k], fx, fy, cx, cy, cfg.width, cfg.height)
+    return [B.prepare_camera(scene.cam_to_world[k], fx, fy, cx, cy, cfg.width, cfg.height)
             for k in range(len(scene.cam_to_world))]
 
 

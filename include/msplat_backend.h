@@ -300,15 +300,19 @@ int msplat_reset_opacity(float* opacities, float* exp_avg, float* exp_avg_sq, in
  * allocator, or that fix their memory budget at start-up): it calls no
  * cudaMalloc/cudaFree and no allocating library routine. Its scratch lives in
  * fixed arrays inside the library's device image, about 192 KiB held by every
- * GPU that loads the library until the process exits, which limits images to
- * 8192 loss blocks (54-column strips: widths up to 442,368 pixels); wider
- * images are rejected with MSPLAT_ERR_ARGUMENT. Inputs and outputs are caller-owned device
- * memory: out_img and gt [H,W,3], out_distortion [H,W] (may be NULL when
- * lambda_dist == 0), dL_dout_img [H,W,3] (written), loss_out one float
- * (written, may be NULL). The first call on a device looks up the scratch
- * addresses; make that first call before any stream capture. All calls share
- * the scratch, so calls that overlap on the GPU (other streams, other host
- * threads) race; serialise them. Asynchronous on `stream`. */
+ * GPU that loads the library until the process exits. The scratch holds 8192
+ * loss blocks; this entry point lays out at most that many (54-column strips,
+ * fewer row segments per strip than the regular path for tall images), so it
+ * accepts any height and widths up to 8192 x 54 = 442,368 pixels. Wider
+ * images are rejected with MSPLAT_ERR_ARGUMENT. Inputs and outputs are
+ * caller-owned device memory: out_img and gt [H,W,3], out_distortion [H,W]
+ * (may be NULL when lambda_dist == 0), dL_dout_img [H,W,3] (written),
+ * loss_out one float (written, may be NULL). A non-finite loss is not turned
+ * into an error code on this path: it shows only as NaN or Inf in *loss_out.
+ * The first call on a device looks up the scratch addresses; make that first
+ * call before any stream capture. All calls share the scratch, so calls that
+ * overlap on the GPU (other streams, other host threads) race; serialise
+ * them. Asynchronous on `stream`. */
 int msplat_loss_ssim_noalloc(const float* out_img, const float* gt, const float* out_distortion, int32_t width,
                              int32_t height, float lambda_l1, float lambda_dist, float lambda_dssim,
                              float* dL_dout_img, float* loss_out, void* stream);

@@ -161,6 +161,15 @@ int msplat_trainer_iteration(MsplatTrainer t);
 int msplat_trainer_get_params(MsplatTrainer t, float* means, float* scales, float* quats, float* opacities,
                               float* featuresDc, float* featuresRest);
 
+/* Additive: when enable != 0, every later msplat_trainer_step also writes the
+ * per-group gradients it hands to Adam (the tensors Model::fullIteration
+ * passes to its six msplat_fused_adam calls, core/src/model.cpp:800-826) to
+ * the backend workspace, readable with msplat_last_tensor (dL_dmean3D,
+ * dL_dscale, dL_dquat, dL_dfeatures_dc, dL_dfeatures_rest, dL_dopacity)
+ * until the next backend call on the device. Costs one extra write of every
+ * gradient per step. Returns 0 on success. */
+int msplat_trainer_set_write_gradients(MsplatTrainer t, int enable);
+
 /* ── Lifecycle (msplat_c_api.h:126-130) ──────────────────────────────────── */
 
 void msplat_set_metallib_path(const char* path);

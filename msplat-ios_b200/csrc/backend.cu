@@ -382,7 +382,7 @@ void stage_loss(Workspace& w, const CameraDev& cam, const float* gt, float l1, f
     la.width = cam.width; la.height = cam.height; la.row_begin = prow0; la.row_end = prow1;
     la.out_img = w.out_img.as<float>(); la.gt = gt; la.out_distortion = w.out_dist.as<float>();
     la.lambda_l1 = l1; la.lambda_dist = ldist; la.lambda_dssim = ldssim;
-    la.inv_num = 1.0f / (float)(cam.height * cam.width * 3);
+    la.inv_num = 1.0f / (float)((double)cam.height * (double)cam.width * 3.0);
     la.dL_dout_img = w.dL_dout_img.as<float>();
     la.partials = w.loss_partials.as<double>();
     mark(w, kStLoss, s);
@@ -403,7 +403,7 @@ void stage_raster_backward(Workspace& w, const CameraDev& cam, const float bg[3]
     ba.bg[0] = bg[0]; ba.bg[1] = bg[1]; ba.bg[2] = bg[2];
     ba.final_Ts = w.final_Ts.as<float>(); ba.final_idx = w.final_idx.as<int32_t>();
     ba.dL_dout_img = w.dL_dout_img.as<float>();
-    ba.dL_dout_distortion = ldist * (1.0f / (float)(cam.height * cam.width * 3)) * 3.0f;  // lambda_dist / HW
+    ba.dL_dout_distortion = ldist * (1.0f / (float)((double)cam.height * (double)cam.width * 3.0)) * 3.0f;  // lambda_dist / HW
     ba.raster_grads = raster_grads;
     ba.blend_mask = w.blend_mask.as<uint8_t>();
     mark(w, kStRasterBwd, s);

@@ -168,8 +168,9 @@ struct LossArgs {
     float* dL_dout_img;                  // written for owned rows
     double* partials;                    // [num_blocks * 3] (l1, ssim, dist) per block
 };
-int loss_num_blocks(int width, int row_begin, int row_end);
-void launch_loss_ssim(const LossArgs& a, cudaStream_t s);
+// max_blocks > 0 caps the grid (strips x row segments) at that many CTAs.
+int loss_num_blocks(int width, int row_begin, int row_end, int max_blocks = 0);
+void launch_loss_ssim(const LossArgs& a, cudaStream_t s, int max_blocks = 0);
 // Sums the block partials in a fixed order: out[0] = loss, out[1] = ssim sum,
 // out[2] = l1 term, out[3] = distortion term (all double), loss_f = float loss.
 void launch_loss_finalize(const double* partials, int num_blocks, float lambda_dssim, float inv_num,

@@ -59,13 +59,15 @@ struct LossGrid {
 
 // Strips x row segments. Every CTA of a segment length L costs about L + 22
 // row steps; the segment count minimises waves x (L + 22), so the grid fills
-// whole waves of resident CTAs with the least recomputed halo.
-LossGrid loss_grid(int width, int rows) {
+// whole waves of resident CTAs with the least recomputed halo. max_blocks > 0
+// caps strips x segments (one segment per strip at least).
+LossGrid loss_grid(int width, int rows, int max_blocks = 0) {
     LossGrid g;
     g.strips = (width + SW - 1) / SW;
+    const int max_segs = max_blocks > 0 ? std::max(1, max_blocks / std::max(g.strips, 1)) : kMaxSegs;
     int best_segs = 1;
     int64_t best_cost = -1;
-    for (int segs = 1; segs <= kMaxSegs && segs <= rows; ++segs) {
+    for (int segs = 1; segs <= kMaxSegs && segs <= max_segs && segs <= rows; ++segs) {
         const int64_t waves = ((int64_t)g.strips * segs + kSlots - 1) / kSlots;
         const int64_t cost = waves * ((rows + segs - 1) / segs + 4 * R + 2);
         if (best_cost < 0 || cost < best_cost) {
@@ -289,22 +291,22 @@ __global__ void __launch_bounds__(1024) k_loss_finalize(const double* partials, 
         out[2] = l1;
         out[3] = dd;
         if (loss_f) *loss_f = (float)loss;
-        if (!(loss == loss) || loss > 1e300 || loss < -1e300) atomicOr(err, kErrNonFinite);
+        if (err && (!(loss == loss) || loss > 1e300 || loss < -1e300)) atomicOr(err, kErrNonFinite);
     }
 }
 
 }  // namespace
 
-int loss_num_blocks(int width, int row_begin, int row_end) {
+int loss_num_blocks(int width, int row_begin, int row_end, int max_blocks) {
     if (row_end <= row_begin || width <= 0) return 0;
-    const LossGrid g = loss_grid(width, row_end - row_begin);
+    const LossGrid g = loss_grid(width, row_end - row_begin, max_blocks);
     return g.strips * g.segs;
 }
 
-void launch_loss_ssim(const LossArgs& a, cudaStream_t s) {
+void launch_loss_ssim(const LossArgs& a, cudaStream_t s, int max_blocks) {
     const int rows = a.row_end - a.row_begin;
     if (rows <= 0 || a.width <= 0) return;
-    const LossGrid g = loss_grid(a.width, rows);
+    const LossGrid g = loss_grid(a.width, rows, max_blocks);
     note_launches(1);
     k_loss_ssim<<<dim3(g.strips, g.segs), kThreads, 0, s>>>(a, g.seg_rows);
 }
@@ -317,17 +319,19 @@ void launch_loss_finalize(const double* partials, int num_blocks, float lambda_d
 
 // ---- allocation-free variant (msplat_loss_ssim_noalloc) --------------------
 //
-// The same two kernels, with their scratch (per-block partial sums, the four
-// loss terms and the error word) in fixed arrays that belong to the library's
-// device image instead of workspace buffers, so the entry point never
-// allocates. Every GPU that loads the library holds these arrays (about
-// 192 KiB) until the process exits. Host code cannot use the array names as
-// device addresses; the addresses are looked up once per device with
-// cudaGetSymbolAddress.
-constexpr int kNoAllocMaxBlocks = 8192;  // loss CTAs (strips x row segments): widths up to 442,368
+// The same two kernels, with their scratch (per-block partial sums and the
+// four loss terms) in fixed arrays that belong to the library's device image
+// instead of workspace buffers, so the entry point never allocates. Every GPU
+// that loads the library holds these arrays (about 192 KiB) until the process
+// exits. The grid is capped at kNoAllocMaxBlocks CTAs (fewer row segments per
+// strip), so any image of up to 8192 strips of 54 columns fits at any height.
+// Host code cannot use the array names as device addresses; the addresses are
+// looked up once per device with cudaGetSymbolAddress. The finalize kernel
+// gets no error word here: a non-finite loss shows only as NaN or Inf in
+// loss_out.
+constexpr int kNoAllocMaxBlocks = 8192;  // loss CTAs: widths up to 8192 x 54 = 442,368 pixels
 static __device__ __align__(256) double g_noalloc_partials[kNoAllocMaxBlocks * 3];
 static __device__ __align__(256) double g_noalloc_terms[4];
-static __device__ __align__(256) uint32_t g_noalloc_err[4];
 
 namespace {
 constexpr int kMaxDevices = 64;
@@ -335,7 +339,6 @@ struct NoAllocScratch {
     bool ready = false;
     double* partials = nullptr;
     double* terms = nullptr;
-    uint32_t* err = nullptr;
 };
 std::mutex g_noalloc_mu;
 NoAllocScratch g_noalloc[kMaxDevices];
@@ -366,11 +369,6 @@ int noalloc_scratch(NoAllocScratch* out, std::string* msg) {
             return MSPLAT_ERR_CUDA;
         }
         s.terms = static_cast<double*>(p);
-        if ((e = cudaGetSymbolAddress(&p, g_noalloc_err)) != cudaSuccess) {
-            *msg = std::string("cudaGetSymbolAddress(err): ") + cudaGetErrorString(e);
-            return MSPLAT_ERR_CUDA;
-        }
-        s.err = static_cast<uint32_t*>(p);
         s.ready = true;
     }
     *out = s;
@@ -393,30 +391,32 @@ int loss_ssim_noalloc(const float* out_img, const float* gt, const float* out_di
         *msg = "out_distortion is required when lambda_dist != 0";
         return MSPLAT_ERR_ARGUMENT;
     }
-    const int64_t nb = loss_num_blocks(width, 0, height);
-    if (nb > kNoAllocMaxBlocks) {
-        *msg = "image too wide for the allocation-free loss: " + std::to_string(nb) + " loss blocks of " +
-               std::to_string(SW) + "-column strips, the fixed scratch holds " + std::to_string(kNoAllocMaxBlocks);
+    const int64_t strips = ((int64_t)width + SW - 1) / SW;
+    if (strips > kNoAllocMaxBlocks) {
+        *msg = "image too wide for the allocation-free loss: " + std::to_string(strips) + " strips of " +
+               std::to_string(SW) + " columns, the fixed scratch holds " + std::to_string(kNoAllocMaxBlocks) +
+               " (widths up to " + std::to_string((int64_t)kNoAllocMaxBlocks * SW) + ")";
+        return MSPLAT_ERR_ARGUMENT;
+    }
+    const int64_t nb = loss_num_blocks(width, 0, height, kNoAllocMaxBlocks);
+    if (nb <= 0 || nb > kNoAllocMaxBlocks) {  // cannot happen with the cap; kept as a guard of the array
+        *msg = "allocation-free loss grid of " + std::to_string(nb) + " blocks exceeds its scratch";
         return MSPLAT_ERR_ARGUMENT;
     }
     NoAllocScratch sc;
     int rc = noalloc_scratch(&sc, msg);
     if (rc != MSPLAT_OK) return rc;
-    cudaError_t e = cudaMemsetAsync(sc.err, 0, sizeof(uint32_t), s);
-    if (e != cudaSuccess) {
-        *msg = std::string("cudaMemsetAsync: ") + cudaGetErrorString(e);
-        return MSPLAT_ERR_CUDA;
-    }
     LossArgs la{};
     la.width = width; la.height = height; la.row_begin = 0; la.row_end = height;
     la.out_img = out_img; la.gt = gt; la.out_distortion = out_distortion;
     la.lambda_l1 = lambda_l1; la.lambda_dist = lambda_dist; la.lambda_dssim = lambda_dssim;
-    la.inv_num = 1.0f / (float)(height * width * 3);
+    // 3HW in double: it can exceed the int range for the largest images
+    la.inv_num = 1.0f / (float)((double)height * (double)width * 3.0);
     la.dL_dout_img = dL_dout_img;
     la.partials = sc.partials;
-    launch_loss_ssim(la, s);
-    launch_loss_finalize(sc.partials, (int)nb, lambda_dssim, la.inv_num, sc.terms, loss_out, sc.err, s);
-    e = cudaGetLastError();
+    launch_loss_ssim(la, s, kNoAllocMaxBlocks);
+    launch_loss_finalize(sc.partials, (int)nb, lambda_dssim, la.inv_num, sc.terms, loss_out, nullptr, s);
+    cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *msg = std::string("loss kernels: ") + cudaGetErrorString(e);
         return MSPLAT_ERR_CUDA;

@@ -160,6 +160,7 @@ struct Trainer {
     DevArray<float> params[6], m[6], v[6], stats[3];
     int64_t counts[6] = {};
     float lr[6] = {0.00016f, 0.005f, 0.001f, 0.0025f, 0.000125f, 0.05f};  // model.cpp:142
+    bool write_grads = false;  // msplat_trainer_set_write_gradients
     float means_lr_init = 0.00016f, means_lr_final = 0.0000016f;
     int adam_step = 0;
     int current_step = 0;
@@ -343,8 +344,8 @@ struct Trainer {
         const int degrees_to_use = std::min(current_step / std::max(1, cfg.shDegreeInterval), degree);
         MsplatGaussians G = gaussians();
         check_rc(msplat_train_step_fused(&G, &cam, degrees_to_use, cfg.bgColor, gt, 1.0f - cfg.ssimWeight, 0.0f,
-                                         cfg.ssimWeight, &A, stats[0].p, stats[1].p, stats[2].p, loss_dev.p, 0,
-                                         stream));
+                                         cfg.ssimWeight, &A, stats[0].p, stats[1].p, stats[2].p, loss_dev.p,
+                                         write_grads ? 1 : 0, stream));
         prefetch_target(peek_camera());
         // schedulersStep (model.cpp:183-186), then afterTrain (:240-306)
         lr[0] = msplat_means_lr(current_step, cfg.iterations, means_lr_init, means_lr_final);
@@ -1005,6 +1006,13 @@ int msplat_trainer_load_checkpoint(MsplatTrainer t, const char* path) {
 }
 int msplat_trainer_splat_count(MsplatTrainer t) { return api<int>(0, [&] { return T(t)->n; }); }
 int msplat_trainer_iteration(MsplatTrainer t) { return api<int>(0, [&] { return T(t)->current_step; }); }
+
+int msplat_trainer_set_write_gradients(MsplatTrainer t, int enable) {
+    return api<int>(-1, [&] {
+        T(t)->write_grads = enable != 0;
+        return 0;
+    });
+}
 
 int msplat_trainer_get_params(MsplatTrainer t, float* means, float* scales, float* quats, float* opacities,
                               float* featuresDc, float* featuresRest) {

@@ -115,6 +115,8 @@ def _lib():
         getattr(L, nm).restype = i
     L.msplat_trainer_get_params.argtypes = [vp, fp, fp, fp, fp, fp, fp]
     L.msplat_trainer_get_params.restype = i
+    L.msplat_trainer_set_write_gradients.argtypes = [vp, i]
+    L.msplat_trainer_set_write_gradients.restype = i
     for nm in ("msplat_trainer_export_ply", "msplat_trainer_export_splat", "msplat_trainer_save_checkpoint"):
         getattr(L, nm).argtypes = [vp, C.c_char_p]
         getattr(L, nm).restype = None
@@ -253,6 +255,12 @@ class GaussianTrainer:
             raise RuntimeError("No test cameras. Load dataset with eval_mode=True.")
         m = _lib().msplat_trainer_evaluate(self._h)
         return {"psnr": m.psnr, "ssim": m.ssim, "l1": m.l1, "num_test": m.numTest, "num_gaussians": m.numGaussians}
+
+    def set_write_gradients(self, enable: bool = True):
+        """Make every later step also write its per-group gradients to the
+        backend workspace (msplat_backend last tensors dL_dmean3D, ...)."""
+        if _lib().msplat_trainer_set_write_gradients(self._h, 1 if enable else 0):
+            raise RuntimeError(_err(_lib()))
 
     def get_params(self):
         n = self.splat_count

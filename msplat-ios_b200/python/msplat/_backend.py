@@ -107,6 +107,7 @@ def load():
     L.msplat_shard_project_backward_adam.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, vp,
                                                      i32, i32, C.POINTER(MsplatAdamState), vp, vp, vp, vp]
     L.msplat_last_tensor.argtypes = [C.c_char_p, C.POINTER(MsplatTensorRef)]
+    L.msplat_prepare_camera.argtypes = [C.POINTER(C.c_float), f, f, f, f, i32, i32, C.POINTER(MsplatCamera)]
     L.msplat_densify_plan.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatDensifyArgs),
                                       C.POINTER(MsplatDensifyPlan), vp]
     L.msplat_densify_apply.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatAdamState),
@@ -130,7 +131,7 @@ def load():
                  "msplat_shard_forward_backward_peers", "msplat_shard_forward_backward_rgb", "msplat_shard_colors",
                  "msplat_device_alloc", "msplat_device_free",
                  "msplat_ipc_handle", "msplat_ipc_open", "msplat_ipc_close",
-                 "msplat_shard_project_backward_adam", "msplat_last_tensor",
+                 "msplat_shard_project_backward_adam", "msplat_last_tensor", "msplat_prepare_camera",
                  "msplat_densify_plan", "msplat_densify_apply", "msplat_reset_opacity"):
         getattr(L, name).restype = C.c_int
     _lib = L
@@ -167,6 +168,17 @@ def camera(viewmat, projmat, fx, fy, cx, cy, width, height, cam_pos) -> MsplatCa
     c.width, c.height = int(width), int(height)
     c.cam_pos[:] = [float(x) for x in np.asarray(cam_pos, np.float32).reshape(3)]
     return c
+
+
+def prepare_camera(cam_to_world, fx, fy, cx, cy, width, height) -> MsplatCamera:
+    """Model::prepareCam (core/src/model.cpp:500-544) in the library
+    (msplat_prepare_camera): view and projection matrices of an OpenGL
+    camToWorld matrix, host code, no GPU needed."""
+    m = np.ascontiguousarray(np.asarray(cam_to_world, np.float32).reshape(16))
+    cam = MsplatCamera()
+    _check(load().msplat_prepare_camera(m.ctypes.data_as(C.POINTER(C.c_float)), fx, fy, cx, cy, width, height,
+                                        C.byref(cam)))
+    return cam
 
 
 def camera_from_oracle(ocam) -> MsplatCamera:

@@ -442,6 +442,72 @@ int64_t orc_bin_and_sort(int n, const float* xys, const float* depths, const int
     return running;
 }
 
+// Raw counts only (the scatter's per-tile counters before the clamp,
+// metal:1557-1591), from per-thread 2-D difference arrays of the tile
+// rectangles; no key buffer, so it scales to billions of intersections.
+void orc_tile_counts(int n, const float* xys, const int32_t* radii, const float* aabb, int tiles_x,
+                     int tiles_y, int64_t* raw_counts) {
+    const int DX = tiles_x + 1, DY = tiles_y + 1;
+    std::vector<int64_t> total((size_t)DX * DY, 0);
+#pragma omp parallel
+    {
+        std::vector<int64_t> d((size_t)DX * DY, 0);
+#pragma omp for schedule(static)
+        for (int i = 0; i < n; ++i) {
+            if (radii[i] <= 0) continue;
+            int x0, y0, x1, y1;
+            tile_bbox(xys[2 * i], xys[2 * i + 1], aabb[2 * i], tiles_x, tiles_y, &x0, &y0, &x1, &y1);
+            if (x1 <= x0 || y1 <= y0) continue;
+            d[(size_t)y0 * DX + x0] += 1;
+            d[(size_t)y0 * DX + x1] -= 1;
+            d[(size_t)y1 * DX + x0] -= 1;
+            d[(size_t)y1 * DX + x1] += 1;
+        }
+#pragma omp critical
+        for (size_t k = 0; k < d.size(); ++k) total[k] += d[k];
+    }
+    // 2-D inclusive prefix sum of the difference array
+    std::vector<int64_t> acc((size_t)DX * DY, 0);
+    for (int y = 0; y < tiles_y; ++y)
+        for (int x = 0; x < tiles_x; ++x) {
+            int64_t v = total[(size_t)y * DX + x];
+            if (x > 0) v += acc[(size_t)y * DX + x - 1];
+            if (y > 0) v += acc[(size_t)(y - 1) * DX + x];
+            if (x > 0 && y > 0) v -= acc[(size_t)(y - 1) * DX + x - 1];
+            acc[(size_t)y * DX + x] = v;
+            raw_counts[(size_t)y * tiles_x + x] = v;
+        }
+}
+
+// Kept ids of the listed tiles under the overflow policy of orc_bin_and_sort
+// (the 2048 lowest Gaussian ids of an overfull tile), sorted by the key
+// (depth_bits << 32) | id. Each tile scans the Gaussians in id order, so the
+// first 2048 it meets are its lowest ids. ids_out holds 2048 ids per listed
+// tile; counts_out the kept count of each.
+void orc_tile_kept_ids(int n, const float* xys, const float* depths, const int32_t* radii, const float* aabb,
+                       int tiles_x, int tiles_y, int num_tiles, const int32_t* tiles, int32_t* ids_out,
+                       int32_t* counts_out) {
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int k = 0; k < num_tiles; ++k) {
+        const int t = tiles[k];
+        const int tx = t % tiles_x, ty = t / tiles_x;
+        std::vector<uint64_t> keys;
+        keys.reserve(kMaxTileElems);
+        for (int i = 0; i < n && (int64_t)keys.size() < kMaxTileElems; ++i) {
+            if (radii[i] <= 0) continue;
+            int x0, y0, x1, y1;
+            tile_bbox(xys[2 * i], xys[2 * i + 1], aabb[2 * i], tiles_x, tiles_y, &x0, &y0, &x1, &y1);
+            if (tx < x0 || tx >= x1 || ty < y0 || ty >= y1) continue;
+            uint32_t db;
+            std::memcpy(&db, &depths[i], 4);
+            keys.push_back(((uint64_t)db << 32) | (uint64_t)(uint32_t)i);
+        }
+        std::sort(keys.begin(), keys.end());
+        counts_out[k] = (int32_t)keys.size();
+        for (size_t q = 0; q < keys.size(); ++q) ids_out[(size_t)k * kMaxTileElems + q] = (int32_t)(keys[q] & 0xFFFFFFFFu);
+    }
+}
+
 void orc_pack(int64_t kept, const int32_t* ids, const float* xys, const float* transmats,
               const float* normal_opacity, const float* colors, float* packed_xy,
               float* packed_transmat, float* packed_normal_opac, float* packed_rgb) {

@@ -73,6 +73,19 @@ int64_t orc_bin_and_sort(int n, const float* xys, const float* depths,
                          int32_t* tile_bins, int32_t* gaussian_ids,
                          int64_t capacity);
 
+/* Raw (un-clamped) intersection counts per tile, as orc_bin_and_sort
+ * reports them, without building the key lists (scales to the billions of
+ * intersections of an overloaded scene). */
+void orc_tile_counts(int n, const float* xys, const int32_t* radii, const float* aabb, int tiles_x,
+                     int tiles_y, int64_t* raw_counts);
+
+/* Sorted kept Gaussian ids of the listed tiles under orc_bin_and_sort's
+ * overflow policy, without building the other tiles' lists. ids_out holds
+ * 2048 entries per listed tile; counts_out[k] = kept count of tiles[k]. */
+void orc_tile_kept_ids(int n, const float* xys, const float* depths, const int32_t* radii, const float* aabb,
+                       int tiles_x, int tiles_y, int num_tiles, const int32_t* tiles, int32_t* ids_out,
+                       int32_t* counts_out);
+
 /* Pack half of bitonic_sort_per_tile_2dgs_kernel (metal:1666-1689). */
 void orc_pack(int64_t kept, const int32_t* gaussian_ids, const float* xys,
               const float* transmats, const float* normal_opacity,

@@ -76,6 +76,9 @@ def lib():
         L.orc_bin_and_sort.restype = C.c_int64
         L.orc_bin_and_sort.argtypes = [C.c_int, f32p, f32p, i32p, f32p, C.c_int, C.c_int, i64p, i32p, i32p,
                                        C.c_int64]
+        L.orc_tile_counts.argtypes = [C.c_int, f32p, i32p, f32p, C.c_int, C.c_int, i64p]
+        L.orc_tile_kept_ids.argtypes = [C.c_int, f32p, f32p, i32p, f32p, C.c_int, C.c_int, C.c_int, i32p, i32p,
+                                        i32p]
         L.orc_pack.argtypes = [C.c_int64, i32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p]
         L.orc_rasterize_forward.argtypes = [C.c_int, C.c_int, C.c_int, i32p, f32p, f32p, f32p, f32p, f32p,
                                             f32p, i32p, f32p, f32p, f32p, f32p, f32p, f32p]
@@ -154,6 +157,25 @@ def bin_and_sort(proj, cam):
                                   tile_bins, ids, cap)
     assert kept >= 0
     return dict(raw_counts=raw, tile_bins=tile_bins, gaussian_ids=ids[:kept].copy(), kept=kept)
+
+
+def tile_counts(proj, cam):
+    """Raw per-tile intersection counts (no key lists)."""
+    tx, ty = tiles(cam)
+    raw = np.zeros(tx * ty, np.int64)
+    lib().orc_tile_counts(proj["xys"].shape[0], proj["xys"], proj["radii"], proj["aabb"], tx, ty, raw)
+    return raw
+
+
+def tile_kept_ids(proj, cam, tile_list):
+    """{tile: sorted kept ids} for the listed tiles (orc_bin_and_sort's policy)."""
+    tx, ty = tiles(cam)
+    tl = np.ascontiguousarray(np.asarray(tile_list, np.int32))
+    ids = np.zeros((len(tl), 2048), np.int32)
+    cnt = np.zeros(len(tl), np.int32)
+    lib().orc_tile_kept_ids(proj["xys"].shape[0], proj["xys"], proj["depths"], proj["radii"], proj["aabb"], tx, ty,
+                            len(tl), tl, ids, cnt)
+    return {int(t): ids[k, :cnt[k]].copy() for k, t in enumerate(tl)}
 
 
 def pack(bins, proj):

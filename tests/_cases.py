@@ -26,8 +26,8 @@ def case_config(name: str) -> S.SceneConfig:
         # ellipses exercise the rasteriser's conic cull at its boundary
         return S.small_config(12_000, 1, 256, 192, focal=230.0, num_cameras=2,
                               log_scale_mean=math.log(0.02), log_scale_std=1.6)
-    if name == "cfg1":
-        return S.CONFIGS[1]
+    if name in ("cfg1", "cfg2", "cfg3", "cfg4"):
+        return S.CONFIGS[int(name[3:])]
     raise KeyError(name)
 
 
@@ -36,6 +36,7 @@ class Case:
 
     def __init__(self, name: str, cam_index: int = 0, seed: int = 0):
         self.name = name
+        self.cam_index = cam_index
         self.cfg = case_config(name)
         self.scene = S.make_scene(self.cfg, seed=seed)
         fx, fy, cx, cy = self.scene.intrinsics
@@ -50,6 +51,12 @@ class Case:
         if self._gt is None:
             self._gt = O.render(self.scene.jittered().params(), self.degree, self.degree, self.bg, self.ocam)
         return self._gt
+
+    def product_camera(self, B):
+        """The camera as the product builds it (msplat_prepare_camera)."""
+        fx, fy, cx, cy = self.scene.intrinsics
+        return B.prepare_camera(self.scene.cam_to_world[self.cam_index], fx, fy, cx, cy, self.cfg.width,
+                                self.cfg.height)
 
     def oracle_forward(self):
         p = O.project_forward(*self.scene.params(), self.degree, self.degree, self.ocam)

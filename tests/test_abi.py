@@ -44,11 +44,10 @@ def test_library_exports_every_declared_symbol():
 
 def test_host_only_entry_points_work_without_gpu():
     from msplat import _backend as B
-    from msplat import camera_setup
     import numpy as np
-    cam = camera_setup.prepare_cam(B, np.eye(4, dtype=np.float32), 100.0, 100.0, 32.0, 24.0, 64, 48)
+    cam = B.prepare_camera(np.eye(4, dtype=np.float32), 100.0, 100.0, 32.0, 24.0, 64, 48)
     assert cam.width == 64 and cam.height == 48
     # identity camToWorld: the OpenGL->OpenCV flip makes the clip w = -z_world
     assert abs(cam.projmat[15]) < 1e-6 and cam.projmat[14] == -1.0
     with pytest.raises(B.MsplatError):
-        camera_setup.prepare_cam(B, np.eye(4, dtype=np.float32), -1.0, 100.0, 32.0, 24.0, 64, 48)
+        B.prepare_camera(np.eye(4, dtype=np.float32), -1.0, 100.0, 32.0, 24.0, 64, 48)
