@@ -323,8 +323,12 @@ int msplat_loss_ssim_noalloc(const float* out_img, const float* gt, const float*
  * final_idx, dL_dout_img, radii, depths, xys, transMats, normal_opacity,
  * colors, num_tiles_hit, tile_bins, gaussian_ids, raw_tile_counts, the
  * dL_d* gradients listed above, loss_partials (f64 [blocks,3]: l1, ssim,
- * distortion sums per loss block) and loss_terms (f64 [4]: loss, ssim sum,
- * l1 term, distortion term). Returns MSPLAT_ERR_ARGUMENT for an unknown
+ * distortion sums per loss block), loss_terms (f64 [4]: loss, ssim sum,
+ * l1 term, distortion term), raster_counters (i64 [4]: blended
+ * (pixel, surfel) pairs of the forward rasteriser, its (warp, surfel) visits
+ * past the cull, the backward's (warp, surfel) visits and its blended pairs;
+ * each visit evaluates 32 pixels) and intersection_totals (i64 [4]: emitted
+ * keys, kept intersections, band begin and end). Returns MSPLAT_ERR_ARGUMENT for an unknown
  * name or a tensor the last call did not produce. */
 int msplat_last_tensor(const char* name, MsplatTensorRef* out);
 

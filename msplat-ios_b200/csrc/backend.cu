@@ -81,7 +81,7 @@ struct Workspace {
     // per pixel
     Buf final_Ts, final_idx, out_img, out_depth, out_normal, out_alpha, out_median, out_dist, dL_dout_img;
     // scalars
-    Buf loss_partials, loss_out, loss_f, err, totals, row_work;
+    Buf loss_partials, loss_out, loss_f, err, totals, row_work, counters;
     int64_t* h_totals = nullptr;  // pinned [4]: raw, kept, band begin, band end
     uint32_t* h_err = nullptr;    // pinned [1]
     // shape bookkeeping of the last call
@@ -103,7 +103,7 @@ struct Workspace {
                       &dL_dfeatures_dc, &dL_dfeatures_rest, &dL_dopacity, &dL_dtransMat, &dL_dnormal3D,
                       &dL_dcolors, &tile_diff, &chunk_counts, &raw_true, &id_limit, &block_max, &raw_counts, &raw_start, &tile_bins, &fill, &raw_keys,
                       &gaussian_ids, &blend_mask, &final_Ts, &final_idx, &out_img, &out_depth, &out_normal, &out_alpha,
-                      &out_median, &out_dist, &dL_dout_img, &loss_partials, &loss_out, &loss_f, &err, &totals, &row_work};
+                      &out_median, &out_dist, &dL_dout_img, &loss_partials, &loss_out, &loss_f, &err, &totals, &row_work, &counters};
         for (Buf* b : all) b->release();
         for (auto& set : ev_pending)
             for (auto& m : set) cudaEventDestroy(m.second);
@@ -360,6 +360,9 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     ra.out_alpha = w.out_alpha.as<float>(); ra.out_median_depth = w.out_median.as<float>();
     ra.out_distortion = w.out_dist.as<float>();
     ra.blend_mask = w.blend_mask.as<uint8_t>();
+    w.counters.ensure(4 * sizeof(unsigned long long));
+    CK(cudaMemsetAsync(w.counters.p, 0, 4 * sizeof(unsigned long long), s));
+    ra.counters = w.counters.as<unsigned long long>();
     mark(w, kStRasterFwd, s);
     launch_rasterize_forward(ra, s);
     w.have_pixels = true;
@@ -406,6 +409,7 @@ void stage_raster_backward(Workspace& w, const CameraDev& cam, const float bg[3]
     ba.dL_dout_distortion = ldist * (1.0f / (float)((double)cam.height * (double)cam.width * 3.0)) * 3.0f;  // lambda_dist / HW
     ba.raster_grads = raster_grads;
     ba.blend_mask = w.blend_mask.as<uint8_t>();
+    ba.counters = w.counters.as<unsigned long long>();
     mark(w, kStRasterBwd, s);
     launch_rasterize_backward(ba, s);
 }
@@ -819,6 +823,8 @@ int msplat_last_tensor(const char* name, MsplatTensorRef* out) {
         else if (nm == "tile_bins") set(w.tile_bins, 1, {T, 2}, px);
         else if (nm == "raw_tile_counts") set(w.raw_true, 1, {T}, px);
         else if (nm == "gaussian_ids") set(w.gaussian_ids, 1, {w.kept}, px);
+        else if (nm == "raster_counters") set(w.counters, 2, {4}, px);
+        else if (nm == "intersection_totals") set(w.totals, 2, {4}, px);
         else if (nm == "xys") set(w.xys, 0, {n, 2}, rp);
         else if (nm == "transMats") set(w.transmats, 0, {n, 9}, rp);
         else if (nm == "normal_opacity") set(w.normal_opacity, 0, {n, 4}, rp);

@@ -138,6 +138,9 @@ struct RasterFwdArgs {
     // [kept intersections] one byte per tile-list entry: bit w set when warp w
     // of the tile's CTA blended that surfel (read by the backward)
     uint8_t* blend_mask;
+    // optional work counters (+=, may be null): [0] blended (pixel, surfel)
+    // pairs, [1] (warp, surfel) visits evaluated past the cull
+    unsigned long long* counters;
 };
 void launch_rasterize_forward(const RasterFwdArgs& a, cudaStream_t s);
 
@@ -155,6 +158,9 @@ struct RasterBwdArgs {
     float dL_dout_distortion;            // uniform per-pixel distortion gradient
     float* raster_grads;                 // [N, 16] (+=)
     const uint8_t* blend_mask;           // written by the forward over the same tiles
+    // optional work counters (+=, may be null): [2] (warp, surfel) visits,
+    // [3] blended (pixel, surfel) pairs replayed
+    unsigned long long* counters;
 };
 void launch_rasterize_backward(const RasterBwdArgs& a, cudaStream_t s);
 

@@ -153,6 +153,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
     bool done = !inside;
 
     int flush_b0 = -1;  // batch whose blend flags are still in sflag
+    unsigned n_visits = 0, n_blend = 0;  // work counters (visits are warp-uniform)
     for (int b0 = range.x; b0 < range.y; b0 += kThreads) {
         const bool all_done = __syncthreads_count(done) == kThreads;
         if (flush_b0 >= 0) flush_blend_flags(a.blend_mask, sflag, flush_b0, range.y);
@@ -194,6 +195,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
                 const float4 q1 = srec[1][s], q2 = srec[2][s];
                 const bool cand = (!done) & pair_stage1(px, py, srec[0][s], q1, q2, srec[4][s].z, e);
                 if (!__any_sync(full, cand)) continue;
+                ++n_visits;
                 if (!(pair_stage2<true>(q1, q2, e) & cand)) continue;
                 contributor = base + s;
                 const float next_T = fmul(T, fsub(1.0f, e.alpha));
@@ -222,6 +224,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
                 nz = ffma(r4.y, w, nz);
                 T = next_T;
                 last_c = contributor;
+                ++n_blend;
                 reinterpret_cast<uint8_t*>(&sflag[s])[warp] = 1;
             }
             if (__all_sync(full, done)) break;
@@ -230,6 +233,13 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
     if (flush_b0 >= 0) {
         __syncthreads();
         flush_blend_flags(a.blend_mask, sflag, flush_b0, range.y);
+    }
+    if (a.counters) {
+        const unsigned blended = __reduce_add_sync(full, n_blend);
+        if (lane == 0) {
+            atomicAdd(a.counters + 0, (unsigned long long)blended);
+            atomicAdd(a.counters + 1, (unsigned long long)n_visits);
+        }
     }
     if (!inside) return;
     const size_t pix = (size_t)i * a.width + j;
@@ -326,6 +336,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
     float accum_rec[3] = {0.f, 0.f, 0.f}, last_color[3] = {0.f, 0.f, 0.f}, last_alpha = 0.f;
     float accum_depth_rec = 0.f, last_depth = 0.f, accum_alpha_rec = 0.f, last_dL_dT = 0.f;
     float accum_normal_rec[3] = {0.f, 0.f, 0.f}, last_normal[3] = {0.f, 0.f, 0.f};
+    unsigned n_visits = 0, n_blend = 0;  // work counters (visits are warp-uniform)
 
     for (int bend = hi; bend > range.x; bend -= kThreads) {
         const int bs = min(kThreads, bend - range.x);
@@ -365,6 +376,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
                 const int s = c + __ffs(bits) - 1;
                 bits &= bits - 1;
                 const int rel = srel[s];
+                ++n_visits;
                 float g[16];
 #pragma unroll
                 for (int k = 0; k < 16; ++k) g[k] = 0.f;
@@ -372,6 +384,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
                 const float4 r0 = srec[0][s], r1 = srec[1][s], r2 = srec[2][s];
                 pair_stage1(px, py, r0, r1, r2, 0.f, e);
                 if ((rel < last_c) & pair_stage2<false>(r1, r2, e)) {
+                    ++n_blend;
                     const float4 r3 = srec[3][s], r4 = srec[4][s];
                     const float alpha = e.alpha, G = e.G, opa = r2.w;
                     const float r1ma = __fdividef(1.0f, 1.0f - alpha);
@@ -516,6 +529,13 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
                 if (p2.x != 0.f || p2.y != 0.f || p2.z != 0.f || p2.w != 0.f) atomicAdd(dst + 2, p2);
                 if (p3.x != 0.f) atomicAdd(dst + 3, p3);
             }
+        }
+    }
+    if (a.counters) {
+        const unsigned blended = __reduce_add_sync(full, n_blend);
+        if (lane == 0) {
+            atomicAdd(a.counters + 2, (unsigned long long)n_visits);
+            atomicAdd(a.counters + 3, (unsigned long long)blended);
         }
     }
 }

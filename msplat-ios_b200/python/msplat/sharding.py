@@ -148,7 +148,7 @@ class PeerParams:
 
 
 def sharded_step(dist, plan: ShardPlan, forward_backward, project_adam, rg, rg_shard, param_fulls, parts,
-                 side_stream=None, skip_color=False, colors_next=None, rgb_full=None):
+                 side_stream=None, skip_color=False, colors_next=None, rgb_full=None, marks=None):
     """One training step across ranks.
 
     forward_backward(plan, rg, parts): fills rg [padded, 16] with this rank's
@@ -173,14 +173,21 @@ def sharded_step(dist, plan: ShardPlan, forward_backward, project_adam, rg, rg_s
         all-gathered on side_stream (12 B per Gaussian instead of the 192 B of
         colour coefficients) and the returned event marks its arrival. Use
         with skip_color=True.
+    marks(name): optional, called on the host after each phase is enqueued
+        ("forward_backward", "reduce_scatter", "project_adam", "all_gather",
+        "all_reduce"), e.g. to record CUDA events between the phases.
     Every rank issues the collectives in the same order.
     """
+    mark = marks if marks is not None else (lambda name: None)
     forward_backward(plan, rg, parts)
+    mark("forward_backward")
     dist.reduce_scatter_tensor(rg_shard, rg, op=dist.ReduceOp.SUM)
+    mark("reduce_scatter")
     project_adam(plan.g_begin, plan.g_end, rg_shard)
     rows = plan.slice_rows()
     if colors_next is not None:
         colors_next(plan.g_begin, plan.g_end)
+    mark("project_adam")
     late = [rgb_full] if rgb_full is not None else []
     for k, full in enumerate(param_fulls):
         if full.numel() == 0 or (skip_color and k in COLOR_GROUPS):
@@ -189,7 +196,9 @@ def sharded_step(dist, plan: ShardPlan, forward_backward, project_adam, rg, rg_s
             late.append(full)
             continue
         dist.all_gather_into_tensor(full, full[rows])
+    mark("all_gather")
     dist.all_reduce(parts)
+    mark("all_reduce")
     if not late:
         return None
     if side_stream is None:

@@ -559,6 +559,9 @@ namespace {
 // Tile-row sampling used only by orc_time_step_sample: rows of tiles whose
 // index is not a multiple of g_row_stride are skipped.
 thread_local int g_row_stride = 1;
+// Pixel rows at or below this limit are skipped by the forward (render of a
+// band, for the reference arm's sampled target). Read on the calling thread.
+thread_local int g_row_limit = 1 << 30;
 }  // namespace
 
 void orc_rasterize_forward(int width, int height, int tiles_x, const int32_t* tile_bins,
@@ -569,10 +572,11 @@ void orc_rasterize_forward(int width, int height, int tiles_x, const int32_t* ti
                            float* out_median_depth, float* out_distortion) {
     const float mscale = kFarN / (kFarN - kNearN);
     const int row_stride = g_row_stride;
+    const int row_limit = g_row_limit;
 #pragma omp parallel for schedule(dynamic, 64)
     for (int64_t pix = 0; pix < (int64_t)width * height; ++pix) {
         int i = (int)(pix / width), j = (int)(pix % width);
-        if ((i / kTile) % row_stride != 0) continue;
+        if ((i / kTile) % row_stride != 0 || i >= row_limit) continue;
         int tile = (i / kTile) * tiles_x + (j / kTile);
         float px = (float)j, py = (float)i;
         int start = tile_bins[2 * tile], end = tile_bins[2 * tile + 1];
@@ -975,6 +979,16 @@ void orc_render(int n, const float* means, const float* scales, const float* qua
                 int degrees_to_use, const float* background, const OrcCamera* cam, float* out_img) {
     Forward F;
     run_forward(n, means, scales, quats, opacities, f_dc, f_rest, degree, degrees_to_use, background, cam, F);
+    std::memcpy(out_img, F.out_img.data(), F.out_img.size() * sizeof(float));
+}
+
+void orc_render_rows(int n, const float* means, const float* scales, const float* quats, const float* opacities,
+                     const float* f_dc, const float* f_rest, int degree, int degrees_to_use,
+                     const float* background, const OrcCamera* cam, int pixel_rows, float* out_img) {
+    g_row_limit = pixel_rows;
+    Forward F;
+    run_forward(n, means, scales, quats, opacities, f_dc, f_rest, degree, degrees_to_use, background, cam, F);
+    g_row_limit = 1 << 30;
     std::memcpy(out_img, F.out_img.data(), F.out_img.size() * sizeof(float));
 }
 

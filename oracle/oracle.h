@@ -172,10 +172,16 @@ void orc_render(int n, const float* means, const float* scales, const float* qua
                 int degree, int degrees_to_use, const float* background,
                 const OrcCamera* cam, float* out_img);
 
+/* orc_render restricted to pixel rows [0, pixel_rows) (the other rows are
+ * left at zero): the target band of orc_time_step_sample's loss. */
+void orc_render_rows(int n, const float* means, const float* scales, const float* quats, const float* opacities,
+                     const float* f_dc, const float* f_rest, int degree, int degrees_to_use,
+                     const float* background, const OrcCamera* cam, int pixel_rows, float* out_img);
+
 /* Times one training step on a bounded sample of the workload, for the CPU
  * baseline: projection, binning, projection VJP and Adam on all N Gaussians;
  * rasterisation forward/backward on every tile_row_stride-th row of tiles and
- * the loss on a band of H / tile_row_stride pixel rows, both scaled back by
+ * the loss on pixel rows [0, H / tile_row_stride), both scaled back by
  * the stride. Parameters are updated in place (values are not checked).
  * Returns the estimated seconds of one full step; stage_seconds[7] receives
  * project, bin+sort+pack, raster fwd, loss, raster bwd, projection VJP, Adam. */

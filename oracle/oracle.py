@@ -96,6 +96,8 @@ def lib():
                                      C.POINTER(C.c_int64)]
         L.orc_render.argtypes = [C.c_int, f32p, f32p, f32p, f32p, f32p, f32p, C.c_int, C.c_int, f32p,
                                  C.POINTER(OrcCamera), f32p]
+        L.orc_render_rows.argtypes = [C.c_int, f32p, f32p, f32p, f32p, f32p, f32p, C.c_int, C.c_int, f32p,
+                                      C.POINTER(OrcCamera), C.c_int, f32p]
         L.orc_time_step_sample.restype = C.c_double
         L.orc_time_step_sample.argtypes = [C.POINTER(OrcStepArgs), C.POINTER(OrcCamera), C.c_int,
                                            C.POINTER(C.c_double)]
@@ -272,6 +274,17 @@ def render(scene_params, degree, degrees_to_use, background, cam):
     lib().orc_render(n, _c(means), _c(scales), _c(quats), _c(opac).reshape(-1), _c(f_dc),
                      _c(f_rest).reshape(-1) if f_rest.size else np.zeros(1, np.float32), degree, degrees_to_use,
                      _c(background), C.byref(cam), out)
+    return out
+
+
+def render_rows(scene_params, degree, degrees_to_use, background, cam, pixel_rows):
+    """render() of pixel rows [0, pixel_rows) only (other rows zero)."""
+    means, scales, quats, opac, f_dc, f_rest = scene_params
+    n = means.shape[0]
+    out = np.zeros((cam.height, cam.width, 3), np.float32)
+    lib().orc_render_rows(n, _c(means), _c(scales), _c(quats), _c(opac).reshape(-1), _c(f_dc),
+                          _c(f_rest).reshape(-1) if f_rest.size else np.zeros(1, np.float32), degree, degrees_to_use,
+                          _c(background), C.byref(cam), int(pixel_rows), out)
     return out
 
 
