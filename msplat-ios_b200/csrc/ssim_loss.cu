@@ -24,7 +24,9 @@
 // Each thread owns one (channel, column) item of S2/S3 and one of S4/S5; the
 // 11-row windows of its moments and partials live in registers (the step loop
 // is unrolled 11 times so that every ring index is a constant), so the only
-// shared-memory traffic is the horizontal taps. The only recomputed halo is
+// shared-memory traffic is the horizontal taps. Paired quantities ((image,
+// target) moments, (g_mu1, g_sigma1^2) partials) use sm_100's packed FP32
+// multiply-adds. The only recomputed halo is
 // 10 columns per strip and 22 rows per segment. The image and target are read
 // once and dL/dimg is written once; no [H,W,3] intermediate touches HBM. Loss
 // partial sums are reduced per CTA in double and summed in a fixed order
@@ -80,9 +82,16 @@ LossGrid loss_grid(int width, int rows, int max_blocks = 0) {
     return g;
 }
 
+// (image, target) pairs and the partial pairs are processed with the packed
+// FP32 instructions of sm_100 (__ffma2_rn / __fmul2_rn: each component is
+// rounded exactly as the scalar fmaf / fmul), which halve the instructions of
+// the paired blurs.
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+
 __global__ void __launch_bounds__(kThreads, 2) k_loss_ssim(LossArgs a, int seg_rows) {
-    __shared__ float sIn[2][2][3][IWID];  // [buffer][image, target][channel][column]
-    __shared__ float sP[2][3][3][CW];     // [buffer][partial][channel][column]
+    __shared__ float2 sIn[2][3][IWID];    // [buffer][channel][column]: (image, target)
+    __shared__ float2 sPa[2][3][CW];      // [buffer][channel][column]: (g_mu1, g_sigma1^2)
+    __shared__ float sPb[2][3][CW];       // [buffer][channel][column]: g_sigma12
     __shared__ double red[3][kThreads];
     const int W = a.width, H = a.height;
     const int t = threadIdx.x;
@@ -103,45 +112,40 @@ __global__ void __launch_bounds__(kThreads, 2) k_loss_ssim(LossArgs a, int seg_r
     const float g = -a.lambda_dssim * a.inv_num;
     double l1_sum = 0.0, ssim_sum = 0.0, dist_sum = 0.0;
 
-    float hm[kRing][5], hp[kRing][3];
+    // register rings of the vertical windows: moments (img, gt), (img^2,
+    // gt^2), img*gt; partials (g_mu1, g_sigma1^2), g_sigma12
+    float2 hm01[kRing], hm23[kRing], hp01[kRing];
+    float hm4[kRing], hp2[kRing];
 #pragma unroll
     for (int k = 0; k < kRing; ++k) {
-#pragma unroll
-        for (int m = 0; m < 5; ++m) hm[k][m] = 0.f;
-#pragma unroll
-        for (int m = 0; m < 3; ++m) hp[k][m] = 0.f;
+        hm01[k] = f2(0.f, 0.f); hm23[k] = f2(0.f, 0.f); hm4[k] = 0.f;
+        hp01[k] = f2(0.f, 0.f); hp2[k] = 0.f;
     }
     // S1 of one row: each thread moves up to two (image, target) pairs of the
     // contiguous span [x0-10, x0+SW+10) x 3 channels
     constexpr int kSpan = 3 * IWID;
     static_assert(kSpan <= 2 * kThreads, "two loads per thread");
-    auto fetch = [&](int y, float (&v)[2][2]) {
+    auto fetch = [&](int y, float2 (&v)[2]) {
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
             const int q = t + u * kThreads;
             const int xx = x0 - 2 * R + q / 3;
-            v[u][0] = 0.f;
-            v[u][1] = 0.f;
+            v[u] = f2(0.f, 0.f);
             if (q < kSpan && y >= 0 && y < H && xx >= 0 && xx < W) {
                 const size_t e = ((size_t)y * W + xx) * 3 + (q - (q / 3) * 3);
-                v[u][0] = __ldg(a.out_img + e);
-                v[u][1] = __ldg(a.gt + e);
+                v[u] = f2(__ldg(a.out_img + e), __ldg(a.gt + e));
             }
         }
     };
-    auto stash = [&](int buf, const float (&v)[2][2]) {
+    auto stash = [&](int buf, const float2 (&v)[2]) {
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
             const int q = t + u * kThreads;
-            if (q < kSpan) {
-                const int c = q % 3, xc = q / 3;
-                sIn[buf][0][c][xc] = v[u][0];
-                sIn[buf][1][c][xc] = v[u][1];
-            }
+            if (q < kSpan) sIn[buf][q % 3][q / 3] = v[u];
         }
     };
     {
-        float v[2][2];
+        float2 v[2];
         fetch(ybase, v);
         stash(0, v);
     }
@@ -152,40 +156,41 @@ __global__ void __launch_bounds__(kThreads, 2) k_loss_ssim(LossArgs a, int seg_r
         for (int k = 0; k < kRing; ++k) {
             const int step = t0 + k;  // sIn[step & 1] holds input row ybase + step
             // S1 (issued first, stored last): input row ybase + step + 1
-            float nv[2][2];
+            float2 nv[2];
             fetch(ybase + step + 1, nv);
             // S2: moments of input row ybase + step
             {
-                const float* pi = &sIn[step & 1][0][ch][col];
-                const float* pg = &sIn[step & 1][1][ch][col];
-                float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f, m4 = 0.f;
+                const float2* pin = &sIn[step & 1][ch][col];
+                float2 m01 = f2(0.f, 0.f), m23 = f2(0.f, 0.f);
+                float m4 = 0.f;
 #pragma unroll
                 for (int j = 0; j < kRing; ++j) {
-                    const float w = kW[j], x = pi[j], y = pg[j];
-                    m0 += w * x;
-                    m1 += w * y;
-                    m2 += w * (x * x);
-                    m3 += w * (y * y);
-                    m4 += w * (x * y);
+                    const float w = kW[j];
+                    const float2 w2 = f2(w, w), xy = pin[j];
+                    m01 = __ffma2_rn(w2, xy, m01);
+                    m23 = __ffma2_rn(w2, __fmul2_rn(xy, xy), m23);
+                    m4 = fmaf(w, xy.x * xy.y, m4);
                 }
-                float* slot = hm[k];
-                slot[0] = m0; slot[1] = m1; slot[2] = m2; slot[3] = m3; slot[4] = m4;
+                hm01[k] = m01; hm23[k] = m23; hm4[k] = m4;
             }
             // S3: SSIM partials of row ybase + step - 5 from moment rows
             // ybase + step - 10 .. ybase + step (ring slots k+1 .. k+11)
             {
                 const int cy = ybase + step - R;
-                float acc[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+                float2 a01 = f2(0.f, 0.f), a23 = f2(0.f, 0.f);
+                float a4 = 0.f;
 #pragma unroll
                 for (int j = 0; j < kRing; ++j) {
                     const float w = kW[j];
-                    const float* slot = hm[(k + 1 + j) % kRing];
-#pragma unroll
-                    for (int m = 0; m < 5; ++m) acc[m] += w * slot[m];
+                    const float2 w2 = f2(w, w);
+                    const int sl = (k + 1 + j) % kRing;
+                    a01 = __ffma2_rn(w2, hm01[sl], a01);
+                    a23 = __ffma2_rn(w2, hm23[sl], a23);
+                    a4 = fmaf(w, hm4[sl], a4);
                 }
                 float gm1 = 0.f, gs1 = 0.f, g12 = 0.f;
                 if (cy >= 0 && cy < H && xm >= 0 && xm < W) {
-                    const float mu1 = acc[0], mu2 = acc[1], b11 = acc[2], b22 = acc[3], b12 = acc[4];
+                    const float mu1 = a01.x, mu2 = a01.y, b11 = a23.x, b22 = a23.y, b12 = a4;
                     // Separately rounded operations: sigma1^2, sigma2^2 and
                     // sigma12 must round identically where img == gt (flat
                     // background), where the reference's SSIM is exactly 1.
@@ -195,8 +200,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_loss_ssim(LossArgs a, int seg_r
                     const float Cd = fadd(fadd(m1s, m2s), C1), Dd = fadd(fadd(v1, v2), C2);
                     const float CD = fmul(Cd, Dd), AB = fmul(A, B);
                     if (own_col && cy >= Y0 && cy < Y1) ssim_sum += (double)(AB / CD);
-                    const float inv_CD = __fdividef(1.0f, CD), inv_Cd = __fdividef(1.0f, Cd);
-                    const float inv_Dd = __fdividef(1.0f, Dd);
+                    // 1/Cd and 1/Dd from 1/CD: one approximate reciprocal
+                    const float inv_CD = __fdividef(1.0f, CD);
+                    const float inv_Cd = Dd * inv_CD, inv_Dd = Cd * inv_CD;
                     const float d_mu1 = 2.0f * inv_CD * (mu2 * B - mu1 * AB * inv_Cd);
                     const float d_s12 = 2.0f * A * inv_CD;
                     const float d_s1 = -AB * inv_CD * inv_Dd;
@@ -204,35 +210,39 @@ __global__ void __launch_bounds__(kThreads, 2) k_loss_ssim(LossArgs a, int seg_r
                     g12 = g * d_s12;
                     gm1 = g * d_mu1 + gs1 * (-2.0f * mu1) + g12 * (-mu2);
                 }
-                sP[step & 1][0][ch][col] = gm1;
-                sP[step & 1][1][ch][col] = gs1;
-                sP[step & 1][2][ch][col] = g12;
+                sPa[step & 1][ch][col] = f2(gm1, gs1);
+                sPb[step & 1][ch][col] = g12;
             }
             if (out_item) {
                 // S4: horizontal blur of the partials of row ybase + step - 6
                 // (written last step) into ring slot k
                 const int pb = (step + 1) & 1;
+                const float2* pa = &sPa[pb][och][ocol];
+                const float* pbb = &sPb[pb][och][ocol];
+                float2 acc01 = f2(0.f, 0.f);
+                float acc2 = 0.f;
 #pragma unroll
-                for (int m = 0; m < 3; ++m) {
-                    const float* src = &sP[pb][m][och][ocol];
-                    float acc = 0.f;
-#pragma unroll
-                    for (int j = 0; j < kRing; ++j) acc += kW[j] * src[j];
-                    hp[k][m] = acc;
+                for (int j = 0; j < kRing; ++j) {
+                    const float w = kW[j];
+                    acc01 = __ffma2_rn(f2(w, w), pa[j], acc01);
+                    acc2 = fmaf(w, pbb[j], acc2);
                 }
+                hp01[k] = acc01;
+                hp2[k] = acc2;
                 // S5: dL/dimg of row ybase + step - 11 from partial rows
                 // ybase + step - 16 .. ybase + step - 6 (slots k+1 .. k+11)
                 const int oy = ybase + step - 2 * R - 1;
                 if (oy >= Y0 && oy < Y1 && xo < W) {
-                    float bm1 = 0.f, bs1 = 0.f, b12 = 0.f;
+                    float2 b01 = f2(0.f, 0.f);
+                    float b12 = 0.f;
 #pragma unroll
                     for (int j = 0; j < kRing; ++j) {
                         const float w = kW[j];
-                        const float* slot = hp[(k + 1 + j) % kRing];
-                        bm1 += w * slot[0];
-                        bs1 += w * slot[1];
-                        b12 += w * slot[2];
+                        const int sl = (k + 1 + j) % kRing;
+                        b01 = __ffma2_rn(f2(w, w), hp01[sl], b01);
+                        b12 = fmaf(w, hp2[sl], b12);
                     }
+                    const float bm1 = b01.x, bs1 = b01.y;
                     const size_t pix = (size_t)oy * W + xo;
                     const float va = __ldg(a.out_img + pix * 3 + och), vb = __ldg(a.gt + pix * 3 + och);
                     const float diff = va - vb;
