@@ -478,8 +478,13 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
                 if (vi < NV) {
                     const float4* row = reinterpret_cast<const float4*>(wb + vi * 36 + (lane & 1) * 16);
                     const float4 q0 = row[0], q1 = row[1], q2 = row[2], q3 = row[3];
-                    tot = ((q0.x + q0.y) + (q0.z + q0.w)) + ((q1.x + q1.y) + (q1.z + q1.w)) +
-                          (((q2.x + q2.y) + (q2.z + q2.w)) + ((q3.x + q3.y) + (q3.z + q3.w)));
+                    // pairwise tree with sm_100 packed FP32 adds
+                    const float2 s0 = __fadd2_rn(make_float2(q0.x, q0.y), make_float2(q0.z, q0.w));
+                    const float2 s1 = __fadd2_rn(make_float2(q1.x, q1.y), make_float2(q1.z, q1.w));
+                    const float2 s2 = __fadd2_rn(make_float2(q2.x, q2.y), make_float2(q2.z, q2.w));
+                    const float2 s3 = __fadd2_rn(make_float2(q3.x, q3.y), make_float2(q3.z, q3.w));
+                    const float2 s = __fadd2_rn(__fadd2_rn(s0, s1), __fadd2_rn(s2, s3));
+                    tot = s.x + s.y;
                 }
                 tot += __shfl_xor_sync(full, tot, 1);
                 __syncwarp();
