@@ -126,7 +126,12 @@ int msplat_fused_adam(float* params, const float* grads, float* exp_avg, float* 
  * moments are updated in place. The loss is written to loss_dev (a device
  * float) and the call does not wait for the GPU beyond one small read of the
  * intersection count. write_grads != 0 additionally materialises the
- * reference-shaped gradients in the workspace. */
+ * reference-shaped gradients in the workspace. With lambda_dist == 0 and
+ * write_grads == 0 the forward computes only what the step reads (the
+ * image, the final transmittance and the last contributor): the depth,
+ * normal, alpha, median-depth and distortion outputs, final_Ts channels 1-2
+ * and final_idx channel 1 are not produced (msplat_last_tensor reports them
+ * as not produced by the last call). */
 int msplat_train_step_fused(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
                             const float background[3], const float* gt, float lambda_l1, float lambda_dist,
                             float lambda_dssim, const MsplatAdamState* adam, float* xys_grad_norm,

@@ -96,6 +96,9 @@ struct Workspace {
     std::vector<std::vector<std::pair<int, cudaEvent_t>>> ev_pending;
     std::vector<cudaEvent_t> ev_pool;
     bool have_ref_proj = false, have_grads = false, have_pixels = false, have_dimg = false;
+    // the last forward wrote every per-pixel output (not only the image, T and
+    // the last contributor that a colour-only training step reads)
+    bool have_aux = false;
 
     void release_all() {
         Buf* all[] = {&records, &cull, &rects, &depths, &radii, &raster_grads, &xys, &transmats, &num_tiles_hit,
@@ -231,7 +234,8 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
                    float glob_scale, float clip, const float bg[3], bool ref_outputs, int row0, int row1,
                    cudaStream_t s, int balance_world = 0, int balance_rank = 0, int* owned0 = nullptr,
                    int* owned1 = nullptr, bool split_color = false, cudaEvent_t features_ready = nullptr,
-                   const MsplatPeerParams* peers = nullptr, const float* rgb_in = nullptr) {
+                   const MsplatPeerParams* peers = nullptr, const float* rgb_in = nullptr,
+                   bool aux_out = true) {
     const int n = g->num_points;
     const int K = sh_rest_bases(g->sh_degree);
     const int tx = cam.tiles_x, ty = cam.tiles_y, T = tx * ty;
@@ -239,6 +243,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     w.n = n; w.K = K; w.W = cam.width; w.H = cam.height; w.tx = tx; w.ty = ty;
     w.flags = 0;
     w.have_ref_proj = ref_outputs;
+    w.have_aux = aux_out;
     w.have_grads = false;
     w.have_dimg = false;
     const size_t nn = (size_t)(n > 0 ? n : 1);
@@ -363,6 +368,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     w.counters.ensure(4 * sizeof(unsigned long long));
     CK(cudaMemsetAsync(w.counters.p, 0, 4 * sizeof(unsigned long long), s));
     ra.counters = w.counters.as<unsigned long long>();
+    ra.aux_outputs = aux_out ? 1 : 0;
     mark(w, kStRasterFwd, s);
     launch_rasterize_forward(ra, s);
     w.have_pixels = true;
@@ -562,7 +568,11 @@ int msplat_train_step_fused(const MsplatGaussians* g, const MsplatCamera* cam, i
         Workspace& w = workspace();
         CameraDev cd = make_cam(cam);
         const int n = g->num_points;
-        stage_forward(w, g, cd, degrees_to_use, 1.0f, 0.01f, background, write_grads != 0, 0, cd.tiles_y, s);
+        // a colour-only step that returns no gradients reads only the image,
+        // T and the last contributor of the forward
+        const bool aux = write_grads != 0 || lambda_dist != 0.0f;
+        stage_forward(w, g, cd, degrees_to_use, 1.0f, 0.01f, background, write_grads != 0, 0, cd.tiles_y, s, 0, 0,
+                      nullptr, nullptr, false, nullptr, nullptr, nullptr, aux);
         stage_loss(w, cd, gt, lambda_l1, lambda_dist, lambda_dssim, 0, cd.height, true, s);
         const size_t nn = (size_t)(n > 0 ? n : 1);
         w.raster_grads.ensure(nn * kGradStride * 4);
@@ -694,7 +704,8 @@ int shard_forward_backward_impl(const MsplatGaussians* g, const MsplatPeerParams
         const int n = g->num_points;
         const int r0 = std::max(0, o0 - 1), r1 = std::min(cd.tiles_y, o1 + 1);
         stage_forward(w, g, cd, degrees_to_use, 1.0f, 0.01f, background, false, r0, r1, s, world, rank, &o0, &o1,
-                      split_color != 0, static_cast<cudaEvent_t>(features_ready), peers, rgb_in);
+                      split_color != 0, static_cast<cudaEvent_t>(features_ready), peers, rgb_in,
+                      lambda_dist != 0.0f);
         tile_rows[0] = o0;
         tile_rows[1] = o1;
         const int p0 = std::min(cd.height, o0 * kTile), p1 = std::min(cd.height, o1 * kTile);
@@ -808,15 +819,15 @@ int msplat_last_tensor(const char* name, MsplatTensorRef* out) {
             for (int64_t d : shape) out->shape[k++] = d;
             for (; k < 4; ++k) out->shape[k] = 0;
         };
-        const bool px = w.have_pixels, rp = w.have_ref_proj, gr = w.have_grads;
+        const bool px = w.have_pixels, rp = w.have_ref_proj, gr = w.have_grads, ax = px && w.have_aux;
         if (nm == "out_img") set(w.out_img, 0, {H, W, 3}, px);
-        else if (nm == "out_depth") set(w.out_depth, 0, {H, W}, px);
-        else if (nm == "out_normal") set(w.out_normal, 0, {H, W, 3}, px);
-        else if (nm == "out_alpha") set(w.out_alpha, 0, {H, W}, px);
-        else if (nm == "out_median_depth") set(w.out_median, 0, {H, W}, px);
-        else if (nm == "out_distortion") set(w.out_dist, 0, {H, W}, px);
-        else if (nm == "final_Ts") set(w.final_Ts, 0, {H, W, 3}, px);
-        else if (nm == "final_idx") set(w.final_idx, 1, {H, W, 2}, px);
+        else if (nm == "out_depth") set(w.out_depth, 0, {H, W}, ax);
+        else if (nm == "out_normal") set(w.out_normal, 0, {H, W, 3}, ax);
+        else if (nm == "out_alpha") set(w.out_alpha, 0, {H, W}, ax);
+        else if (nm == "out_median_depth") set(w.out_median, 0, {H, W}, ax);
+        else if (nm == "out_distortion") set(w.out_dist, 0, {H, W}, ax);
+        else if (nm == "final_Ts") set(w.final_Ts, 0, {H, W, 3}, ax);
+        else if (nm == "final_idx") set(w.final_idx, 1, {H, W, 2}, ax);
         else if (nm == "dL_dout_img") set(w.dL_dout_img, 0, {H, W, 3}, w.have_dimg);
         else if (nm == "radii") set(w.radii, 1, {n}, px);
         else if (nm == "depths") set(w.depths, 0, {n}, px);

@@ -141,6 +141,10 @@ struct RasterFwdArgs {
     // optional work counters (+=, may be null): [0] blended (pixel, surfel)
     // pairs, [1] (warp, surfel) visits evaluated past the cull
     unsigned long long* counters;
+    // 1: every output of the reference's forward; 0: only out_img, final_Ts
+    // channel 0 (T) and final_idx channel 0 (last contributor), which is all a
+    // colour-only training step reads
+    int aux_outputs;
 };
 void launch_rasterize_forward(const RasterFwdArgs& a, cudaStream_t s);
 

@@ -94,7 +94,7 @@ __device__ void cull_record(V3 tu, V3 tv, V3 tw, float rmax, float4* out) {
     out[1] = c1;
 }
 
-__global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
+__global__ void __launch_bounds__(256, 4) k_project_forward(ProjFwdArgs a) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= a.n) return;
     const CameraDev& cam = a.cam;
@@ -132,12 +132,21 @@ __global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
         for (int k = 0; k < 3; ++k) a.colors[3 * i + k] = 0.f;
         a.aabb[2 * i] = 0.f; a.aabb[2 * i + 1] = 0.f;
     }
-    V3 p = v3(pp.means[3 * i], pp.means[3 * i + 1], pp.means[3 * i + 2]);
+    // every parameter load is issued before the first dependent arithmetic
+    V3 p = v3(__ldg(pp.means + 3 * i), __ldg(pp.means + 3 * i + 1), __ldg(pp.means + 3 * i + 2));
+    const float s0 = __ldg(pp.scales + 2 * i), s1 = __ldg(pp.scales + 2 * i + 1);
+    float q[4];
+    if ((reinterpret_cast<uintptr_t>(pp.quats) & 15) == 0) {
+        const float4 qv = __ldg(reinterpret_cast<const float4*>(pp.quats) + i);
+        q[0] = qv.x; q[1] = qv.y; q[2] = qv.z; q[3] = qv.w;
+    } else {
+        for (int k = 0; k < 4; ++k) q[k] = __ldg(pp.quats + 4 * i + k);
+    }
+    const float opac_raw = __ldg(pp.opacities + i);
     float pvz = vm[8] * p.x + vm[9] * p.y + vm[10] * p.z + vm[11];
     if (pvz <= a.clip_thresh) return;
-    float sx = det_exp(pp.scales[2 * i]) * a.glob_scale;
-    float sy = det_exp(pp.scales[2 * i + 1]) * a.glob_scale;
-    float q[4] = {pp.quats[4 * i], pp.quats[4 * i + 1], pp.quats[4 * i + 2], pp.quats[4 * i + 3]};
+    float sx = det_exp(s0) * a.glob_scale;
+    float sy = det_exp(s1) * a.glob_scale;
     V3 R[3];
     quat_to_rotmat(q, R);
     V3 tu = scale3(R[0], sx), tv = scale3(R[1], sy);
@@ -184,7 +193,6 @@ __global__ void __launch_bounds__(256) k_project_forward(ProjFwdArgs a) {
 
     float col[3] = {0.f, 0.f, 0.f}, rgb[3] = {0.f, 0.f, 0.f};
     if (a.pass == 0) gaussian_color(a, pp, i, p, col, rgb);
-    float opac_raw = pp.opacities[i];
     float opac = 1.f / (1.f + det_exp(-opac_raw));
     V3 nrm = R[2];
     rec[0] = make_float4(T0.x, T0.y, T0.z, T1.x);

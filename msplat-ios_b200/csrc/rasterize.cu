@@ -126,6 +126,10 @@ __device__ __forceinline__ void flush_blend_flags(uint8_t* mask, const uint2* sf
     mask[idx] = (uint8_t)m;
 }
 
+// AUXOUT: every output of the reference's forward; otherwise only what a
+// colour-only training step consumes (the image, the final transmittance and
+// the last contributor), skipping depth, normal, median and distortion.
+template <bool AUXOUT>
 __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
     __shared__ float4 srec[kRecordF4][kThreads];
     __shared__ float4 scull[kCullF4][kThreads];
@@ -204,24 +208,29 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
                     continue;
                 }
                 const float w = fmul(e.alpha, T);
-                const float A = fsub(1.f, T);
-                const float m = fmul(mscale, fsub(1.f, __fdiv_rn(kNearN, e.depth)));
-                const float mm = fmul(m, m);
-                dist = ffma(fsub(fadd(fmul(mm, A), M2), fmul(fmul(2.f, m), M1)), w, dist);
-                M1 = ffma(m, w, M1);
-                M2 = ffma(mm, w, M2);
-                if (T > 0.5f) {
-                    median_depth = e.depth;
-                    median_c = contributor;
+                if constexpr (AUXOUT) {
+                    const float A = fsub(1.f, T);
+                    const float m = fmul(mscale, fsub(1.f, __fdiv_rn(kNearN, e.depth)));
+                    const float mm = fmul(m, m);
+                    dist = ffma(fsub(fadd(fmul(mm, A), M2), fmul(fmul(2.f, m), M1)), w, dist);
+                    M1 = ffma(m, w, M1);
+                    M2 = ffma(mm, w, M2);
+                    if (T > 0.5f) {
+                        median_depth = e.depth;
+                        median_c = contributor;
+                    }
                 }
-                const float4 r3 = srec[3][s], r4 = srec[4][s];
+                const float4 r3 = srec[3][s];
                 cr = ffma(r3.x, w, cr);
                 cg = ffma(r3.y, w, cg);
                 cb = ffma(r3.z, w, cb);
-                pdepth = ffma(e.depth, w, pdepth);
-                nx = ffma(r3.w, w, nx);
-                ny = ffma(r4.x, w, ny);
-                nz = ffma(r4.y, w, nz);
+                if constexpr (AUXOUT) {
+                    const float4 r4 = srec[4][s];
+                    pdepth = ffma(e.depth, w, pdepth);
+                    nx = ffma(r3.w, w, nx);
+                    ny = ffma(r4.x, w, ny);
+                    nz = ffma(r4.y, w, nz);
+                }
                 T = next_T;
                 last_c = contributor;
                 ++n_blend;
@@ -244,13 +253,14 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
     if (!inside) return;
     const size_t pix = (size_t)i * a.width + j;
     a.final_Ts[3 * pix + 0] = T;
-    a.final_Ts[3 * pix + 1] = M1;
-    a.final_Ts[3 * pix + 2] = M2;
     a.final_idx[2 * pix + 0] = last_c;
-    a.final_idx[2 * pix + 1] = median_c;
     a.out_img[3 * pix + 0] = ffma(a.bg[0], T, cr);
     a.out_img[3 * pix + 1] = ffma(a.bg[1], T, cg);
     a.out_img[3 * pix + 2] = ffma(a.bg[2], T, cb);
+    if (!AUXOUT) return;
+    a.final_Ts[3 * pix + 1] = M1;
+    a.final_Ts[3 * pix + 2] = M2;
+    a.final_idx[2 * pix + 1] = median_c;
     a.out_depth[pix] = pdepth;
     a.out_normal[3 * pix + 0] = nx;
     a.out_normal[3 * pix + 1] = ny;
@@ -309,10 +319,12 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
     const float dL_dreg = a.dL_dout_distortion;
     if (inside) {
         T_final = a.final_Ts[3 * pix];
-        final_D = a.final_Ts[3 * pix + 1];
-        final_D2 = a.final_Ts[3 * pix + 2];
         last_c = a.final_idx[2 * pix];
-        median_c = a.final_idx[2 * pix + 1];
+        if (AUX) {
+            final_D = a.final_Ts[3 * pix + 1];
+            final_D2 = a.final_Ts[3 * pix + 2];
+            median_c = a.final_idx[2 * pix + 1];
+        }
         dpix[0] = a.dL_dout_img[3 * pix];
         dpix[1] = a.dL_dout_img[3 * pix + 1];
         dpix[2] = a.dL_dout_img[3 * pix + 2];
@@ -551,7 +563,10 @@ void launch_rasterize_forward(const RasterFwdArgs& a, cudaStream_t s) {
     const int rows = a.tile_row_end - a.tile_row_begin;
     if (rows <= 0 || a.tiles_x <= 0) return;
     note_launches(1);
-    k_raster_fwd<<<dim3(a.tiles_x, rows), kThreads, 0, s>>>(a);
+    if (a.aux_outputs)
+        k_raster_fwd<true><<<dim3(a.tiles_x, rows), kThreads, 0, s>>>(a);
+    else
+        k_raster_fwd<false><<<dim3(a.tiles_x, rows), kThreads, 0, s>>>(a);
 }
 
 void launch_rasterize_backward(const RasterBwdArgs& a, cudaStream_t s) {

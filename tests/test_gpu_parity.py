@@ -228,3 +228,32 @@ def test_errors_are_reported_not_raised_through_the_abi():
     assert "degrees_to_use" in str(ei.value)
     with pytest.raises(B.MsplatError):
         B.last_tensor("no_such_tensor")
+
+
+def test_fused_step_light_forward_matches_full_forward():
+    """A colour-only fused step that returns no gradients computes only the
+    forward outputs it reads (image, T, last contributor). Its loss, image and
+    updated parameters equal the same step with every forward output
+    (write_grads=True), and the skipped outputs are reported as not produced."""
+    case = Case("sh3_small")
+    B = _B()
+    cam = B.camera_from_oracle(case.ocam)
+    gt = torch.as_tensor(case.gt).cuda()
+    res = []
+    for write in (True, False):
+        g = _device_scene(case)
+        adam = B.AdamState(g)
+        loss_dev = torch.zeros(1, device="cuda")
+        B.train_step_fused(g, cam, case.degree, case.bg, gt, 0.8, 0.0, 0.2, adam, loss_dev=loss_dev,
+                           write_grads=write)
+        torch.cuda.synchronize()
+        res.append((float(_np(loss_dev)[0]), _np(B.last_tensor("out_img")).copy(), [_np(t).copy() for t in g.groups()]))
+    (l_full, img_full, p_full), (l_light, img_light, p_light) = res
+    assert l_full == l_light
+    assert np.array_equal(img_full, img_light)
+    for a, b in zip(p_full, p_light):
+        # float atomics in the backward may reorder sums between two runs
+        assert np.allclose(a, b, rtol=1e-5, atol=1e-6)
+    for k in ("out_depth", "out_distortion", "final_Ts", "final_idx"):
+        with pytest.raises(B.MsplatError):
+            B.last_tensor(k)
