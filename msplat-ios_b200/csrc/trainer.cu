@@ -557,82 +557,104 @@ struct Trainer {
         return h;
     }
 
-    void export_ply(const std::string& path) {  // saveGaussianPly, :11-58
+    // Position in the dataset's original frame when keepCrs is set (the
+    // dataset normalised positions by translation and scale).
+    float out_pos(const std::vector<float>& means, int64_t i, int axis) const {
+        const float v = means[3 * i + axis];
+        return cfg.keepCrs ? v / ds->scale + ds->translation[axis] : v;
+    }
+
+    // 2DGS PLY (the reference's saveGaussianPly format,
+    // core/src/loaders/save_gaussians.cpp:11-58): binary little-endian
+    // vertices with the property list below; f_rest is stored channel-major
+    // ([3, bases]) and normals are zero. Built as a column table, written with
+    // one call.
+    void export_ply(const std::string& path) {
         CKT(cudaStreamSynchronize(stream));
+        std::vector<std::string> props = {"x", "y", "z", "nx", "ny", "nz", "f_dc_0", "f_dc_1", "f_dc_2"};
+        for (int k = 0; k < 3 * K; ++k) props.push_back("f_rest_" + std::to_string(k));
+        props.push_back("opacity");
+        props.push_back("scale_0");
+        props.push_back("scale_1");
+        for (int k = 0; k < 4; ++k) props.push_back("rot_" + std::to_string(k));
+        const size_t stride = props.size();
+        const std::vector<float> means = host_group(0), log_scales = host_group(1), quats = host_group(2),
+                                 dc = host_group(3), rest = host_group(4), opac = host_group(5);
+        std::vector<float> table((size_t)n * stride, 0.0f);
+        for (int64_t i = 0; i < n; ++i) {
+            float* v = &table[(size_t)i * stride];
+            for (int axis = 0; axis < 3; ++axis) v[axis] = out_pos(means, i, axis);  // normals (3..5) stay 0
+            for (int ch = 0; ch < 3; ++ch) {
+                v[6 + ch] = dc[3 * i + ch];
+                for (int b = 0; b < K; ++b) v[9 + ch * K + b] = rest[((size_t)i * K + b) * 3 + ch];
+            }
+            float* tail = v + 9 + 3 * K;
+            tail[0] = opac[i];
+            for (int k = 0; k < 2; ++k) {
+                const float ls = log_scales[2 * i + k];
+                tail[1 + k] = cfg.keepCrs ? std::log(std::exp(ls) / ds->scale) : ls;
+            }
+            for (int k = 0; k < 4; ++k) tail[3 + k] = quats[4 * i + k];
+        }
+        std::string header = "ply\nformat binary_little_endian 1.0\ncomment msplat v" + std::to_string(current_step) +
+                             "\nelement vertex " + std::to_string(n) + "\n";
+        for (const std::string& name : props) header += "property float " + name + "\n";
+        header += "end_header\n";
         std::ofstream o(path, std::ios::binary);
         if (!o.is_open()) throw ApiError("Cannot open PLY file for writing: " + path);
-        const int fr_bases = K, num_fr = 3 * K, num_scales = 2;
-        o << "ply\nformat binary_little_endian 1.0\n";
-        o << "comment msplat v" << current_step << "\n";
-        o << "element vertex " << n << "\n";
-        o << "property float x\nproperty float y\nproperty float z\n";
-        o << "property float nx\nproperty float ny\nproperty float nz\n";
-        for (int i = 0; i < 3; ++i) o << "property float f_dc_" << i << "\n";
-        for (int i = 0; i < num_fr; ++i) o << "property float f_rest_" << i << "\n";
-        o << "property float opacity\n";
-        for (int i = 0; i < num_scales; ++i) o << "property float scale_" << i << "\n";
-        o << "property float rot_0\nproperty float rot_1\nproperty float rot_2\nproperty float rot_3\n";
-        o << "end_header\n";
-        const std::vector<float> mp = host_group(0), sp = host_group(1), qp = host_group(2), dp = host_group(3),
-                                 frp = host_group(4), op = host_group(5);
-        const bool keep = cfg.keepCrs;
-        const float sc = ds->scale;
-        const int row_floats = 3 + 3 + 3 + num_fr + 1 + num_scales + 4;
-        std::vector<float> row(row_floats);
-        for (int64_t i = 0; i < n; ++i) {
-            int c = 0;
-            for (int j = 0; j < 3; ++j) row[c++] = keep ? (mp[i * 3 + j] / sc + ds->translation[j]) : mp[i * 3 + j];
-            row[c++] = 0.f;
-            row[c++] = 0.f;
-            row[c++] = 0.f;
-            for (int j = 0; j < 3; ++j) row[c++] = dp[i * 3 + j];
-            for (int ch = 0; ch < 3; ++ch)  // [bases, 3] -> [3, bases]
-                for (int b = 0; b < fr_bases; ++b) row[c++] = frp[i * fr_bases * 3 + b * 3 + ch];
-            row[c++] = op[i];
-            for (int j = 0; j < num_scales; ++j)
-                row[c++] = keep ? std::log(std::exp(sp[i * num_scales + j]) / sc) : sp[i * num_scales + j];
-            for (int j = 0; j < 4; ++j) row[c++] = qp[i * 4 + j];
-            o.write(reinterpret_cast<const char*>(row.data()), row_floats * sizeof(float));
-        }
+        o.write(header.data(), (std::streamsize)header.size());
+        o.write(reinterpret_cast<const char*>(table.data()), (std::streamsize)(table.size() * sizeof(float)));
         if (!o) throw ApiError("error writing PLY: " + path);
     }
 
-    void export_splat(const std::string& path) {  // saveGaussianSplat, :60-111
+    // .splat (the 32-byte-per-splat web viewer format the reference writes,
+    // core/src/loaders/save_gaussians.cpp:60-111): float position, float
+    // scale (a flat disc: third axis 1e-5), RGBA8 colour (SH DC through
+    // 0.5 + C0 dc, alpha = sigmoid(opacity)), quaternion quantised to q * 128 +
+    // 128; splats ordered by (sum of scales) x opacity, largest first, as the
+    // reference orders them.
+    struct SplatRecord {
+        float pos[3];
+        float scale[3];
+        uint8_t rgba[4];
+        uint8_t rot[4];
+    };
+    static_assert(sizeof(SplatRecord) == 32, "splat records are 32 bytes");
+
+    static uint8_t quantise_u8(double x) { return (uint8_t)std::min(255.0, std::max(0.0, x)); }
+
+    void export_splat(const std::string& path) {
         CKT(cudaStreamSynchronize(stream));
+        const std::vector<float> means = host_group(0), log_scales = host_group(1), quats = host_group(2),
+                                 dc = host_group(3), opac = host_group(5);
+        std::vector<SplatRecord> recs((size_t)n);
+        std::vector<float> importance((size_t)n);
+        for (int64_t i = 0; i < n; ++i) {
+            SplatRecord& r = recs[(size_t)i];
+            const float opacity = 1.0f / (1.0f + std::exp(-opac[i]));
+            float size = 0.0f;
+            for (int axis = 0; axis < 3; ++axis) r.pos[axis] = out_pos(means, i, axis);
+            for (int k = 0; k < 2; ++k) {
+                float e = std::exp(log_scales[2 * i + k]);
+                size += e;
+                r.scale[k] = cfg.keepCrs ? e / ds->scale : e;
+            }
+            r.scale[2] = 1e-5f;
+            importance[(size_t)i] = (cfg.keepCrs ? size / ds->scale : size) / (1.0f + std::exp(-opac[i]));
+            for (int ch = 0; ch < 3; ++ch) r.rgba[ch] = quantise_u8(((double)dc[3 * i + ch] * kC0 + 0.5) * 255.0);
+            r.rgba[3] = quantise_u8((double)(opacity * 255.0f));
+            for (int k = 0; k < 4; ++k) r.rot[k] = quantise_u8((double)(quats[4 * i + k] * 128.0f + 128.0f));
+        }
+        std::vector<int64_t> order((size_t)n);
+        std::iota(order.begin(), order.end(), (int64_t)0);
+        std::sort(order.begin(), order.end(),
+                  [&](int64_t x, int64_t y) { return importance[(size_t)x] > importance[(size_t)y]; });
+        std::vector<SplatRecord> sorted;
+        sorted.reserve((size_t)n);
+        for (int64_t i : order) sorted.push_back(recs[(size_t)i]);
         std::ofstream o(path, std::ios::binary);
         if (!o.is_open()) throw ApiError("Cannot open .splat file for writing: " + path);
-        const std::vector<float> mp = host_group(0), sp = host_group(1), qp = host_group(2), dp = host_group(3),
-                                 op = host_group(5);
-        const bool keep = cfg.keepCrs;
-        const float scl = ds->scale;
-        std::vector<float> order(n);
-        for (int64_t i = 0; i < n; ++i) {
-            float s = 0.0f;
-            for (int j = 0; j < 2; ++j) s += std::exp(sp[i * 2 + j]);
-            if (keep) s /= scl;
-            order[i] = s / (1.0f + std::exp(-op[i]));
-        }
-        std::vector<size_t> idx(n);
-        std::iota(idx.begin(), idx.end(), 0);
-        std::sort(idx.begin(), idx.end(), [&](size_t a, size_t b) { return order[a] > order[b]; });
-        for (size_t i : idx) {
-            float mm[3];
-            for (int j = 0; j < 3; ++j) mm[j] = keep ? (mp[i * 3 + j] / scl + ds->translation[j]) : mp[i * 3 + j];
-            o.write(reinterpret_cast<const char*>(mm), 12);
-            float sc[3] = {0.f, 0.f, 0.f};
-            for (int j = 0; j < 2; ++j) sc[j] = keep ? (std::exp(sp[i * 2 + j]) / scl) : std::exp(sp[i * 2 + j]);
-            sc[2] = 1e-5f;  // 2DGS surfels are flat discs
-            o.write(reinterpret_cast<const char*>(sc), 12);
-            uint8_t rgba[4];
-            for (int j = 0; j < 3; ++j)
-                rgba[j] = (uint8_t)std::clamp(((double)dp[i * 3 + j] * kC0 + 0.5) * 255.0, 0.0, 255.0);
-            const float sig = 1.0f / (1.0f + std::exp(-op[i]));
-            rgba[3] = (uint8_t)std::clamp(sig * 255.0f, 0.0f, 255.0f);
-            o.write(reinterpret_cast<const char*>(rgba), 4);
-            uint8_t q[4];
-            for (int j = 0; j < 4; ++j) q[j] = (uint8_t)std::clamp(qp[i * 4 + j] * 128.0f + 128.0f, 0.0f, 255.0f);
-            o.write(reinterpret_cast<const char*>(q), 4);
-        }
+        o.write(reinterpret_cast<const char*>(sorted.data()), (std::streamsize)(sorted.size() * sizeof(SplatRecord)));
         if (!o) throw ApiError("error writing .splat: " + path);
     }
 
