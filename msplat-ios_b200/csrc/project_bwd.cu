@@ -81,6 +81,56 @@ __device__ __forceinline__ void adam_stream(int n, const float* sparam, GradAt g
     }
 }
 
+// adam_stream for a group whose old parameters are read from global memory
+// (coalesced float4 with the moments) instead of shared memory.
+template <typename GradAt>
+__device__ __forceinline__ void adam_stream_global(int n, GradAt grad, float* __restrict__ p, float* __restrict__ m,
+                                                   float* __restrict__ v, float* __restrict__ gout, float st,
+                                                   float b1, float b2, float bc, float eps, bool do_adam) {
+    const uintptr_t al = reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(m) |
+                         reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(gout);
+    int done = 0;
+    if (do_adam && (al & 15) == 0) {
+        constexpr int U = 4;
+        const int n4 = n >> 2;
+        const int step = blockDim.x * U;
+        for (int base = threadIdx.x; base < n4; base += step) {
+            float4 pp[U], mm[U], vv[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = base + u * blockDim.x;
+                if (c < n4) {
+                    pp[u] = reinterpret_cast<const float4*>(p)[c];
+                    mm[u] = reinterpret_cast<const float4*>(m)[c];
+                    vv[u] = reinterpret_cast<const float4*>(v)[c];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = base + u * blockDim.x;
+                if (c >= n4) break;
+                const int e = c << 2;
+                const float g0 = grad(e), g1 = grad(e + 1), g2 = grad(e + 2), g3 = grad(e + 3);
+                float4 q;
+                q.x = adam_update(pp[u].x, g0, &mm[u].x, &vv[u].x, st, b1, b2, bc, eps);
+                q.y = adam_update(pp[u].y, g1, &mm[u].y, &vv[u].y, st, b1, b2, bc, eps);
+                q.z = adam_update(pp[u].z, g2, &mm[u].z, &vv[u].z, st, b1, b2, bc, eps);
+                q.w = adam_update(pp[u].w, g3, &mm[u].w, &vv[u].w, st, b1, b2, bc, eps);
+                reinterpret_cast<float4*>(p)[c] = q;
+                reinterpret_cast<float4*>(m)[c] = mm[u];
+                reinterpret_cast<float4*>(v)[c] = vv[u];
+                if (gout) reinterpret_cast<float4*>(gout)[c] = make_float4(g0, g1, g2, g3);
+            }
+        }
+        done = n4 << 2;
+    }
+    for (int q = done + threadIdx.x; q < n; q += blockDim.x) {
+        const float g = grad(q);
+        if (gout) gout[q] = g;
+        if (do_adam) p[q] = adam_update(p[q], g, m + q, v + q, st, b1, b2, bc, eps);
+    }
+}
+
 // One CTA owns kBwdThreads consecutive Gaussians [b0, b0 + cnt).
 //  phase 0: stage their parameters and SH-rest coefficients in shared memory
 //           (contiguous, float4 loads);
@@ -89,7 +139,7 @@ __device__ __forceinline__ void adam_stream(int n, const float* sparam, GradAt g
 //  phase 2: Adam on every group as contiguous streams (fused_adam_kernel),
 //           so moments and parameters are read and written fully coalesced.
 template <int K>
-__global__ void __launch_bounds__(kBwdThreads) k_project_backward(ProjBwdArgs a) {
+__global__ void __launch_bounds__(kBwdThreads, 6) k_project_backward(ProjBwdArgs a) {
     extern __shared__ float smem[];
     constexpr int K3 = 3 * K;
     const int b0 = a.g_begin + blockIdx.x * kBwdThreads;
@@ -108,13 +158,11 @@ __global__ void __launch_bounds__(kBwdThreads) k_project_backward(ProjBwdArgs a)
     float* gOp = gDc + 3 * T;       // [T]
     float* sB = gOp + T;            // [T][15] SH basis of the used bands
     float* sDC = sB + 15 * T;       // [T][3] dL/d colour
-    float* sR = sDC + 3 * T;        // [T * K3] SH-rest coefficients
     copy_in(sMean, a.means + 3 * (size_t)b0, 3 * cnt);
     copy_in(sScale, a.scales + 2 * (size_t)b0, 2 * cnt);
     copy_in(sQuat, a.quats + 4 * (size_t)b0, 4 * cnt);
     copy_in(sDc, a.f_dc + 3 * (size_t)b0, 3 * cnt);
     copy_in(sOp, a.opacities + (size_t)b0, cnt);
-    if constexpr (K3 > 0) copy_in(sR, a.f_rest + (size_t)b0 * K3, cnt * K3);
     __syncthreads();
 
     const int t = threadIdx.x;
@@ -133,8 +181,10 @@ __global__ void __launch_bounds__(kBwdThreads) k_project_backward(ProjBwdArgs a)
         float basis[15];
         int nb = 0;
         const int rad = a.radii[i];
-        const float* myR = sR + t * K3;
-        auto rest_at = [&](int k) { return myR[k]; };
+        // the SH-rest coefficients are read from global memory here and again,
+        // coalesced, by the Adam stream below (an L2 hit)
+        const float* myR = a.f_rest + (size_t)i * K3;
+        auto rest_at = [&](int k) { return __ldg(myR + k); };
         if (rad > 0) {
             V3 p = v3(sMean[3 * t], sMean[3 * t + 1], sMean[3 * t + 2]);
             float ex = det_exp(sScale[2 * t]), ey = det_exp(sScale[2 * t + 1]);
@@ -233,16 +283,16 @@ __global__ void __launch_bounds__(kBwdThreads) k_project_backward(ProjBwdArgs a)
                 ad ? Vv[5] + i0 : nullptr, a.dL_dopacity ? a.dL_dopacity + i0 : nullptr, a.step_size[5], b1, b2, bc,
                 eps, ad);
     if constexpr (K3 > 0)
-        adam_stream(cnt * K3, sR,
-                    [&](int q) {
-                        const int gl = q / K3;
-                        const int r = q - gl * K3;
-                        const int k = r / 3;
-                        return sB[gl * 15 + k] * sDC[gl * 3 + (r - k * 3)];
-                    },
-                    a.f_rest + i0 * K3, ad ? M[4] + i0 * K3 : nullptr, ad ? Vv[4] + i0 * K3 : nullptr,
-                    a.dL_dfeatures_rest ? a.dL_dfeatures_rest + i0 * K3 : nullptr, a.step_size[4], b1, b2, bc, eps,
-                    ad);
+        adam_stream_global(cnt * K3,
+                           [&](int q) {
+                               const int gl = q / K3;
+                               const int r = q - gl * K3;
+                               const int k = r / 3;
+                               return sB[gl * 15 + k] * sDC[gl * 3 + (r - k * 3)];
+                           },
+                           a.f_rest + i0 * K3, ad ? M[4] + i0 * K3 : nullptr, ad ? Vv[4] + i0 * K3 : nullptr,
+                           a.dL_dfeatures_rest ? a.dL_dfeatures_rest + i0 * K3 : nullptr, a.step_size[4], b1, b2, bc,
+                           eps, ad);
 }
 
 }  // namespace
@@ -257,7 +307,7 @@ void launch_k(const ProjBwdArgs& a, int grid, size_t smem, cudaStream_t s) {
 void launch_project_backward(const ProjBwdArgs& a, cudaStream_t s) {
     int cnt = a.g_end - a.g_begin;
     if (cnt <= 0) return;
-    const size_t smem = sizeof(float) * (size_t)kBwdThreads * (26 + 15 + 3 + 3 * a.rest_bases);
+    const size_t smem = sizeof(float) * (size_t)kBwdThreads * (26 + 15 + 3);
     if (a.rest_bases == 0 || a.rest_bases == 3 || a.rest_bases == 8 || a.rest_bases == 15) note_launches(1);
     const int grid = (cnt + kBwdThreads - 1) / kBwdThreads;
     switch (a.rest_bases) {
