@@ -332,8 +332,9 @@ int msplat_loss_ssim_noalloc(const float* out_img, const float* gt, const float*
  * l1 term, distortion term), raster_counters (i64 [4]: blended
  * (pixel, surfel) pairs of the forward rasteriser, its (warp, surfel) visits
  * past the cull, the backward's (warp, surfel) visits and its blended pairs;
- * each visit evaluates 32 pixels) and intersection_totals (i64 [4]: emitted
- * keys, kept intersections, band begin and end). Returns MSPLAT_ERR_ARGUMENT for an unknown
+ * each visit evaluates 32 pixels) and intersection_totals (i64 [5]: emitted
+ * keys, kept intersections, band begin and end, tiles with more than 512
+ * keys). Returns MSPLAT_ERR_ARGUMENT for an unknown
  * name or a tensor the last call did not produce. */
 int msplat_last_tensor(const char* name, MsplatTensorRef* out);
 

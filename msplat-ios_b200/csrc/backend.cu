@@ -81,8 +81,8 @@ struct Workspace {
     // per pixel
     Buf final_Ts, final_idx, out_img, out_depth, out_normal, out_alpha, out_median, out_dist, dL_dout_img;
     // scalars
-    Buf loss_partials, loss_out, loss_f, err, totals, row_work, counters;
-    int64_t* h_totals = nullptr;  // pinned [4]: raw, kept, band begin, band end
+    Buf loss_partials, loss_out, loss_f, err, totals, row_work, counters, big_tiles;
+    int64_t* h_totals = nullptr;  // pinned [5]: raw, kept, band begin, band end, large tiles
     uint32_t* h_err = nullptr;    // pinned [1]
     // shape bookkeeping of the last call
     int n = 0, K = 0, W = 0, H = 0, tx = 0, ty = 0;
@@ -106,7 +106,7 @@ struct Workspace {
                       &dL_dfeatures_dc, &dL_dfeatures_rest, &dL_dopacity, &dL_dtransMat, &dL_dnormal3D,
                       &dL_dcolors, &tile_diff, &chunk_counts, &raw_true, &id_limit, &block_max, &raw_counts, &raw_start, &tile_bins, &fill, &raw_keys,
                       &gaussian_ids, &blend_mask, &final_Ts, &final_idx, &out_img, &out_depth, &out_normal, &out_alpha,
-                      &out_median, &out_dist, &dL_dout_img, &loss_partials, &loss_out, &loss_f, &err, &totals, &row_work, &counters};
+                      &out_median, &out_dist, &dL_dout_img, &loss_partials, &loss_out, &loss_f, &err, &totals, &row_work, &counters, &big_tiles};
         for (Buf* b : all) b->release();
         for (auto& set : ev_pending)
             for (auto& m : set) cudaEventDestroy(m.second);
@@ -149,7 +149,7 @@ Workspace& workspace() {
     }
     Workspace& w = *g_ws[dev];
     if (!w.h_totals) {
-        CK(cudaHostAlloc(reinterpret_cast<void**>(&w.h_totals), 4 * sizeof(int64_t), cudaHostAllocDefault));
+        CK(cudaHostAlloc(reinterpret_cast<void**>(&w.h_totals), 5 * sizeof(int64_t), cudaHostAllocDefault));
         CK(cudaHostAlloc(reinterpret_cast<void**>(&w.h_err), sizeof(uint32_t), cudaHostAllocDefault));
     }
     return w;
@@ -268,7 +268,8 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     w.raw_start.ensure((size_t)T * 8);
     w.tile_bins.ensure((size_t)T * sizeof(int2));
     w.fill.ensure((size_t)T * 8);
-    w.totals.ensure(4 * sizeof(int64_t));
+    w.totals.ensure(5 * sizeof(int64_t));
+    w.big_tiles.ensure((size_t)T * sizeof(int32_t));
     w.err.ensure(sizeof(uint32_t));
     w.final_Ts.ensure(P * 3 * 4); w.final_idx.ensure(P * 2 * 4); w.out_img.ensure(P * 3 * 4);
     w.out_depth.ensure(P * 4); w.out_normal.ensure(P * 3 * 4); w.out_alpha.ensure(P * 4);
@@ -308,10 +309,10 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
                        w.id_limit.as<int32_t>(), w.block_max.as<int32_t>(), tx, ty, row0, row1, w.raw_counts.as<int32_t>(),
                        w.raw_start.as<int64_t>(), w.fill.as<uint64_t>(), w.tile_bins.as<int2>(), w.totals.as<int64_t>(),
                        balance_world > 0 ? w.row_work.as<int64_t>() : nullptr, w.err.as<uint32_t>(), s, balance_world,
-                       balance_rank);
+                       balance_rank, w.big_tiles.as<int32_t>());
     // The one host read of the step: buffer sizes for the intersections (and
     // the band the kernel chose, when balancing).
-    CK(cudaMemcpyAsync(w.h_totals, w.totals.p, 4 * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(w.h_totals, w.totals.p, 5 * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
     if (balance_world > 0) {
         const int o0 = (int)w.h_totals[2], o1 = (int)w.h_totals[3];
@@ -321,8 +322,9 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
         row0 = o1 > o0 ? std::max(0, o0 - 1) : 0;
         row1 = o1 > o0 ? std::min(ty, o1 + 1) : 0;
     }
-    const int64_t raw_total = w.h_totals[0], kept = w.h_totals[1];
-    if (raw_total < 0 || kept < 0 || kept > raw_total) throw Error(MSPLAT_ERR_CAPACITY, "corrupt tile totals");
+    const int64_t raw_total = w.h_totals[0], kept = w.h_totals[1], num_big = w.h_totals[4];
+    if (raw_total < 0 || kept < 0 || kept > raw_total || num_big < 0 || num_big > T)
+        throw Error(MSPLAT_ERR_CAPACITY, "corrupt tile totals");
     w.kept = kept;
     w.raw_keys.ensure((size_t)(raw_total > 0 ? raw_total : 1) * sizeof(uint64_t));
     w.gaussian_ids.ensure((size_t)(kept > 0 ? kept : 1) * sizeof(int32_t));
@@ -332,7 +334,8 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
                      w.block_max.as<int32_t>(), w.fill.as<uint64_t>(), w.raw_keys.as<uint64_t>(), s);
     mark(w, kStSort, s);
     launch_tile_sort(row0 * tx, (row1 - row0) * tx, w.raw_counts.as<int32_t>(), w.raw_start.as<int64_t>(), w.raw_keys.as<uint64_t>(),
-                     w.tile_bins.as<int2>(), w.gaussian_ids.as<int32_t>(), w.err.as<uint32_t>(), n, s);
+                     w.tile_bins.as<int2>(), w.gaussian_ids.as<int32_t>(), w.err.as<uint32_t>(), n,
+                     w.big_tiles.as<int32_t>(), (int)num_big, s);
     if (split_color) {
         // colour after binning: the caller may still be gathering features_dc /
         // features_rest until features_ready
@@ -835,7 +838,7 @@ int msplat_last_tensor(const char* name, MsplatTensorRef* out) {
         else if (nm == "raw_tile_counts") set(w.raw_true, 1, {T}, px);
         else if (nm == "gaussian_ids") set(w.gaussian_ids, 1, {w.kept}, px);
         else if (nm == "raster_counters") set(w.counters, 2, {4}, px);
-        else if (nm == "intersection_totals") set(w.totals, 2, {4}, px);
+        else if (nm == "intersection_totals") set(w.totals, 2, {5}, px);
         else if (nm == "xys") set(w.xys, 0, {n, 2}, rp);
         else if (nm == "transMats") set(w.transmats, 0, {n, 9}, rp);
         else if (nm == "normal_opacity") set(w.normal_opacity, 0, {n, 4}, rp);

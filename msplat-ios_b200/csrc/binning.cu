@@ -130,6 +130,8 @@ k_tile_select(const int32_t* __restrict__ chunk_counts, int num_tiles, int tx, i
     atomicMax(bmax, limit);
 }
 
+constexpr int kWarpSortMax = 512;  // tiles up to this many keys are sorted by one warp
+
 // From the per-tile emitted counts (k_tile_select): the row work, clamped
 // kept counts and both exclusive scans, for tile rows [row0, row1) (other
 // rows get zero counts). With world > 0 the rows are chosen here: band `rank`
@@ -138,8 +140,10 @@ k_tile_select(const int32_t* __restrict__ chunk_counts, int num_tiles, int tx, i
 __global__ void __launch_bounds__(kCountThreads)
 k_tile_counts(int tx, int ty, int row0, int row1, int32_t* __restrict__ raw_counts,
               int64_t* __restrict__ raw_start, unsigned long long* __restrict__ fill, int2* __restrict__ tile_bins,
-              int64_t* __restrict__ totals, int64_t* __restrict__ row_work, int world, int rank) {
+              int64_t* __restrict__ totals, int64_t* __restrict__ row_work, int world, int rank,
+              int32_t* __restrict__ big_tiles) {
     __shared__ int s_rows[2];
+    __shared__ int s_big;
     // The work of each row (one warp per tile row).
     if (row_work) {
         const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
@@ -167,6 +171,7 @@ k_tile_counts(int tx, int ty, int row0, int row1, int32_t* __restrict__ raw_coun
         }
         s_rows[0] = r0;
         s_rows[1] = r1;
+        s_big = 0;
     }
     __syncthreads();
     // Rows outside [row0, row1) get zero counts so that nothing is emitted there.
@@ -233,6 +238,16 @@ k_tile_counts(int tx, int ty, int row0, int row1, int32_t* __restrict__ raw_coun
             fill[t] = (unsigned long long)(run_raw + ir - r);
             tile_bins[t] = make_int2(run_kept + ik - k, run_kept + ik);
         }
+        // tiles the CTA sort handles (more than kWarpSortMax keys), listed in
+        // any order so that its grid covers just them
+        const bool big = t < e && r > kWarpSortMax;
+        const unsigned bb = __ballot_sync(0xffffffffu, big);
+        if (bb) {
+            int at = 0;
+            if (lane == 0) at = atomicAdd(&s_big, __popc(bb));
+            at = __shfl_sync(0xffffffffu, at, 0);
+            if (big) big_tiles[at + __popc(bb & ((1u << lane) - 1u))] = t;
+        }
         run_raw += __shfl_sync(0xffffffffu, ir, 31);
         run_kept += __shfl_sync(0xffffffffu, ik, 31);
     }
@@ -246,6 +261,8 @@ k_tile_counts(int tx, int ty, int row0, int row1, int32_t* __restrict__ raw_coun
         totals[0] = tr;
         totals[1] = tk;
     }
+    __syncthreads();
+    if (threadIdx.x == 0) totals[4] = s_big;
 }
 
 // One warp per 32 consecutive Gaussians: their clipped tile rectangles are
@@ -336,7 +353,6 @@ k_emit_keys(int n, const uint2* __restrict__ rects, const float* __restrict__ de
 }
 
 constexpr int kSortThreads = 256;
-constexpr int kWarpSortMax = 512;  // tiles up to this many keys are sorted by one warp
 
 // Compare-exchange for an ascending (up) or descending block.
 __device__ __forceinline__ void cmp_swap(uint64_t& a, uint64_t& b, bool up) {
@@ -498,12 +514,12 @@ __device__ __forceinline__ void find_digit(const int* hist, int need, int* s_dig
 __global__ void __launch_bounds__(kSortThreads)
 k_tile_sort(const int32_t* __restrict__ raw_counts, const int64_t* __restrict__ raw_start,
             const uint64_t* __restrict__ keys, const int2* __restrict__ tile_bins,
-            int32_t* __restrict__ gaussian_ids, int tile0, uint32_t* err, int num_ids) {
+            int32_t* __restrict__ gaussian_ids, const int32_t* __restrict__ big_tiles, uint32_t* err, int num_ids) {
     __shared__ uint64_t data[kMaxTileElems];
     __shared__ int hist[kSelectBins];
     __shared__ uint32_t s_prefix;
     __shared__ int s_digit, s_need, s_count;
-    const int t = tile0 + blockIdx.x;
+    const int t = big_tiles[blockIdx.x];
     const int count = raw_counts[t];
     if (count <= kWarpSortMax) return;
     const uint64_t* src = keys + raw_start[t];
@@ -572,7 +588,7 @@ k_tile_sort(const int32_t* __restrict__ raw_counts, const int64_t* __restrict__ 
 void launch_tile_counts(const int32_t* tile_diff, int id_chunk, int32_t* chunk_counts, int32_t* raw_true,
                         int32_t* id_limit, int32_t* block_max, int tiles_x, int tiles_y, int row0, int row1,
                         int32_t* raw_counts, int64_t* raw_start, uint64_t* fill, int2* tile_bins, int64_t* totals,
-                        int64_t* row_work, uint32_t* err, cudaStream_t s, int world, int rank) {
+                        int64_t* row_work, uint32_t* err, cudaStream_t s, int world, int rank, int32_t* big_tiles) {
     const int T = tiles_x * tiles_y;
     note_launches(3);
     k_chunk_counts<<<kIdChunks, kCountThreads, 0, s>>>(tile_diff, tiles_x, tiles_y, chunk_counts);
@@ -580,7 +596,7 @@ void launch_tile_counts(const int32_t* tile_diff, int id_chunk, int32_t* chunk_c
                                                   raw_counts, id_limit, block_max, err);
     k_tile_counts<<<1, kCountThreads, 0, s>>>(tiles_x, tiles_y, row0, row1, raw_counts, raw_start,
                                               reinterpret_cast<unsigned long long*>(fill), tile_bins, totals,
-                                              row_work, world, rank);
+                                              row_work, world, rank, big_tiles);
 }
 
 void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x, int row0, int row1,
@@ -594,15 +610,16 @@ void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_
 
 void launch_tile_sort(int tile0, int num_tiles, const int32_t* raw_counts, const int64_t* raw_start,
                       const uint64_t* raw_keys, const int2* tile_bins, int32_t* gaussian_ids, uint32_t* err,
-                      int num_gaussians, cudaStream_t s) {
+                      int num_gaussians, const int32_t* big_tiles, int num_big, cudaStream_t s) {
     if (num_tiles <= 0) return;
-    note_launches(2);
+    note_launches(num_big > 0 ? 2 : 1);
     const int warps = kSortThreads / 32;
     k_tile_sort_warp<<<(num_tiles + warps - 1) / warps, kSortThreads, 0, s>>>(raw_counts, raw_start, raw_keys,
                                                                               tile_bins, gaussian_ids, tile0,
                                                                               num_tiles);
-    k_tile_sort<<<num_tiles, kSortThreads, 0, s>>>(raw_counts, raw_start, raw_keys, tile_bins, gaussian_ids, tile0,
-                                                    err, num_gaussians);
+    if (num_big > 0)
+        k_tile_sort<<<num_big, kSortThreads, 0, s>>>(raw_counts, raw_start, raw_keys, tile_bins, gaussian_ids,
+                                                      big_tiles, err, num_gaussians);
 }
 
 }  // namespace msplat

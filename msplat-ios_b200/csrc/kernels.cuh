@@ -107,7 +107,9 @@ void launch_project_backward(const ProjBwdArgs& a, cudaStream_t s);
 // (raw_counts: all intersections of a tile within the cap, the chunks up to
 // the one holding its 2048th lowest id otherwise) with the id bound of each
 // tile (id_limit), kept counts, exclusive scans and the two totals.
-// totals[0] = emitted intersections (int64), totals[1] = kept.
+// totals[0] = emitted intersections (int64), totals[1] = kept, totals[2..3]
+// = the band (when balancing), totals[4] = tiles with more than 512 keys,
+// listed in big_tiles (capacity: the tile count) for the CTA sort.
 // fill[t] receives raw_start[t]: the key counter of k_emit_keys. Only
 // tile rows [row0, row1) are binned; the other rows get empty ranges.
 // row_work (optional, [tiles_y]) receives a per-row work estimate over all
@@ -116,7 +118,7 @@ void launch_tile_counts(const int32_t* tile_diff, int id_chunk, int32_t* chunk_c
                         int32_t* id_limit, int32_t* block_max, int tiles_x, int tiles_y, int row0, int row1,
                         int32_t* raw_counts, int64_t* raw_start, uint64_t* fill, int2* tile_bins, int64_t* totals,
                         int64_t* row_work, uint32_t* err, cudaStream_t s,
-                        int world = 0, int rank = 0);
+                        int world, int rank, int32_t* big_tiles);
 void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_x, int row0, int row1,
                       const int32_t* id_limit, const int32_t* block_max, uint64_t* fill, uint64_t* raw_keys,
                       cudaStream_t s);
@@ -124,7 +126,7 @@ void launch_emit_keys(int n, const uint2* rects, const float* depths, int tiles_
 // pass above 2^24 Gaussians).
 void launch_tile_sort(int tile0, int num_tiles, const int32_t* raw_counts, const int64_t* raw_start,
                       const uint64_t* raw_keys, const int2* tile_bins, int32_t* gaussian_ids,
-                      uint32_t* err, int num_gaussians, cudaStream_t s);
+                      uint32_t* err, int num_gaussians, const int32_t* big_tiles, int num_big, cudaStream_t s);
 
 // ---- rasterisation (rasterize.cu) -------------------------------------------
 struct RasterFwdArgs {
