@@ -64,11 +64,15 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--exchange", default="rgb", choices=["peers", "nccl", "rgb"],
+    ap.add_argument("--exchange", default="rgb", choices=["peers", "nccl", "rgb", "route", "route-peer"],
                     help="multi-GPU parameter exchange: geometry all-gathered and the owners' colours for the "
                          "next camera all-gathered instead of the colour coefficients (rgb, default); NCCL "
-                         "all-gathers of all groups with the colour groups overlapped with binning (nccl); or "
-                         "geometry all-gathered and colour read from its owner over NVLink (CUDA IPC, peers)")
+                         "all-gathers of all groups with the colour groups overlapped with binning (nccl); "
+                         "geometry all-gathered and colour read from its owner over NVLink (CUDA IPC, peers); "
+                         "or each owner projects its slice and sends the projected Gaussians to the bands they "
+                         "touch, gradients come back to the owner, nothing is gathered (route: NCCL "
+                         "all-to-alls; route-peer: the pack and return kernels store straight into the other "
+                         "GPUs' inboxes over NVLink)")
     ap.add_argument("--render-frames", type=int, default=20,
                     help="render-only frames timed after the training steps (single GPU); 0 = skip")
     ap.add_argument("--cameras", type=int, default=0,
@@ -261,12 +265,33 @@ class Stepper:
         self.rgb_full = None
         self.have_rgb = False
         self.use_peers = False
+        self.route = None
         if ws == 1:
             return
         from msplat import sharding
         self.sharding = sharding
         self.plan = sharding.ShardPlan(n, (cfg.height + 15) // 16, ws, rank)
         self.exchange = "NCCL all-gather (colour groups overlapped with binning)"
+        if exchange in ("route", "route-peer"):
+            # the owner's slice is all a rank reads; the parameter groups stay
+            # [padded, ...] only so that gathered_params can collect them
+            sharding.pad_gaussians(self.g, self.plan.padded)
+            self.route_peers = None
+            how = "NCCL all-to-all"
+            if exchange == "route-peer":
+                self.route_peers = sharding.RoutePeers(B, dist, self.plan, n, dev)
+                how = ("stored by the pack kernel straight into the destination GPU's inbox over NVLink "
+                       "(CUDA IPC); records pushed back the same way")
+                if not self.route_peers.ok:
+                    how = "NCCL all-to-all (peer mapping failed: " + self.route_peers.error[:120] + ")"
+            self.route = sharding.gpu_route_calls(B, self.g, cams[0], cfg.degree, _bg(), gts[0], 1.0 - SSIM_WEIGHT,
+                                                  0.0, SSIM_WEIGHT, self.adam, self.stats, self.plan,
+                                                  peers=self.route_peers)
+            self.parts = torch.zeros(3, dtype=torch.float64, device=dev)
+            self.exchange = ("routed: each owner projects its slice and sends the projected Gaussians (128 B) "
+                             "to the tile-row bands they touch (" + how + "); gradient records (64 B) return "
+                             "to the owner for the VJP and Adam; no parameter is gathered")
+            return
         if exchange == "peers":
             self.peers = sharding.PeerParams(B, dist, self.plan, self.g)
             if self.peers.ok:
@@ -327,6 +352,11 @@ class Stepper:
             return
         sh = self.sharding
         self.adam.step += 1
+        if self.route is not None:
+            self.route.cam, self.route.gt = cam, gt
+            sh.routed_step(self.dist, self.plan, self.route, self.parts, marks=self._marks())
+            self._collect()
+            return
         cam_next = self.cams[(k + 1) % C if cam_next_index is None else cam_next_index]
         fb, pa = sh.gpu_step_fns(B, self.g, cam, self.cfg.degree, _bg(), gt, 1.0 - SSIM_WEIGHT, 0.0, SSIM_WEIGHT,
                                  self.adam, self.stats, features_ready=self.pending[0],
@@ -384,6 +414,10 @@ class Stepper:
         torch.cuda.synchronize()
         if self.peers is not None:
             self.peers.close()
+        if getattr(self, "route_peers", None) is not None:
+            self.route = None
+            self.route_peers.close()
+            self.route_peers = None
 
 
 _BG = None
@@ -530,6 +564,10 @@ def rank_breakdown(st, per_stage, kept, ws, rank, dist):
             "project_adam_ms": round(ph.get("project_adam", 0.0), 4),
             "all_gather_ms": round(ph.get("all_gather", 0.0), 4),
             "all_reduce_ms": round(ph.get("all_reduce", 0.0), 4)}
+    if st.route is not None:
+        # routed exchange: project + plan, payload all-to-all, band forward/
+        # loss/backward, gradient return, VJP + Adam, loss all-reduce
+        mine["route_phases_ms"] = {k: round(v, 4) for k, v in ph.items()}
     ranks = [None] * ws
     dist.all_gather_object(ranks, mine)
     return ranks
@@ -763,7 +801,8 @@ def e2e_sharded(B, dist, st, gts, cams, e2e_steps, dev):
     dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
     return {"value": round(1.0 / float(e2e_s.item()), 3), "unit": "iters/s",
             "h2d_bytes_per_step": int(gts[0].numel() * 4), "d2h_bytes_per_step": 24, "steps": e2e_steps,
-            "path": ("msplat_shard_* C ABI + NCCL per rank: target image H2D from pinned memory on a copy "
+            "path": (("msplat_route_*" if st.route is not None else "msplat_shard_*") +
+                     " C ABI + NCCL per rank: target image H2D from pinned memory on a copy "
                      "stream overlapping the previous step, loss sums D2H")}
 
 

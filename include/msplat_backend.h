@@ -212,6 +212,84 @@ int msplat_shard_project_backward_adam(const MsplatGaussians* g, const MsplatCam
                                        const float* raster_grads, int32_t g_begin, int32_t g_end,
                                        const MsplatAdamState* adam, float* xys_grad_norm, float* vis_counts,
                                        float* max_2d_size, void* stream);
+
+/* Routed multi-GPU exchange (one process per GPU; no counterpart in the
+ * reference, which runs on one GPU). Rank r owns Gaussians [g_begin, g_end)
+ * (parameters and Adam state, updated only by it; the rest of its parameter
+ * buffers is never read) and one band of tile rows. A step, with the
+ * caller's collectives in brackets:
+ *   msplat_route_project   projection of the own slice; the slice's
+ *                          summary (int32 [msplat_route_summary_len]): its
+ *                          per-tile intersection counts, then the number of
+ *                          its Gaussians whose tile rectangle starts at row
+ *                          y, then those whose rectangle ends at row y
+ *                          (y in [0, tiles_y])
+ *   [all-gather the summaries, rank order]
+ *   msplat_route_plan      the bands of all ranks and how many Gaussians
+ *                          each rank sends to each rank (identical on every
+ *                          rank): a Gaussian goes to every rank whose band
+ *                          plus a one-tile-row halo its tile rectangle meets
+ *   msplat_route_pack      128 bytes per (Gaussian, destination), grouped by
+ *                          destination rank, increasing id within a group
+ *   [all-to-all of the payloads, sources in rank order]
+ *   msplat_route_band      binning, sort, forward rasteriser, loss and
+ *                          backward over the received Gaussians for the
+ *                          rank's band; raster-gradient records [recv, 16]
+ *                          and the band's loss partial sums (l1, ssim, dist)
+ *   [all-to-all of the records back; all-reduce of the loss sums]
+ *   msplat_route_return    adds the returned records per own Gaussian
+ *   msplat_route_project_backward_adam   projection VJP + Adam on the slice
+ * Results equal the single-GPU step (same tile lists: the received set is in
+ * increasing global id order). Per call state lives in the device workspace,
+ * so one routed step runs at a time per device. */
+int msplat_route_summary_len(const MsplatCamera* cam, int64_t* len_out);
+int msplat_route_project(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use, int32_t g_begin,
+                         int32_t g_end, int32_t* summary_out, void* stream);
+/* summaries: device int32 [world][summary length], every rank's summary;
+ * bands_out: host int32 [world + 1] (band of rank r: [bands[r], bands[r+1]));
+ * send_counts_out / recv_counts_out: host int64 [world], the items this rank
+ * sends to / receives from each rank. Waits for the stream; fails if this
+ * slice's destinations disagree with the counts derived from the summaries. */
+int msplat_route_plan(const int32_t* summaries, const MsplatCamera* cam, int32_t world, int32_t rank,
+                      int32_t* bands_out, int64_t* send_counts_out, int64_t* recv_counts_out, void* stream);
+/* send_payload: device buffer of sum(send_counts) x 128 bytes. */
+int msplat_route_pack(void* send_payload, void* stream);
+/* The routed exchange without collectives for the payloads: every rank's
+ * inbox (the payloads it receives, sources in rank order) and return box
+ * (the records of its own packed items, in packing order) are device
+ * buffers that every rank maps (msplat_device_alloc + msplat_ipc_*). */
+typedef struct MsplatRoutePeers {
+    int32_t world, rank;      /* as in the last msplat_route_plan */
+    int64_t inbox_items;      /* capacity of each inbox (128-byte items) */
+    int64_t returnbox_items;  /* capacity of each return box (64-byte items) */
+    void* inbox[MSPLAT_MAX_PEER_RANKS];     /* [rank]: that rank's inbox, mapped here */
+    void* returnbox[MSPLAT_MAX_PEER_RANKS]; /* [rank]: that rank's return box, mapped here */
+} MsplatRoutePeers;
+/* msplat_route_pack writing each destination's group straight into that
+ * rank's inbox (NVLink stores). Every rank must finish this call's kernel
+ * before any rank reads its inbox (e.g. a one-element all-reduce on the
+ * stream); then msplat_route_band reads inbox[rank], sum(recv_counts) items. */
+int msplat_route_pack_peers(const MsplatRoutePeers* peers, void* stream);
+/* The band's records ([sum(recv_counts), 16] from msplat_route_band) into
+ * their owners' return boxes; after every rank's push (a one-element
+ * all-reduce), msplat_route_return reads returnbox[rank], sum(send_counts)
+ * items. */
+int msplat_route_push_peers(const MsplatRoutePeers* peers, const float* raster_grads, void* stream);
+/* recv_payload: num_recv x 128 bytes; raster_grads_out: device float
+ * [num_recv, 16]; loss_parts_dev: device double [3]. */
+int msplat_route_band(const MsplatCamera* cam, int32_t sh_degree, const void* recv_payload, int64_t num_recv,
+                      int32_t band_begin, int32_t band_end, const float background[3], const float* gt,
+                      float lambda_l1, float lambda_dist, float lambda_dssim, float* raster_grads_out,
+                      double* loss_parts_dev, void* stream);
+/* recv_grads: the records of this rank's packed items, returned in packing
+ * order (sum(send_counts) x 16 floats); slice_grads: device float
+ * [g_end - g_begin, 16] (overwritten). */
+int msplat_route_return(const float* recv_grads, int64_t num_items, float* slice_grads, void* stream);
+/* The projection VJP and Adam on the slice of the last msplat_route_project,
+ * from slice_grads; densify statistics indexed by global id (may be NULL). */
+int msplat_route_project_backward_adam(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
+                                       const float* slice_grads, const MsplatAdamState* adam, float* xys_grad_norm,
+                                       float* vis_counts, float* max_2d_size, void* stream);
 /* Colour exchange by clamped colour instead of SH coefficients (no
  * reference counterpart; the colour evaluation is sh_coeffs_to_color,
  * core/metal/msplat_metal.metal:756-823, as in the projection). The colour a

@@ -82,6 +82,17 @@ struct Workspace {
     Buf final_Ts, final_idx, out_img, out_depth, out_normal, out_alpha, out_median, out_dist, dL_dout_img;
     // scalars
     Buf loss_partials, loss_out, loss_f, err, totals, row_work, counters, big_tiles;
+    // routed multi-GPU exchange (route.cu): the owner's projected slice, its
+    // destinations and packing order, the received global ids
+    Buf own_records, own_cull, own_rects, own_depths, own_radii, own_dest, route_diff, route_colsum, route_block,
+        route_totals, route_base, route_bands, route_matrix, route_row_work, route_src, route_ids;
+    // pinned: bands (int32 [17] in the first 9 slots), the slice's items per
+    // rank [16], the count matrix [16 x 16]
+    static constexpr int kHostRouteSlots = (kMaxPeerRanks + 2) / 2 + kMaxPeerRanks + kMaxPeerRanks * kMaxPeerRanks;
+    int64_t* h_route = nullptr;
+    int route_n = 0, route_g0 = 0, route_world = 0, route_rank = 0;
+    std::vector<int64_t> route_matrix_h;  // the last plan's count matrix [world x world]
+    int64_t route_items = 0;
     int64_t* h_totals = nullptr;  // pinned [5]: raw, kept, band begin, band end, large tiles
     uint32_t* h_err = nullptr;    // pinned [1]
     // shape bookkeeping of the last call
@@ -106,7 +117,9 @@ struct Workspace {
                       &dL_dfeatures_dc, &dL_dfeatures_rest, &dL_dopacity, &dL_dtransMat, &dL_dnormal3D,
                       &dL_dcolors, &tile_diff, &chunk_counts, &raw_true, &id_limit, &block_max, &raw_counts, &raw_start, &tile_bins, &fill, &raw_keys,
                       &gaussian_ids, &blend_mask, &final_Ts, &final_idx, &out_img, &out_depth, &out_normal, &out_alpha,
-                      &out_median, &out_dist, &dL_dout_img, &loss_partials, &loss_out, &loss_f, &err, &totals, &row_work, &counters, &big_tiles};
+                      &out_median, &out_dist, &dL_dout_img, &loss_partials, &loss_out, &loss_f, &err, &totals, &row_work, &counters, &big_tiles, &own_records, &own_cull, &own_rects, &own_depths,
+                      &own_radii, &own_dest, &route_diff, &route_colsum, &route_block, &route_totals, &route_base,
+                      &route_bands, &route_matrix, &route_row_work, &route_src, &route_ids};
         for (Buf* b : all) b->release();
         for (auto& set : ev_pending)
             for (auto& m : set) cudaEventDestroy(m.second);
@@ -114,6 +127,8 @@ struct Workspace {
         ev_pending.clear();
         ev_pool.clear();
         if (h_totals) cudaFreeHost(h_totals);
+        if (h_route) cudaFreeHost(h_route);
+        h_route = nullptr;
         if (h_err) cudaFreeHost(h_err);
         h_totals = nullptr;
         h_err = nullptr;
@@ -151,6 +166,8 @@ Workspace& workspace() {
     if (!w.h_totals) {
         CK(cudaHostAlloc(reinterpret_cast<void**>(&w.h_totals), 5 * sizeof(int64_t), cudaHostAllocDefault));
         CK(cudaHostAlloc(reinterpret_cast<void**>(&w.h_err), sizeof(uint32_t), cudaHostAllocDefault));
+        CK(cudaHostAlloc(reinterpret_cast<void**>(&w.h_route), Workspace::kHostRouteSlots * sizeof(int64_t),
+                         cudaHostAllocDefault));
     }
     return w;
 }
@@ -235,7 +252,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
                    cudaStream_t s, int balance_world = 0, int balance_rank = 0, int* owned0 = nullptr,
                    int* owned1 = nullptr, bool split_color = false, cudaEvent_t features_ready = nullptr,
                    const MsplatPeerParams* peers = nullptr, const float* rgb_in = nullptr,
-                   bool aux_out = true) {
+                   bool aux_out = true, bool prefilled = false) {
     const int n = g->num_points;
     const int K = sh_rest_bases(g->sh_degree);
     const int tx = cam.tiles_x, ty = cam.tiles_y, T = tx * ty;
@@ -275,7 +292,10 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     w.out_depth.ensure(P * 4); w.out_normal.ensure(P * 3 * 4); w.out_alpha.ensure(P * 4);
     w.out_median.ensure(P * 4); w.out_dist.ensure(P * 4);
 
-    CK(cudaMemsetAsync(w.tile_diff.p, 0, diff_bytes, s));
+    // prefilled: the records, cull records, rectangles, depths and the
+    // per-id-chunk difference arrays already hold n Gaussians (the routed
+    // exchange's received set), so the projection is skipped
+    if (!prefilled) CK(cudaMemsetAsync(w.tile_diff.p, 0, diff_bytes, s));
     CK(cudaMemsetAsync(w.block_max.p, 0, bmax_bytes, s));
     CK(cudaMemsetAsync(w.err.p, 0, sizeof(uint32_t), s));
 
@@ -302,7 +322,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
         pa.colors = w.colors.as<float>(); pa.aabb = w.aabb.as<float>();
     }
     mark(w, kStProject, s);
-    launch_project_forward(pa, s);
+    if (!prefilled) launch_project_forward(pa, s);
     mark(w, kStCounts, s);
     if (balance_world > 0) w.row_work.ensure((size_t)ty * sizeof(int64_t));
     launch_tile_counts(w.tile_diff.as<int32_t>(), id_chunk, w.chunk_counts.as<int32_t>(), w.raw_true.as<int32_t>(),
@@ -798,6 +818,305 @@ int msplat_shard_project_backward_adam(const MsplatGaussians* g, const MsplatCam
         Workspace& w = workspace();
         CameraDev cd = make_cam(cam);
         ProjBwdArgs pb = make_proj_bwd(w, g, cd, degrees_to_use, 1.0f, raster_grads, g_begin, g_end);
+        set_adam(pb, adam);
+        pb.xys_grad_norm = xys_grad_norm; pb.vis_counts = vis_counts; pb.max_2d_size = max_2d_size;
+        mark(w, kStProjectBwd, s);
+        launch_project_backward(pb, s);
+        mark(w, -1, s);
+        CK(cudaGetLastError());
+    });
+}
+
+// ---- routed multi-GPU exchange (route.cu) -----------------------------------
+
+int msplat_route_summary_len(const MsplatCamera* cam, int64_t* len_out) {
+    return guarded([&] {
+        if (!cam || !len_out) throw Error(MSPLAT_ERR_ARGUMENT, "null argument");
+        const CameraDev cd = make_cam(cam);
+        *len_out = route_summary_len(cd.tiles_x, cd.tiles_y);
+    });
+}
+
+int msplat_route_project(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use, int32_t g_begin,
+                         int32_t g_end, int32_t* summary_out, void* stream) {
+    return guarded([&] {
+        check_inputs(g, cam, degrees_to_use);
+        if (g_begin < 0 || g_end > g->num_points || g_begin > g_end) throw Error(MSPLAT_ERR_ARGUMENT, "bad slice");
+        if (!summary_out) throw Error(MSPLAT_ERR_ARGUMENT, "null summary_out");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        Workspace& w = workspace();
+        const CameraDev cd = make_cam(cam);
+        const int n = g_end - g_begin;
+        const size_t nn = (size_t)(n > 0 ? n : 1);
+        const int tx = cd.tiles_x, ty = cd.tiles_y;
+        w.own_records.ensure(nn * kRecordF4 * sizeof(float4));
+        w.own_cull.ensure(nn * kCullF4 * sizeof(float4));
+        w.own_rects.ensure(nn * sizeof(uint2));
+        w.own_depths.ensure(nn * sizeof(float));
+        w.own_radii.ensure(nn * sizeof(int32_t));
+        const size_t diff_bytes = (size_t)(tx + 1) * (ty + 1) * 4;
+        w.route_diff.ensure(diff_bytes);
+        w.route_colsum.ensure((size_t)tx * ty * 4);
+        CK(cudaMemsetAsync(w.route_diff.p, 0, diff_bytes, s));
+        const int K = sh_rest_bases(g->sh_degree);
+        ProjFwdArgs pa{};
+        pa.n = n;
+        pa.pass = 0;
+        pa.means = g->means + 3 * (size_t)g_begin;
+        pa.scales = g->scales + 2 * (size_t)g_begin;
+        pa.quats = g->quats + 4 * (size_t)g_begin;
+        pa.opacities = g->opacities + (size_t)g_begin;
+        pa.f_dc = g->features_dc + 3 * (size_t)g_begin;
+        pa.f_rest = K > 0 ? g->features_rest + 3 * (size_t)K * g_begin : g->features_rest;
+        pa.rest_bases = K; pa.degrees_to_use = degrees_to_use;
+        pa.glob_scale = 1.0f; pa.clip_thresh = 0.01f;
+        pa.cam = cd;
+        pa.records = w.own_records.as<float4>(); pa.cull = w.own_cull.as<float4>();
+        pa.rects = w.own_rects.as<uint2>(); pa.depths = w.own_depths.as<float>();
+        pa.radii = w.own_radii.as<int32_t>(); pa.tile_diff = w.route_diff.as<int32_t>();
+        pa.id_chunk = std::max(1, n);  // one difference array for the slice
+        mark(w, kStProject, s);
+        launch_project_forward(pa, s);
+        CK(cudaMemsetAsync(summary_out + (size_t)tx * ty, 0, 2 * (size_t)(ty + 1) * sizeof(int32_t), s));
+        launch_route_summary(w.route_diff.as<int32_t>(), tx, ty, n, w.own_rects.as<uint2>(), w.own_radii.as<int32_t>(),
+                             w.route_colsum.as<int32_t>(), summary_out, s);
+        w.route_n = n;
+        w.route_g0 = g_begin;
+        CK(cudaGetLastError());
+    });
+}
+
+int msplat_route_plan(const int32_t* summaries, const MsplatCamera* cam, int32_t world, int32_t rank,
+                      int32_t* bands_out, int64_t* send_counts_out, int64_t* recv_counts_out, void* stream) {
+    return guarded([&] {
+        if (!summaries || !cam || !bands_out || !send_counts_out || !recv_counts_out)
+            throw Error(MSPLAT_ERR_ARGUMENT, "null argument");
+        if (world < 1 || world > kMaxPeerRanks) throw Error(MSPLAT_ERR_ARGUMENT, "world must be in [1, 16]");
+        if (rank < 0 || rank >= world) throw Error(MSPLAT_ERR_ARGUMENT, "rank out of range");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        Workspace& w = workspace();
+        const CameraDev cd = make_cam(cam);
+        const int tx = cd.tiles_x, ty = cd.tiles_y, n = w.route_n;
+        const int nblocks = (n + 255) / 256;
+        w.own_dest.ensure((size_t)(n > 0 ? n : 1) * sizeof(int2));
+        w.route_block.ensure((size_t)(nblocks > 0 ? nblocks : 1) * world * sizeof(int32_t));
+        w.route_totals.ensure(kMaxPeerRanks * sizeof(int64_t));
+        w.route_base.ensure(kMaxPeerRanks * sizeof(int64_t));
+        w.route_bands.ensure((kMaxPeerRanks + 1) * sizeof(int32_t));
+        w.route_matrix.ensure(kMaxPeerRanks * kMaxPeerRanks * sizeof(int64_t));
+        w.route_row_work.ensure((size_t)(ty > 0 ? ty : 1) * sizeof(int64_t));
+        launch_route_plan(summaries, tx, ty, world, w.route_row_work.as<int64_t>(), w.route_bands.as<int32_t>(),
+                          w.route_matrix.as<int64_t>(), n, w.own_rects.as<uint2>(), w.own_radii.as<int32_t>(),
+                          w.own_dest.as<int2>(), w.route_block.as<int32_t>(), w.route_totals.as<int64_t>(),
+                          w.route_base.as<int64_t>(), s);
+        // host: bands (int32, world + 1), this slice's totals (int64, world),
+        // the count matrix (int64, world x world)
+        int32_t* hb = reinterpret_cast<int32_t*>(w.h_route);
+        int64_t* ht = w.h_route + (kMaxPeerRanks + 2) / 2;
+        int64_t* hm = ht + kMaxPeerRanks;
+        CK(cudaMemcpyAsync(hb, w.route_bands.p, (world + 1) * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+        CK(cudaMemcpyAsync(ht, w.route_totals.p, world * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+        CK(cudaMemcpyAsync(hm, w.route_matrix.p, (size_t)world * world * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+        CK(cudaStreamSynchronize(s));
+        for (int r = 0; r <= world; ++r) {
+            if (hb[r] < 0 || hb[r] > ty || (r > 0 && hb[r] < hb[r - 1])) throw Error(MSPLAT_ERR_CAPACITY, "corrupt bands");
+            bands_out[r] = hb[r];
+        }
+        int64_t items = 0;
+        for (int q = 0; q < world; ++q) {
+            const int64_t c = ht[q];
+            // the slice's own destinations must agree with the count matrix
+            // every rank computed from the gathered histograms
+            if (c < 0 || c > n || c != hm[(size_t)rank * world + q])
+                throw Error(MSPLAT_ERR_CAPACITY, "route counts disagree with the gathered summaries");
+            send_counts_out[q] = c;
+            items += c;
+        }
+        for (int r = 0; r < world; ++r) {
+            const int64_t c = hm[(size_t)r * world + rank];
+            if (c < 0) throw Error(MSPLAT_ERR_CAPACITY, "corrupt route counts");
+            recv_counts_out[r] = c;
+        }
+        w.route_world = world;
+        w.route_rank = rank;
+        w.route_matrix_h.assign(hm, hm + (size_t)world * world);
+        w.route_items = items;
+        w.route_src.ensure((size_t)(items > 0 ? items : 1) * sizeof(int32_t));
+    });
+}
+
+namespace {
+// Items from rank r to rank q in the last plan.
+int64_t route_count(const Workspace& w, int r, int q) { return w.route_matrix_h[(size_t)r * w.route_world + q]; }
+
+RouteDests own_dests(const Workspace& w) {
+    RouteDests d{};
+    int64_t run = 0;
+    for (int q = 0; q < w.route_world; ++q) {
+        d.send_base[q] = run;
+        run += route_count(w, w.route_rank, q);
+    }
+    return d;
+}
+
+void check_route_peers(const Workspace& w, const MsplatRoutePeers* peers) {
+    if (!peers) throw Error(MSPLAT_ERR_ARGUMENT, "null peers");
+    if (peers->world != w.route_world || peers->rank != w.route_rank)
+        throw Error(MSPLAT_ERR_ARGUMENT, "peers world/rank differ from the last msplat_route_plan");
+    for (int q = 0; q < w.route_world; ++q)
+        if (!peers->inbox[q] || !peers->returnbox[q]) throw Error(MSPLAT_ERR_ARGUMENT, "null peer buffer");
+}
+}  // namespace
+
+int msplat_route_pack(void* send_payload, void* stream) {
+    return guarded([&] {
+        Workspace& w = workspace();
+        if (w.route_items > 0 && !send_payload) throw Error(MSPLAT_ERR_ARGUMENT, "null send_payload");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        RouteDests d = own_dests(w);
+        for (int q = 0; q < w.route_world; ++q)
+            d.dst[q] = static_cast<float4*>(send_payload) + (size_t)d.send_base[q] * kRoutePayloadF4;
+        launch_route_pack(w.route_n, w.route_g0, w.own_records.as<float4>(), w.own_cull.as<float4>(),
+                          w.own_rects.as<uint2>(), w.own_depths.as<float>(), w.own_dest.as<int2>(),
+                          w.route_block.as<int32_t>(), w.route_world, d, false, w.route_src.as<int32_t>(), s);
+        CK(cudaGetLastError());
+    });
+}
+
+int msplat_route_pack_peers(const MsplatRoutePeers* peers, void* stream) {
+    return guarded([&] {
+        Workspace& w = workspace();
+        check_route_peers(w, peers);
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        RouteDests d = own_dests(w);
+        for (int q = 0; q < w.route_world; ++q) {
+            // q's inbox holds the sources in rank order
+            int64_t off = 0;
+            for (int r = 0; r < w.route_rank; ++r) off += route_count(w, r, q);
+            if (off + route_count(w, w.route_rank, q) > peers->inbox_items)
+                throw Error(MSPLAT_ERR_CAPACITY, "a peer inbox is too small for this step");
+            d.dst[q] = static_cast<float4*>(peers->inbox[q]) + (size_t)off * kRoutePayloadF4;
+        }
+        launch_route_pack(w.route_n, w.route_g0, w.own_records.as<float4>(), w.own_cull.as<float4>(),
+                          w.own_rects.as<uint2>(), w.own_depths.as<float>(), w.own_dest.as<int2>(),
+                          w.route_block.as<int32_t>(), w.route_world, d, true, w.route_src.as<int32_t>(), s);
+        CK(cudaGetLastError());
+    });
+}
+
+int msplat_route_push_peers(const MsplatRoutePeers* peers, const float* raster_grads, void* stream) {
+    return guarded([&] {
+        Workspace& w = workspace();
+        check_route_peers(w, peers);
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        RouteReturns ret{};
+        int64_t m = 0;
+        for (int r = 0; r < w.route_world; ++r) {
+            ret.recv_off[r] = m;
+            m += route_count(w, r, w.route_rank);
+            // r's return box holds its items in its packing order: groups by
+            // destination rank
+            int64_t off = 0, row = 0;
+            for (int q = 0; q < w.route_world; ++q) {
+                if (q < w.route_rank) off += route_count(w, r, q);
+                row += route_count(w, r, q);
+            }
+            if (row > peers->returnbox_items) throw Error(MSPLAT_ERR_CAPACITY, "a peer return box is too small");
+            ret.dst[r] = static_cast<float4*>(peers->returnbox[r]) + (size_t)off * (kGradStride / 4);
+        }
+        ret.recv_off[w.route_world] = m;
+        if (m > 0 && !raster_grads) throw Error(MSPLAT_ERR_ARGUMENT, "null raster_grads");
+        launch_route_push(m, reinterpret_cast<const float4*>(raster_grads), w.route_world, ret, s);
+        CK(cudaGetLastError());
+    });
+}
+
+int msplat_route_band(const MsplatCamera* cam, int32_t sh_degree, const void* recv_payload, int64_t num_recv,
+                      int32_t band_begin, int32_t band_end, const float background[3], const float* gt,
+                      float lambda_l1, float lambda_dist, float lambda_dssim, float* raster_grads_out,
+                      double* loss_parts_dev, void* stream) {
+    return guarded([&] {
+        if (!cam || !background || !gt || !loss_parts_dev) throw Error(MSPLAT_ERR_ARGUMENT, "null argument");
+        if (num_recv < 0 || num_recv > (1 << 25)) throw Error(MSPLAT_ERR_ARGUMENT, "num_recv must be in [0, 2^25]");
+        if (num_recv > 0 && (!recv_payload || !raster_grads_out)) throw Error(MSPLAT_ERR_ARGUMENT, "null buffer");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        Workspace& w = workspace();
+        const CameraDev cd = make_cam(cam);
+        if (band_begin < 0 || band_end > cd.tiles_y || band_begin > band_end)
+            throw Error(MSPLAT_ERR_ARGUMENT, "bad band");
+        const int m = (int)num_recv;
+        const size_t nn = (size_t)(m > 0 ? m : 1);
+        const int tx = cd.tiles_x, ty = cd.tiles_y;
+        // the arrays the binning and rasterisers read, filled from the payloads
+        w.records.ensure(nn * kRecordF4 * sizeof(float4));
+        w.cull.ensure(nn * kCullF4 * sizeof(float4));
+        w.rects.ensure(nn * sizeof(uint2));
+        w.depths.ensure(nn * sizeof(float));
+        w.radii.ensure(nn * sizeof(int32_t));
+        w.route_ids.ensure(nn * sizeof(int32_t));
+        const size_t diff_bytes = (size_t)kIdChunks * (tx + 1) * (ty + 1) * 4;
+        w.tile_diff.ensure(diff_bytes);
+        CK(cudaMemsetAsync(w.tile_diff.p, 0, diff_bytes, s));
+        const int id_chunk = std::max(1, (m + kIdChunks - 1) / kIdChunks);
+        launch_route_unpack(num_recv, static_cast<const float4*>(recv_payload), tx, ty, id_chunk,
+                            w.records.as<float4>(), w.cull.as<float4>(), w.rects.as<uint2>(), w.depths.as<float>(),
+                            w.route_ids.as<int32_t>(), w.radii.as<int32_t>(), w.tile_diff.as<int32_t>(), s);
+        MsplatGaussians recv{};
+        recv.num_points = m;
+        recv.sh_degree = sh_degree;
+        const int r0 = band_end > band_begin ? std::max(0, band_begin - 1) : 0;
+        const int r1 = band_end > band_begin ? std::min(ty, band_end + 1) : 0;
+        stage_forward(w, &recv, cd, 0, 1.0f, 0.01f, background, false, r0, r1, s, 0, 0, nullptr, nullptr, false,
+                      nullptr, nullptr, nullptr, lambda_dist != 0.0f, /*prefilled=*/true);
+        const int p0 = std::min(cd.height, band_begin * kTile), p1 = std::min(cd.height, band_end * kTile);
+        if (m > 0) CK(cudaMemsetAsync(raster_grads_out, 0, nn * kGradStride * 4, s));
+        if (p1 > p0) {
+            stage_loss(w, cd, gt, lambda_l1, lambda_dist, lambda_dssim, p0, p1, false, s);
+            if (m > 0) stage_raster_backward(w, cd, background, lambda_dist, band_begin, band_end, raster_grads_out, s);
+            const int nb = loss_num_blocks(cd.width, p0, p1);
+            launch_loss_finalize(w.loss_partials.as<double>(), nb, 0.0f, 0.0f, w.loss_out.as<double>(), nullptr,
+                                 w.err.as<uint32_t>(), s);
+            // loss_out = {l1 + dist, ssim, l1, dist} -> parts (l1, ssim, dist)
+            CK(cudaMemcpyAsync(loss_parts_dev, w.loss_out.as<double>() + 2, sizeof(double), cudaMemcpyDeviceToDevice, s));
+            CK(cudaMemcpyAsync(loss_parts_dev + 1, w.loss_out.as<double>() + 1, sizeof(double), cudaMemcpyDeviceToDevice,
+                               s));
+            CK(cudaMemcpyAsync(loss_parts_dev + 2, w.loss_out.as<double>() + 3, sizeof(double), cudaMemcpyDeviceToDevice,
+                               s));
+        } else {
+            CK(cudaMemsetAsync(loss_parts_dev, 0, 3 * sizeof(double), s));
+        }
+        mark(w, kStBetweenShardCalls, s);
+        CK(cudaGetLastError());
+    });
+}
+
+int msplat_route_return(const float* recv_grads, int64_t num_items, float* slice_grads, void* stream) {
+    return guarded([&] {
+        Workspace& w = workspace();
+        if (num_items != w.route_items) throw Error(MSPLAT_ERR_ARGUMENT, "num_items differs from the packed items");
+        if (!slice_grads || (num_items > 0 && !recv_grads)) throw Error(MSPLAT_ERR_ARGUMENT, "null buffer");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (w.route_n > 0) CK(cudaMemsetAsync(slice_grads, 0, (size_t)w.route_n * kGradStride * 4, s));
+        launch_route_gather(num_items, reinterpret_cast<const float4*>(recv_grads), w.route_src.as<int32_t>(),
+                            slice_grads, s);
+        CK(cudaGetLastError());
+    });
+}
+
+int msplat_route_project_backward_adam(const MsplatGaussians* g, const MsplatCamera* cam, int32_t degrees_to_use,
+                                       const float* slice_grads, const MsplatAdamState* adam, float* xys_grad_norm,
+                                       float* vis_counts, float* max_2d_size, void* stream) {
+    return guarded([&] {
+        check_inputs(g, cam, degrees_to_use);
+        Workspace& w = workspace();
+        const int g0 = w.route_g0, g1 = w.route_g0 + w.route_n;
+        if (g1 > g->num_points) throw Error(MSPLAT_ERR_ARGUMENT, "slice beyond num_points");
+        if (w.route_n > 0 && !slice_grads) throw Error(MSPLAT_ERR_ARGUMENT, "null slice_grads");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        CameraDev cd = make_cam(cam);
+        // the kernel indexes by global id: offset the slice buffers
+        ProjBwdArgs pb = make_proj_bwd(w, g, cd, degrees_to_use, 1.0f, slice_grads - (size_t)g0 * kGradStride, g0, g1);
+        pb.radii = w.own_radii.as<int32_t>() - g0;
         set_adam(pb, adam);
         pb.xys_grad_norm = xys_grad_norm; pb.vis_counts = vis_counts; pb.max_2d_size = max_2d_size;
         mark(w, kStProjectBwd, s);

@@ -35,25 +35,6 @@ namespace msplat {
 namespace {
 
 constexpr int kCountThreads = 1024;
-// Work estimate of a tile row for band balancing: kept intersections plus a
-// per-tile cost in the same unit. Fitted to per-rank rasteriser + loss times
-// of 8 ranks on the 4946x3286 benchmark scene (time ~ 0.33 ns per kept
-// intersection + 144 ns per tile): per-pixel outputs and the loss cost the
-// same for every tile, and sparse regions carry larger surfels that blend
-// over more pixels per intersection.
-constexpr int kRowWorkPerTile = 430;
-
-// First row of band r of `world` contiguous bands of about equal work
-// (rows are added while less than half of the next row's work overshoots).
-__device__ int band_cut(const int64_t* work, int ty, double total, int r, int world) {
-    if (r <= 0) return 0;
-    if (r >= world) return ty;
-    const double target = total * r / world;
-    double run = 0;
-    int y = 0;
-    while (y < ty && run + (double)work[y] / 2 < target) run += (double)work[y++];
-    return y;
-}
 
 // Per-tile intersection counts of one id chunk (blockIdx.x) from its 2-D
 // difference array: column prefix over y (one thread per tile column), then

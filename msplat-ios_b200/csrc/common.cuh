@@ -62,6 +62,26 @@ __device__ __forceinline__ float reject_rho(float opac) {
 //   [10..12] dL/d(raw SH colour)      [13..15] dL/d(world normal)
 constexpr int kGradStride = 16;
 
+// Work estimate of a tile row for band balancing across GPUs: kept
+// intersections plus a per-tile cost in the same unit. Fitted to per-rank
+// rasteriser + loss times of 8 ranks on the 4946x3286 benchmark scene
+// (time ~ 0.33 ns per kept intersection + 144 ns per tile): per-pixel outputs
+// and the loss cost the same for every tile, and sparse regions carry larger
+// surfels that blend over more pixels per intersection.
+constexpr int kRowWorkPerTile = 430;
+
+// First row of band r of `world` contiguous bands of about equal work
+// (rows are added while less than half of the next row's work overshoots).
+__device__ inline int band_cut(const int64_t* work, int ty, double total, int r, int world) {
+    if (r <= 0) return 0;
+    if (r >= world) return ty;
+    const double target = total * r / world;
+    double run = 0;
+    int y = 0;
+    while (y < ty && run + (double)work[y] / 2 < target) run += (double)work[y++];
+    return y;
+}
+
 __device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
 __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
 __device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }

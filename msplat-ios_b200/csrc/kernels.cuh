@@ -194,6 +194,54 @@ int loss_ssim_noalloc(const float* out_img, const float* gt, const float* out_di
                       float lambda_l1, float lambda_dist, float lambda_dssim, float* dL_dout_img, float* loss_out,
                       cudaStream_t s, std::string* msg);
 
+// ---- routed multi-GPU exchange (route.cu) -------------------------------------
+// Route summary of a slice ([tiles + 2 (ty + 1)] int32): per-tile counts
+// from its projection's difference array, then the number of the slice's
+// routable Gaussians whose tile rectangle starts at row y, then those whose
+// rectangle ends at row y (y in [0, ty]). rowsum: scratch [ty * tx].
+inline int64_t route_summary_len(int tx, int ty) { return (int64_t)tx * ty + 2 * (int64_t)(ty + 1); }
+void launch_route_summary(const int32_t* diff, int tx, int ty, int n, const uint2* rects, const int32_t* radii,
+                          int32_t* rowsum, int32_t* summary, cudaStream_t s);
+// From the summaries of all ranks ([world][summary length]): the bands of all
+// ranks (bands [world + 1]), the items from every rank to every rank
+// (matrix [world][world], int64), the destination range of each projected
+// Gaussian of this slice, per-block offsets per destination (block_counts,
+// scanned in place) and this slice's items per destination (totals [world]).
+void launch_route_plan(const int32_t* summaries, int tx, int ty, int world, int64_t* row_work, int32_t* bands,
+                       int64_t* matrix, int n, const uint2* rects, const int32_t* radii, int2* dest,
+                       int32_t* block_counts, int64_t* totals, int64_t* base, cudaStream_t s);
+// A routed Gaussian: raster record (5 float4), cull record (2 float4), then
+// (rect.x bits, rect.y bits, depth, global id bits).
+constexpr int kRoutePayloadF4 = 8;
+// Where the routed items go: group q (the items for destination rank q)
+// starts at dst[q] (a local send buffer or a peer's inbox mapped here), and
+// send_base[q] is its first item in this rank's packing order.
+struct RouteDests {
+    float4* dst[kMaxPeerRanks];
+    int64_t send_base[kMaxPeerRanks];
+};
+// Where the band's records go back: items from source r (received items
+// [recv_off[r], recv_off[r+1])) to dst[r] (the owner's return box at this
+// band's group, mapped here).
+struct RouteReturns {
+    float4* dst[kMaxPeerRanks];
+    int64_t recv_off[kMaxPeerRanks + 1];
+};
+// 128-byte payloads of the slice's Gaussians per destination;
+// src[item] = local index (packing order). fence: system-scope fence after
+// the stores (peer destinations).
+void launch_route_pack(int n, int g0, const float4* records, const float4* cull, const uint2* rects,
+                       const float* depths, const int2* dest, const int32_t* block_offsets, int world,
+                       const RouteDests& d, bool fence, int32_t* src, cudaStream_t s);
+// The band's records [m, 16] back to their owners' return boxes.
+void launch_route_push(int64_t m, const float4* grads, int world, const RouteReturns& ret, cudaStream_t s);
+// Received payloads into the binning and rasteriser arrays (radii = 1: the
+// received set is visible) and the per-id-chunk difference arrays.
+void launch_route_unpack(int64_t m, const float4* in, int tx, int ty, int id_chunk, float4* records, float4* cull,
+                         uint2* rects, float* depths, int32_t* ids, int32_t* radii, int32_t* tile_diff,
+                         cudaStream_t s);
+void launch_route_gather(int64_t items, const float4* grads, const int32_t* src, float* slice_grads, cudaStream_t s);
+
 // ---- image helpers of the trainer API (image_ops.cu) --------------------------
 void launch_resize_area(const float* src, int sw, int sh, float* dst, int dw, int dh, cudaStream_t s);
 void launch_rgba8(const float* src, uint8_t* dst, int64_t n, cudaStream_t s);

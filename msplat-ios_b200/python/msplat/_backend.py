@@ -60,6 +60,12 @@ class MsplatPeerParams(C.Structure):
     _fields_ = [("world", C.c_int32), ("chunk", C.c_int32), ("base", (C.c_void_p * MAX_PEER_RANKS) * 6)]
 
 
+class MsplatRoutePeers(C.Structure):
+    _fields_ = [("world", C.c_int32), ("rank", C.c_int32), ("inbox_items", C.c_int64),
+                ("returnbox_items", C.c_int64), ("inbox", C.c_void_p * MAX_PEER_RANKS),
+                ("returnbox", C.c_void_p * MAX_PEER_RANKS)]
+
+
 class MsplatTensorRef(C.Structure):
     _fields_ = [("data", C.c_void_p), ("shape", C.c_int64 * 4), ("ndim", C.c_int32), ("dtype", C.c_int32)]
 
@@ -107,6 +113,17 @@ def load():
     L.msplat_shard_project_backward_adam.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, vp,
                                                      i32, i32, C.POINTER(MsplatAdamState), vp, vp, vp, vp]
     L.msplat_last_tensor.argtypes = [C.c_char_p, C.POINTER(MsplatTensorRef)]
+    L.msplat_route_project.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, i32, i32, vp, vp]
+    L.msplat_route_summary_len.argtypes = [C.POINTER(MsplatCamera), C.POINTER(C.c_int64)]
+    L.msplat_route_plan.argtypes = [vp, C.POINTER(MsplatCamera), i32, i32, C.POINTER(C.c_int32), C.POINTER(C.c_int64),
+                                    C.POINTER(C.c_int64), vp]
+    L.msplat_route_pack.argtypes = [vp, vp]
+    L.msplat_route_pack_peers.argtypes = [C.POINTER(MsplatRoutePeers), vp]
+    L.msplat_route_push_peers.argtypes = [C.POINTER(MsplatRoutePeers), vp, vp]
+    L.msplat_route_band.argtypes = [C.POINTER(MsplatCamera), i32, vp, i64, i32, i32, fp3, vp, f, f, f, vp, vp, vp]
+    L.msplat_route_return.argtypes = [vp, i64, vp, vp]
+    L.msplat_route_project_backward_adam.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatCamera), i32, vp,
+                                                     C.POINTER(MsplatAdamState), vp, vp, vp, vp]
     L.msplat_prepare_camera.argtypes = [C.POINTER(C.c_float), f, f, f, f, i32, i32, C.POINTER(MsplatCamera)]
     L.msplat_densify_plan.argtypes = [C.POINTER(MsplatGaussians), C.POINTER(MsplatDensifyArgs),
                                       C.POINTER(MsplatDensifyPlan), vp]
@@ -132,6 +149,9 @@ def load():
                  "msplat_device_alloc", "msplat_device_free",
                  "msplat_ipc_handle", "msplat_ipc_open", "msplat_ipc_close",
                  "msplat_shard_project_backward_adam", "msplat_last_tensor", "msplat_prepare_camera",
+                 "msplat_route_summary_len", "msplat_route_project", "msplat_route_plan", "msplat_route_pack", "msplat_route_pack_peers",
+                 "msplat_route_push_peers", "msplat_route_band",
+                 "msplat_route_return", "msplat_route_project_backward_adam",
                  "msplat_densify_plan", "msplat_densify_apply", "msplat_reset_opacity"):
         getattr(L, name).restype = C.c_int
     _lib = L
@@ -328,6 +348,74 @@ def shard_project_backward_adam(g, cam, degrees_to_use, raster_grads, g0, g1, ad
     sp = [None, None, None] if stats is None else [_ptr(s) for s in stats]
     _check(load().msplat_shard_project_backward_adam(C.byref(gs), C.byref(cam), degrees_to_use, _ptr(raster_grads),
                                                      g0, g1, C.byref(st), sp[0], sp[1], sp[2], _stream(stream)))
+
+
+# ---- routed multi-GPU exchange (msplat_route_*) --------------------------------
+
+ROUTE_PAYLOAD_FLOATS = 32  # 128 bytes per routed Gaussian
+
+
+def route_summary_len(cam) -> int:
+    """Length (int32 entries) of a slice's route summary for this camera."""
+    n = C.c_int64()
+    _check(load().msplat_route_summary_len(C.byref(cam), C.byref(n)))
+    return int(n.value)
+
+
+def route_project(g, cam, degrees_to_use, g0, g1, summary, stream=None):
+    """Projects Gaussians [g0, g1) of g; summary (int32 [route_summary_len])
+    receives the slice's per-tile intersection counts and the histograms of
+    its tile rectangles' first and last rows."""
+    gs = g.struct()
+    _check(load().msplat_route_project(C.byref(gs), C.byref(cam), degrees_to_use, g0, g1, _ptr(summary),
+                                       _stream(stream)))
+
+
+def route_plan(summaries, cam, world, rank, stream=None):
+    """(bands [world + 1], items sent to each rank [world], items received
+    from each rank [world]) as host lists, from all ranks' summaries
+    (int32 [world, route_summary_len])."""
+    bands = (C.c_int32 * (world + 1))()
+    send = (C.c_int64 * world)()
+    recv = (C.c_int64 * world)()
+    _check(load().msplat_route_plan(_ptr(summaries), C.byref(cam), world, rank, bands, send, recv, _stream(stream)))
+    return list(bands), list(send), list(recv)
+
+
+def route_pack(send_payload, stream=None):
+    _check(load().msplat_route_pack(_ptr(send_payload) if send_payload.numel() else None, _stream(stream)))
+
+
+def route_pack_peers(peers: MsplatRoutePeers, stream=None):
+    """Packs into every destination's inbox (peer stores)."""
+    _check(load().msplat_route_pack_peers(C.byref(peers), _stream(stream)))
+
+
+def route_push_peers(peers: MsplatRoutePeers, raster_grads, stream=None):
+    """The band's records back into their owners' return boxes (peer stores)."""
+    _check(load().msplat_route_push_peers(C.byref(peers), _ptr(raster_grads) if raster_grads.numel() else None,
+                                          _stream(stream)))
+
+
+def route_band(cam, sh_degree, recv_payload, num_recv, band, background, gt, lambda_l1, lambda_dist, lambda_dssim,
+               raster_grads, loss_parts, stream=None):
+    _check(load().msplat_route_band(C.byref(cam), sh_degree, _ptr(recv_payload) if num_recv else None, num_recv,
+                                    int(band[0]), int(band[1]), _bg(background), _ptr(gt), lambda_l1, lambda_dist,
+                                    lambda_dssim, _ptr(raster_grads) if num_recv else None, _ptr(loss_parts),
+                                    _stream(stream)))
+
+
+def route_return(recv_grads, num_items, slice_grads, stream=None):
+    _check(load().msplat_route_return(_ptr(recv_grads) if num_items else None, num_items, _ptr(slice_grads),
+                                      _stream(stream)))
+
+
+def route_project_backward_adam(g, cam, degrees_to_use, slice_grads, adam: "AdamState", stats=None, stream=None):
+    gs = g.struct()
+    st = adam.struct()
+    sp = [None, None, None] if stats is None else [_ptr(s) for s in stats]
+    _check(load().msplat_route_project_backward_adam(C.byref(gs), C.byref(cam), degrees_to_use, _ptr(slice_grads),
+                                                     C.byref(st), sp[0], sp[1], sp[2], _stream(stream)))
 
 
 _DT = {0: "float32", 1: "int32", 2: "int64"}

@@ -268,3 +268,203 @@ def colors_fn(B, g, cam_next, degree, rgb_full):
     def colors_next(g0, g1):
         B.shard_colors(g, cam_next, degree, g0, g1, rgb_full)
     return colors_next
+
+
+# ---------------------------------------------------------------- routed exchange
+PAYLOAD_FLOATS = 32  # 128 bytes per routed Gaussian
+
+
+def routed_step(dist, plan: ShardPlan, calls, parts, marks=None):
+    """One training step with the routed exchange (msplat_route_*): each rank
+    projects only its own Gaussians and sends each projected Gaussian to the
+    ranks whose tile-row band (plus a one-row halo) it touches; every rank
+    rasterises its band over what it received and sends the per-Gaussian
+    gradient records back to their owners, which run the projection VJP and
+    Adam on their slice. Nothing is gathered: each rank reads only its own
+    slice of the parameters.
+
+    calls (objects with these methods; bound to the C ABI by gpu_route_calls,
+    or to a CPU stand-in in the tests):
+      project()                  -> the slice's summary (int32 tensor [L]):
+                                    per-tile intersection counts and the
+                                    histograms of its rectangles' first and
+                                    last tile rows
+      plan(summaries)            -> (bands [world + 1], items sent to each
+                                    rank [world], items received from each
+                                    rank [world]) from all ranks' summaries
+                                    ([world, L], rank order)
+      pack(n_items)              -> payload tensor [n_items, 32] grouped by
+                                    destination, increasing id per group
+      band(payload, n, band, parts) -> raster-gradient records [n, 16] of the
+                                    received Gaussians; parts [3] loss sums
+      give_back(records, n_items) -> adds the returned records per own
+                                    Gaussian (packing order)
+      adam()                     -> projection VJP + Adam on the slice
+    Returns the bands. Every rank issues the collectives in the same order:
+    one all-gather of the summaries, two all-to-alls, one all-reduce.
+    """
+    import torch
+    mark = marks if marks is not None else (lambda name: None)
+    peers = getattr(calls, "peers", None)
+    summary = calls.project()
+    gathered = torch.empty((plan.world, summary.numel()), dtype=summary.dtype, device=summary.device)
+    if dist.get_backend() == "nccl":
+        dist.all_gather_into_tensor(gathered, summary)
+    else:  # gloo has no all_gather_into_tensor
+        dist.all_gather(list(gathered.unbind(0)), summary)
+    bands, send_counts, recv_counts = calls.plan(gathered)
+    mark("project_plan")
+    n_send, n_recv = sum(send_counts), sum(recv_counts)
+    if peers is not None:
+        # payloads stored straight into the destinations' inboxes; a
+        # one-element all-reduce orders every rank's pack before any band
+        calls.pack_peers()
+        dist.all_reduce(peers.fence)
+        recv_buf = peers.inbox_view(n_recv)
+    else:
+        send_buf = calls.pack(n_send)
+        recv_buf = torch.empty((n_recv, PAYLOAD_FLOATS), dtype=send_buf.dtype, device=send_buf.device)
+        dist.all_to_all_single(recv_buf, send_buf, output_split_sizes=recv_counts, input_split_sizes=send_counts)
+    mark("route")
+    grads = calls.band(recv_buf, n_recv, (bands[plan.rank], bands[plan.rank + 1]), parts)
+    mark("band")
+    if peers is not None:
+        calls.push(grads[:n_recv])
+        dist.all_reduce(peers.fence)
+        back = peers.returnbox_view(n_send)
+    else:
+        back = torch.empty((n_send, GRAD_STRIDE), dtype=grads.dtype, device=grads.device)
+        dist.all_to_all_single(back, grads[:n_recv], output_split_sizes=send_counts, input_split_sizes=recv_counts)
+    mark("return")
+    calls.give_back(back, n_send)
+    calls.adam()
+    mark("project_adam")
+    dist.all_reduce(parts)
+    mark("all_reduce")
+    plan.row0, plan.row1 = bands[plan.rank], bands[plan.rank + 1]
+    return bands
+
+
+class RoutePeers:
+    """Inboxes and return boxes of the routed exchange that every rank maps
+    through CUDA IPC (msplat_route_pack_peers / msplat_route_push_peers).
+    Rank q's inbox holds up to n_total 128-byte payloads (a band receives a
+    Gaussian at most once); its return box up to world * chunk 64-byte
+    records (each own Gaussian goes to at most every band). When any rank
+    cannot map its peers, `ok` is False on every rank and routed_step keeps
+    the NCCL all-to-alls. close() must run on every rank."""
+
+    def __init__(self, B, dist, plan: ShardPlan, n_total: int, device):
+        import torch
+        if plan.world > B.MAX_PEER_RANKS:
+            raise ValueError("too many ranks for the peer view")
+        self.B, self.dist = B, dist
+        self.inbox_items = max(int(n_total), 1)
+        self.returnbox_items = max(plan.chunk * plan.world, 1)
+        self.own = [B.device_alloc(self.inbox_items * PAYLOAD_FLOATS * 4),
+                    B.device_alloc(self.returnbox_items * GRAD_STRIDE * 4)]
+        self.mapped = []
+        self.inbox = torch.as_tensor(B.DeviceArray(self.own[0], (self.inbox_items, PAYLOAD_FLOATS)), device=device)
+        self.returnbox = torch.as_tensor(B.DeviceArray(self.own[1], (self.returnbox_items, GRAD_STRIDE)),
+                                         device=device)
+        self.fence = torch.zeros(1, dtype=torch.int32, device=device)
+        torch.cuda.synchronize()
+        handles = [B.ipc_handle(p) for p in self.own]
+        everyone = [None] * plan.world
+        dist.all_gather_object(everyone, handles)
+        st = B.MsplatRoutePeers()
+        st.world, st.rank = plan.world, plan.rank
+        st.inbox_items, st.returnbox_items = self.inbox_items, self.returnbox_items
+        self.error = ""
+        try:
+            for q in range(plan.world):
+                for k, field in enumerate((st.inbox, st.returnbox)):
+                    if q == plan.rank:
+                        ptr = self.own[k]
+                    else:
+                        ptr = B.ipc_open(everyone[q][k])
+                        self.mapped.append(ptr)
+                    field[q] = ptr
+        except Exception as e:  # e.g. no peer access between these GPUs
+            self.error = str(e)
+        ok = torch.tensor([0 if self.error else 1], device=device, dtype=torch.int32)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        self.ok = bool(ok.item())
+        if not self.ok:
+            for p in self.mapped:
+                B.ipc_close(p)
+            self.mapped = []
+            self.error = self.error or "a peer could not map this rank's boxes"
+        self.struct = st if self.ok else None
+        dist.barrier()
+
+    def inbox_view(self, n):
+        return self.inbox[:n]
+
+    def returnbox_view(self, n):
+        return self.returnbox[:n]
+
+    def close(self):
+        import torch
+        torch.cuda.synchronize()
+        self.dist.barrier()  # no rank writes into a peer box any more
+        for p in self.mapped:
+            self.B.ipc_close(p)
+        self.mapped = []
+        self.dist.barrier()  # no rank maps this rank's boxes any more
+        self.inbox = self.returnbox = None
+        for p in self.own:
+            self.B.device_free(p)
+        self.own = []
+
+
+class gpu_route_calls:
+    """The callables of routed_step bound to the C ABI (msplat_route_*);
+    with `peers` (a RoutePeers whose mapping succeeded) the payloads and the
+    returned records move by peer stores instead of NCCL all-to-alls."""
+
+    def __init__(self, B, g, cam, degree, bg, gt, lambda_l1, lambda_dist, lambda_dssim, adam_state, stats,
+                 shard_plan, tiles=None, peers=None):
+        import torch
+        self.peers = peers if (peers is not None and peers.ok) else None
+        self.B, self.g, self.cam, self.degree, self.bg, self.gt = B, g, cam, degree, bg, gt
+        self.l1, self.ld, self.lds = lambda_l1, lambda_dist, lambda_dssim
+        self.adam_state, self.stats, self.shard_plan = adam_state, stats, shard_plan
+        dev = g.means.device
+        self.dev = dev
+        self.summary = torch.zeros(B.route_summary_len(cam), dtype=torch.int32, device=dev)
+        self.slice_grads = torch.zeros((max(shard_plan.g_end - shard_plan.g_begin, 1), GRAD_STRIDE), device=dev)
+
+    def project(self):
+        p = self.shard_plan
+        self.B.route_project(self.g, self.cam, self.degree, p.g_begin, p.g_end, self.summary)
+        return self.summary
+
+    def plan(self, summaries):
+        return self.B.route_plan(summaries, self.cam, self.shard_plan.world, self.shard_plan.rank)
+
+    def pack(self, n_items):
+        import torch
+        buf = torch.empty((n_items, PAYLOAD_FLOATS), device=self.dev)
+        self.B.route_pack(buf)
+        return buf
+
+    def band(self, payload, n, band, parts):
+        import torch
+        grads = torch.empty((max(n, 1), GRAD_STRIDE), device=self.dev)
+        self.B.route_band(self.cam, self.g.sh_degree, payload, n, band, self.bg, self.gt, self.l1, self.ld,
+                          self.lds, grads, parts)
+        return grads
+
+    def pack_peers(self):
+        self.B.route_pack_peers(self.peers.struct)
+
+    def push(self, grads):
+        self.B.route_push_peers(self.peers.struct, grads)
+
+    def give_back(self, records, n_items):
+        self.B.route_return(records, n_items, self.slice_grads)
+
+    def adam(self):
+        self.B.route_project_backward_adam(self.g, self.cam, self.degree, self.slice_grads, self.adam_state,
+                                           stats=self.stats)

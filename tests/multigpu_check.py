@@ -6,7 +6,12 @@ side stream while the next step bins; MSPLAT_EXCHANGE=nccl), with the
 geometry all-gathered and the colour read from its owner rank through CUDA
 IPC (MSPLAT_EXCHANGE=peers), or with the geometry all-gathered and the
 owners' clamped colours for the next camera all-gathered instead of the
-colour coefficients (MSPLAT_EXCHANGE=rgb); rank 0 also runs the same two
+colour coefficients (MSPLAT_EXCHANGE=rgb), or with the routed exchange
+(MSPLAT_EXCHANGE=route: each owner projects its slice, the projected
+Gaussians go to the bands they touch and the gradients come back to the
+owner, by NCCL all-to-alls; MSPLAT_EXCHANGE=route-peer: by stores into the
+other GPU's inbox and return box over NVLink; nothing is gathered); rank 0
+also runs the same two
 steps with the single-GPU fused
 step on a private copy and compares the parameters. Prints "MULTIGPU OK" on
 success (rank 0) and exits non-zero otherwise.
@@ -50,6 +55,15 @@ def main():
         adam = B.AdamState(g)
     else:
         sharding.pad_gaussians(g, plan.padded)
+    route = route_peers = None
+    if exchange in ("route", "route-peer"):
+        if exchange == "route-peer":
+            route_peers = sharding.RoutePeers(B, dist, plan, n, dev)
+            if not route_peers.ok:
+                print("peer mapping failed: " + route_peers.error, flush=True)
+                sys.exit(1)
+        route = sharding.gpu_route_calls(B, g, cam, case.degree, case.bg, gt, 0.8, 0.0, 0.2, adam, None, plan,
+                                         peers=route_peers)
     rgb_full = torch.zeros(plan.padded, 3, device=dev) if exchange == "rgb" else None
     rg = torch.zeros(plan.padded, 16, device=dev)
     rg_shard = torch.zeros(plan.chunk, 16, device=dev)
@@ -58,7 +72,7 @@ def main():
     # gathered on a side stream while the next step bins its geometry
     side = torch.cuda.Stream(device=dev)
     ready = None
-    for step in range(2):
+    for step in range(2 if route is None else 0):
         adam.step += 1
         fb, pa = sharding.gpu_step_fns(B, g, cam, case.degree, case.bg, gt, 0.8, 0.0, 0.2, adam, None,
                                        features_ready=ready, split_color=peers is None, peers=peers,
@@ -68,9 +82,15 @@ def main():
                                       side_stream=None if peers else side,
                                       skip_color=peers is not None or rgb_full is not None,
                                       colors_next=colors_next, rgb_full=rgb_full)
+    bands = None
+    for step in range(2 if route is not None else 0):
+        adam.step += 1
+        bands = sharding.routed_step(dist, plan, route, parts)
+    if bands is not None and rank == 0:
+        print(f"bands {bands}", flush=True)
     torch.cuda.synchronize()
     loss_sh = sharding.loss_from_parts(parts.cpu().numpy(), 0.2, cfg.width, cfg.height)
-    if peers is not None or rgb_full is not None:
+    if peers is not None or rgb_full is not None or route is not None:
         # each rank's colour buffers are current only in the rows it owns:
         # gather them once to compare the whole parameter set
         rows = plan.slice_rows()
@@ -84,6 +104,8 @@ def main():
         torch.cuda.synchronize()
         if peers is not None:
             peers.close()
+        if route_peers is not None:
+            route_peers.close()
     else:
         got = [t.cpu().numpy() for t in g.groups()]
     ok = True

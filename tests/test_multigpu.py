@@ -14,7 +14,7 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-@pytest.mark.parametrize("exchange", ["nccl", "peers", "rgb"])
+@pytest.mark.parametrize("exchange", ["nccl", "peers", "rgb", "route", "route-peer"])
 def test_two_gpu_sharded_step_matches_single_gpu(exchange):
     torch = pytest.importorskip("torch")
     if torch.cuda.device_count() < 2:
