@@ -64,15 +64,15 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--exchange", default="rgb", choices=["peers", "nccl", "rgb", "route", "route-peer"],
+    ap.add_argument("--exchange", default="route-peer", choices=["peers", "nccl", "rgb", "route", "route-peer"],
                     help="multi-GPU parameter exchange: geometry all-gathered and the owners' colours for the "
-                         "next camera all-gathered instead of the colour coefficients (rgb, default); NCCL "
+                         "next camera all-gathered instead of the colour coefficients (rgb); NCCL "
                          "all-gathers of all groups with the colour groups overlapped with binning (nccl); "
                          "geometry all-gathered and colour read from its owner over NVLink (CUDA IPC, peers); "
                          "or each owner projects its slice and sends the projected Gaussians to the bands they "
                          "touch, gradients come back to the owner, nothing is gathered (route: NCCL "
-                         "all-to-alls; route-peer: the pack and return kernels store straight into the other "
-                         "GPUs' inboxes over NVLink)")
+                         "all-to-alls; route-peer, default: the pack and return kernels store straight into "
+                         "the other GPUs' inboxes over NVLink)")
     ap.add_argument("--render-frames", type=int, default=20,
                     help="render-only frames timed after the training steps (single GPU); 0 = skip")
     ap.add_argument("--cameras", type=int, default=0,

@@ -285,6 +285,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_pack(
     const uint2* __restrict__ rects, const float* __restrict__ depths, const int2* __restrict__ dest,
     const int32_t* __restrict__ block_offsets, int world, RouteDests d, int fence, int32_t* __restrict__ src) {
     __shared__ int wcount[kMaxPeerRanks][kRouteThreads / 32];
+    __shared__ int slane[kRouteThreads / 32][32];  // per warp: t-th going lane
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int2 dq = i < n ? dest[i] : make_int2(-1, -2);
@@ -293,22 +294,41 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_pack(
         if (lane == 0) wcount[q][warp] = __popc(b);
     }
     __syncthreads();
+    const int i0 = blockIdx.x * blockDim.x + warp * 32;  // the warp's first local index
     for (int q = 0; q < world; ++q) {
         const bool goes = q >= dq.x && q <= dq.y;
         const unsigned b = __ballot_sync(0xffffffffu, goes);
-        if (!goes) continue;
-        int before = __popc(b & ((1u << lane) - 1u));
-        for (int w2 = 0; w2 < warp; ++w2) before += wcount[q][w2];
-        const int64_t k = block_offsets[(size_t)blockIdx.x * world + q] + before;
-        float4* o = d.dst[q] + k * kRoutePayloadF4;
-#pragma unroll
-        for (int c = 0; c < kRecordF4; ++c) o[c] = records[(size_t)i * kRecordF4 + c];
-#pragma unroll
-        for (int c = 0; c < kCullF4; ++c) o[kRecordF4 + c] = cull[(size_t)i * kCullF4 + c];
-        const uint2 r = rects[i];
-        o[kRecordF4 + kCullF4] = make_float4(__uint_as_float(r.x), __uint_as_float(r.y), depths[i],
-                                             __int_as_float(g0 + i));
-        src[d.send_base[q] + k] = i;
+        if (b == 0u) continue;
+        // the warp's items for q are consecutive in the group, from k0
+        int wbefore = 0;
+        for (int w2 = 0; w2 < warp; ++w2) wbefore += wcount[q][w2];
+        const int64_t k0 = block_offsets[(size_t)blockIdx.x * world + q] + wbefore;
+        const int rk = __popc(b & ((1u << lane) - 1u));
+        if (goes) {
+            src[d.send_base[q] + k0 + rk] = i;
+            slane[warp][rk] = lane;
+        }
+        __syncwarp();
+        // the warp writes the run together: four whole payloads (512
+        // contiguous bytes) per store instruction, lane l the float4 l % 8
+        // of payload l / 8 (peer stores stay full-line over NVLink)
+        const int cnt = __popc(b);
+        float4* run = d.dst[q] + k0 * kRoutePayloadF4;
+        for (int idx = lane; idx < cnt * kRoutePayloadF4; idx += 32) {
+            const int t = idx / kRoutePayloadF4, c = idx % kRoutePayloadF4;
+            const int j = i0 + slane[warp][t];  // t-th lane going to q (t < cnt)
+            float4 v;
+            if (c < kRecordF4) {
+                v = records[(size_t)j * kRecordF4 + c];
+            } else if (c < kRecordF4 + kCullF4) {
+                v = cull[(size_t)j * kCullF4 + (c - kRecordF4)];
+            } else {
+                const uint2 r = rects[j];
+                v = make_float4(__uint_as_float(r.x), __uint_as_float(r.y), depths[j], __int_as_float(g0 + j));
+            }
+            run[idx] = v;
+        }
+        __syncwarp();  // slane is rewritten for the next destination
     }
     if (fence) __threadfence_system();
 }
@@ -319,13 +339,17 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_pack(
 // return box at the offset of this band's group, written over NVLink).
 __global__ void __launch_bounds__(kRouteThreads) k_route_push(int64_t m, const float4* __restrict__ grads, int world,
                                                               RouteReturns ret) {
-    const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (j < m) {
+    // a warp moves 32 items, eight whole records (512 bytes) per store
+    // instruction: lane l the float4 l % 4 of item l / 4 of each group of 8
+    constexpr int kF4 = kGradStride / 4;
+    const int lane = threadIdx.x & 31;
+    const int64_t j0 = ((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31));
+    for (int idx = lane; idx < 32 * kF4; idx += 32) {
+        const int64_t j = j0 + idx / kF4;
+        if (j >= m) break;
         int r = 0;
         while (r + 1 < world && j >= ret.recv_off[r + 1]) ++r;
-        float4* o = ret.dst[r] + (j - ret.recv_off[r]) * (kGradStride / 4);
-#pragma unroll
-        for (int c = 0; c < kGradStride / 4; ++c) o[c] = grads[j * (kGradStride / 4) + c];
+        ret.dst[r][(j - ret.recv_off[r]) * kF4 + idx % kF4] = grads[j * kF4 + idx % kF4];
     }
     __threadfence_system();
 }
