@@ -155,24 +155,31 @@ def param_bytes(K: int) -> int:
     return 4 * (3 + 2 + 4 + 1 + 3 + 3 * K)
 
 
-def raster_bwd_bytes(kept: int, n_vis: int, pixels: int) -> int:
+def raster_bwd_bytes(kept: int, n_vis: int, pixels: int, aux: bool = False) -> int:
     """5 B per kept intersection (sorted id + the forward's per-warp blend
-    byte), 80 B per visible Gaussian (raster record, read once), 32 B per
-    pixel (final T/M1/M2, last/median index, dL/dimg), 64 B read + 64 B
-    written per visible Gaussian (gradient record)."""
-    return 5 * kept + 80 * n_vis + 32 * pixels + 128 * n_vis
+    byte), 80 B per visible Gaussian (raster record, read once), per pixel
+    the final T, last index and dL/dimg (20 B; with the auxiliary outputs
+    also M1/M2 and the median index, 32 B), 64 B read + 64 B written per
+    visible Gaussian (gradient record)."""
+    return 5 * kept + 80 * n_vis + (32 if aux else 20) * pixels + 128 * n_vis
 
 
-def raster_fwd_bytes(kept: int, n_vis: int, pixels: int) -> int:
+def raster_fwd_bytes(kept: int, n_vis: int, pixels: int, aux: bool = False) -> int:
     """5 B per kept intersection (sorted id read, blend byte written), 112 B
-    per visible Gaussian (80 B raster record + 32 B cull record), 60 B per
-    pixel of outputs (image, T/M1/M2, indices, depth, normal, alpha, median,
-    distortion)."""
-    return 5 * kept + 112 * n_vis + 60 * pixels
+    per visible Gaussian (80 B raster record + 32 B cull record), per pixel
+    the outputs: image, final T and last index (20 B) for the colour-only
+    training step; with the auxiliary outputs also M1/M2, median index,
+    depth, normal, alpha, median and distortion (60 B)."""
+    return 5 * kept + 112 * n_vis + (60 if aux else 20) * pixels
 
 
-def byte_models(n, n_vis, K, T, P, emitted, kept):
-    """{stage: algorithmic bytes per launch} for the kernels of one step."""
+def byte_models(n, n_vis, K, T, P, emitted, kept, P_fwd=None, P_bwd=None):
+    """{stage: algorithmic bytes per launch} for the kernels of one step
+    (the colour-only training step: light forward and backward). n: the
+    Gaussians projected (and updated by Adam); P: the loss's pixels; P_fwd,
+    P_bwd: the rasterisers' pixels (default P)."""
+    P_fwd = P if P_fwd is None else P_fwd
+    P_bwd = P if P_bwd is None else P_bwd
     return {
         # parameters read; raster record 80 B, cull record 32 B, tile rect 8 B,
         # depth 4 B, radius 4 B written
@@ -184,10 +191,10 @@ def byte_models(n, n_vis, K, T, P, emitted, kept):
         "emit_keys": 12 * n + 8 * emitted,
         # keys read, sorted ids written, tile ranges read
         "tile_sort": 8 * emitted + 4 * kept + 8 * T,
-        "rasterize_forward": raster_fwd_bytes(kept, n_vis, P),
+        "rasterize_forward": raster_fwd_bytes(kept, n_vis, P_fwd),
         # image and target read, dL/dimg written
         "loss_ssim": 36 * P,
-        "rasterize_backward": raster_bwd_bytes(kept, n_vis, P),
+        "rasterize_backward": raster_bwd_bytes(kept, n_vis, P_bwd),
         # parameters, both Adam moments, gradient record and radius read;
         # parameters and both moments written; three densify statistics
         # read and written
@@ -342,7 +349,9 @@ class Stepper:
         self._evlist = []
         return {k: sum(v) / len(v) for k, v in self.phase_ms.items() if v}
 
-    def step(self, k, gt=None, cam_next_index=None):
+    def step(self, k, gt=None, cam_next_index=None, between=None):
+        """between(): enqueued mid-step by the routed exchange (after the
+        payload exchange, before the band); after the step otherwise."""
         B, C = self.B, self.C
         cam = self.cams[k % C]
         gt = self.gts[k % C] if gt is None else gt
@@ -354,7 +363,7 @@ class Stepper:
         self.adam.step += 1
         if self.route is not None:
             self.route.cam, self.route.gt = cam, gt
-            sh.routed_step(self.dist, self.plan, self.route, self.parts, marks=self._marks())
+            sh.routed_step(self.dist, self.plan, self.route, self.parts, marks=self._marks(), between=between)
             self._collect()
             return
         cam_next = self.cams[(k + 1) % C if cam_next_index is None else cam_next_index]
@@ -370,6 +379,8 @@ class Stepper:
                                           colors_next=colors_next, rgb_full=self.rgb_full, marks=self._marks())
         self.have_rgb = self.rgb_full is not None
         self._collect()
+        if between is not None:
+            between()
 
     def prime_rgb(self, cam):
         """Colours for `cam` from the owners' current coefficients (the state
@@ -565,9 +576,22 @@ def rank_breakdown(st, per_stage, kept, ws, rank, dist):
             "all_gather_ms": round(ph.get("all_gather", 0.0), 4),
             "all_reduce_ms": round(ph.get("all_reduce", 0.0), 4)}
     if st.route is not None:
-        # routed exchange: project + plan, payload all-to-all, band forward/
-        # loss/backward, gradient return, VJP + Adam, loss all-reduce
-        mine["route_phases_ms"] = {k: round(v, 4) for k, v in ph.items()}
+        # routed exchange: nothing is replicated; the phases between the
+        # library calls (CUDA events): project + plan, payload dispatch,
+        # band forward/loss/backward, gradient return, VJP + Adam, loss
+        # all-reduce; and the kernel stages of the slice projection, the
+        # exchange (summary, plan, pack and the waits for the other ranks)
+        # and the band's unpack
+        mine = {"rank": rank, "tile_rows": [st.plan.row0, st.plan.row1], "intersections": kept,
+                "slice": [st.plan.g_begin, st.plan.g_end],
+                "slice_project_ms": g("project_forward"), "route_exchange_ms": g("route_exchange"),
+                "route_unpack_ms": g("route_unpack"),
+                "bin_sort_ms": round(per_stage.get("tile_counts", 0.0) + per_stage.get("emit_keys", 0.0) +
+                                     per_stage.get("tile_sort", 0.0), 4),
+                "rasterize_forward_ms": g("rasterize_forward"), "loss_ssim_ms": g("loss_ssim"),
+                "rasterize_backward_ms": g("rasterize_backward"),
+                "project_adam_stage_ms": g("project_backward_adam"),
+                "route_phases_ms": {k: round(v, 4) for k, v in ph.items()}}
     ranks = [None] * ws
     dist.all_gather_object(ranks, mine)
     return ranks
@@ -624,7 +648,21 @@ def run_ours(args, ws, rank, local):
         pass
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
-    models = byte_models(n, n_vis, cfg.rest_bases, T, pixels, int(totals[0]), kept)
+    if ws == 1:
+        models = byte_models(n, n_vis, cfg.rest_bases, T, pixels, int(totals[0]), kept)
+    else:
+        # per rank: its band's pixels (the forward also renders the one-row
+        # halo) and, under the routed exchange, its own slice's projection
+        # and Adam; n_vis is the band's visible (received) set
+        W_, H_ = cfg.width, cfg.height
+        r0, r1 = st.plan.row0, st.plan.row1
+        px_rows = lambda a, b: max(0, min(H_, b * 16) - min(H_, a * 16)) * W_
+        band_px = px_rows(r0, r1)
+        fwd_px = px_rows(max(0, r0 - 1), min((H_ + 15) // 16, r1 + 1)) if r1 > r0 else 0
+        n_proj = (st.plan.g_end - st.plan.g_begin) if st.route is not None else n
+        models = byte_models(n_proj, n_vis, cfg.rest_bases, T, band_px, int(totals[0]), kept, P_fwd=fwd_px,
+                             P_bwd=band_px)
+
     traffic = None
     try:
         tr = json.load(open(os.path.join(REPO, "profiles", "traffic.json")))
@@ -760,50 +798,72 @@ def e2e_trainer(B, S, cfg, scene, gts, C, args, e2e_steps, render):
 
 
 def e2e_sharded(B, dist, st, gts, cams, e2e_steps, dev):
-    """Each step's target is copied host->device on a copy stream while the
-    previous step computes (two device buffers); the loss sums are read
-    back every step."""
+    """Each step's target image reaches every rank as 1/N of its rows copied
+    host->device per rank (pinned memory, a copy stream) and an NCCL
+    all-gather of the row blocks over NVLink, both for the next step while
+    the current one computes (two device buffers; under the routed exchange
+    the gather is enqueued after the payload exchange, so it runs under the
+    band's compute); the loss sums are read back every step."""
     import torch
+    ws, rank = st.ws, st.rank
     stream = st.stream
+    H, W = gts[0].shape[0], gts[0].shape[1]
+    rows = -(-H // ws)
+    r0, r1 = min(H, rank * rows), min(H, (rank + 1) * rows)
     host_gt = [gts[k].cpu().pin_memory() for k in range(min(len(gts), 4))]
-    dev_gt = [torch.empty_like(gts[0]), torch.empty_like(gts[0])]
+    dev_gt = [torch.empty((rows * ws,) + tuple(gts[0].shape[1:]), dtype=gts[0].dtype, device=dev) for _ in range(2)]
     copy_stream = torch.cuda.Stream(device=dev)
+    copied = [torch.cuda.Event(), torch.cuda.Event()]
     ready = [torch.cuda.Event(), torch.cuda.Event()]
     free = [torch.cuda.Event(), torch.cuda.Event()]
     parts_host = torch.zeros(3, dtype=torch.float64).pin_memory()
     for b in range(2):
         free[b].record(stream)
+    H_ = len(host_gt)
 
-    def prefetch(k):
+    def copy(k):
         b = k % 2
         copy_stream.wait_event(free[b])
         with torch.cuda.stream(copy_stream):
-            dev_gt[b].copy_(host_gt[k % len(host_gt)], non_blocking=True)
+            if r1 > r0:
+                dev_gt[b][r0:r1].copy_(host_gt[k % H_][r0:r1], non_blocking=True)
+            copied[b].record(copy_stream)
+
+    def gather(k):
+        b = k % 2
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(copied[b])
+            dist.all_gather_into_tensor(dev_gt[b], dev_gt[b][rank * rows:(rank + 1) * rows])
             ready[b].record(copy_stream)
 
-    H = len(host_gt)
     st.prime_rgb(cams[0])
     dist.barrier()
     t0 = time.perf_counter()
-    prefetch(0)
+    copy(0)
+    gather(0)
     for k in range(e2e_steps):
         b = k % 2
         stream.wait_event(ready[b])
-        st.step(k % H, gt=dev_gt[b], cam_next_index=(k + 1) % H)
+        nxt = k + 1 < e2e_steps
+        if nxt:
+            copy(k + 1)
+        st.step(k % H_, gt=dev_gt[b][:H], cam_next_index=(k + 1) % H_,
+                between=(lambda: gather(k + 1)) if nxt else None)
         free[b].record(stream)
-        if k + 1 < e2e_steps:
-            prefetch(k + 1)
         parts_host.copy_(st.parts, non_blocking=True)
         stream.synchronize()
     if st.pending[0] is not None:
         st.pending[0].synchronize()
+    torch.cuda.synchronize()
     e2e_s = torch.tensor([(time.perf_counter() - t0) / e2e_steps], device=dev, dtype=torch.float64)
     dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
     return {"value": round(1.0 / float(e2e_s.item()), 3), "unit": "iters/s",
-            "h2d_bytes_per_step": int(gts[0].numel() * 4), "d2h_bytes_per_step": 24, "steps": e2e_steps,
+            "h2d_bytes_per_step": int(gts[0].numel() * 4), "d2h_bytes_per_step": 24 * ws, "steps": e2e_steps,
+            "h2d_per_rank_bytes": int((r1 - r0) * gts[0][0].numel() * 4),
             "path": (("msplat_route_*" if st.route is not None else "msplat_shard_*") +
-                     " C ABI + NCCL per rank: target image H2D from pinned memory on a copy "
-                     "stream overlapping the previous step, loss sums D2H")}
+                     " C ABI + NCCL per rank: each rank copies 1/N of the target's rows host->device "
+                     "from pinned memory and the row blocks are all-gathered over NVLink, for the next "
+                     "step while the current one computes; loss sums D2H")}
 
 
 # ---------------------------------------------------------------- config 4

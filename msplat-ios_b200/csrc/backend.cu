@@ -141,14 +141,18 @@ std::vector<Workspace*> g_ws;
 // Stage timing: CUDA events recorded on the launch stream at stage
 // boundaries, read back only when msplat_stage_times() is called.
 enum Stage { kStProject = 0, kStCounts, kStEmit, kStSort, kStRasterFwd, kStLoss, kStRasterBwd, kStProjectBwd,
-             kStBetweenShardCalls, kStColor, kNumStages };
+             kStBetweenShardCalls, kStColor, kStRouteExchange, kStRouteUnpack, kNumStages };
 // between_shard_calls: from the end of msplat_shard_forward_backward to the
 // start of msplat_shard_project_backward_adam on the stream (the caller's
 // reduce-scatter and any wait for slower ranks)
 const char* kStageNames[kNumStages] = {"project_forward", "tile_counts", "emit_keys", "tile_sort",
                                        "rasterize_forward", "loss_ssim", "rasterize_backward",
                                        "project_backward_adam", "between_shard_calls",
-                                       "project_color"};  // colour pass of a split projection, incl. its wait
+                                       "project_color",   // colour pass of a split projection, incl. its wait
+                                       // routed exchange: the slice summary, the plan and the payload
+                                       // dispatch (from the end of the slice's projection to the band's
+                                       // start, incl. the caller's collectives), then the unpack
+                                       "route_exchange", "route_unpack"};
 bool g_timing = false;
 double g_stage_ms[kNumStages] = {};
 int64_t g_stage_n[kNumStages] = {};
@@ -321,8 +325,12 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
         pa.num_tiles_hit = w.num_tiles_hit.as<int32_t>(); pa.normal_opacity = w.normal_opacity.as<float>();
         pa.colors = w.colors.as<float>(); pa.aabb = w.aabb.as<float>();
     }
-    mark(w, kStProject, s);
-    if (!prefilled) launch_project_forward(pa, s);
+    // a prefilled (routed) band was projected by the owners: no projection
+    // stage here, the caller marked its unpack
+    if (!prefilled) {
+        mark(w, kStProject, s);
+        launch_project_forward(pa, s);
+    }
     mark(w, kStCounts, s);
     if (balance_world > 0) w.row_work.ensure((size_t)ty * sizeof(int64_t));
     launch_tile_counts(w.tile_diff.as<int32_t>(), id_chunk, w.chunk_counts.as<int32_t>(), w.raw_true.as<int32_t>(),
@@ -877,6 +885,7 @@ int msplat_route_project(const MsplatGaussians* g, const MsplatCamera* cam, int3
         pa.id_chunk = std::max(1, n);  // one difference array for the slice
         mark(w, kStProject, s);
         launch_project_forward(pa, s);
+        mark(w, kStRouteExchange, s);
         CK(cudaMemsetAsync(summary_out + (size_t)tx * ty, 0, 2 * (size_t)(ty + 1) * sizeof(int32_t), s));
         launch_route_summary(w.route_diff.as<int32_t>(), tx, ty, n, w.own_rects.as<uint2>(), w.own_radii.as<int32_t>(),
                              w.route_colsum.as<int32_t>(), summary_out, s);
@@ -1058,6 +1067,7 @@ int msplat_route_band(const MsplatCamera* cam, int32_t sh_degree, const void* re
         w.tile_diff.ensure(diff_bytes);
         CK(cudaMemsetAsync(w.tile_diff.p, 0, diff_bytes, s));
         const int id_chunk = std::max(1, (m + kIdChunks - 1) / kIdChunks);
+        mark(w, kStRouteUnpack, s);
         launch_route_unpack(num_recv, static_cast<const float4*>(recv_payload), tx, ty, id_chunk,
                             w.records.as<float4>(), w.cull.as<float4>(), w.rects.as<uint2>(), w.depths.as<float>(),
                             w.route_ids.as<int32_t>(), w.radii.as<int32_t>(), w.tile_diff.as<int32_t>(), s);

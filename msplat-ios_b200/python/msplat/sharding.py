@@ -274,7 +274,7 @@ def colors_fn(B, g, cam_next, degree, rgb_full):
 PAYLOAD_FLOATS = 32  # 128 bytes per routed Gaussian
 
 
-def routed_step(dist, plan: ShardPlan, calls, parts, marks=None):
+def routed_step(dist, plan: ShardPlan, calls, parts, marks=None, between=None):
     """One training step with the routed exchange (msplat_route_*): each rank
     projects only its own Gaussians and sends each projected Gaussian to the
     ranks whose tile-row band (plus a one-row halo) it touches; every rank
@@ -300,8 +300,12 @@ def routed_step(dist, plan: ShardPlan, calls, parts, marks=None):
       give_back(records, n_items) -> adds the returned records per own
                                     Gaussian (packing order)
       adam()                     -> projection VJP + Adam on the slice
+    between(): optional, called on every rank after the payloads are
+    exchanged and before the band is enqueued (e.g. to enqueue a collective
+    that should run under the band's compute).
     Returns the bands. Every rank issues the collectives in the same order:
-    one all-gather of the summaries, two all-to-alls, one all-reduce.
+    one all-gather of the summaries, two all-to-alls (or two one-element
+    all-reduces with peer stores), one all-reduce.
     """
     import torch
     mark = marks if marks is not None else (lambda name: None)
@@ -326,6 +330,8 @@ def routed_step(dist, plan: ShardPlan, calls, parts, marks=None):
         recv_buf = torch.empty((n_recv, PAYLOAD_FLOATS), dtype=send_buf.dtype, device=send_buf.device)
         dist.all_to_all_single(recv_buf, send_buf, output_split_sizes=recv_counts, input_split_sizes=send_counts)
     mark("route")
+    if between is not None:
+        between()
     grads = calls.band(recv_buf, n_recv, (bands[plan.rank], bands[plan.rank + 1]), parts)
     mark("band")
     if peers is not None:
