@@ -757,6 +757,26 @@ def time_render(B, g, cams, cfg, stream, frames, dev):
             "path": "msplat_render, image kept on the device"}
 
 
+def h2d_gbs(host, dev_view, reps=3):
+    """Host->device bandwidth of one pinned copy of `host` into `dev_view`
+    (GB/s, best of `reps`, CUDA events on a private stream): what an e2e step
+    that copies its target image is bounded by."""
+    import torch
+    s = torch.cuda.Stream()
+    best = 0.0
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            e0.record(s)
+            dev_view.copy_(host, non_blocking=True)
+            e1.record(s)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        if ms > 0:
+            best = max(best, host.numel() * host.element_size() / (ms * 1e-3) / 1e9)
+    return round(best, 2)
+
+
 def e2e_trainer(B, S, cfg, scene, gts, C, args, e2e_steps, render):
     """The metric through the public trainer API (msplat_trainer_step): every
     step copies its target image host->device from pinned memory and reads
@@ -776,8 +796,13 @@ def e2e_trainer(B, S, cfg, scene, gts, C, args, e2e_steps, render):
     for _ in range(e2e_steps):
         trainer.step()
     e2e_s = (time.perf_counter() - t0) / e2e_steps
+    import torch
+    probe_host = torch.from_numpy(host_imgs[0]).pin_memory()
+    probe_dev = torch.empty_like(probe_host, device="cuda")
+    bw = h2d_gbs(probe_host, probe_dev)
+    del probe_host, probe_dev
     e2e = {"value": round(1.0 / e2e_s, 3), "unit": "iters/s", "h2d_bytes_per_step": int(host_imgs[0].nbytes),
-           "d2h_bytes_per_step": 4, "steps": e2e_steps,
+           "d2h_bytes_per_step": 4, "steps": e2e_steps, "h2d_gbs_measured": bw,
            "path": ("msplat_trainer_step (public C API): each step's target image H2D from pinned memory "
                     "(the trainer copies the next camera's image on a copy stream during the current step), "
                     "loss D2H, sync")}
@@ -836,6 +861,7 @@ def e2e_sharded(B, dist, st, gts, cams, e2e_steps, dev):
             dist.all_gather_into_tensor(dev_gt[b], dev_gt[b][rank * rows:(rank + 1) * rows])
             ready[b].record(copy_stream)
 
+    bw = h2d_gbs(host_gt[0][r0:r1], dev_gt[0][r0:r1]) if r1 > r0 else 0.0
     st.prime_rgb(cams[0])
     dist.barrier()
     t0 = time.perf_counter()
@@ -859,7 +885,7 @@ def e2e_sharded(B, dist, st, gts, cams, e2e_steps, dev):
     dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
     return {"value": round(1.0 / float(e2e_s.item()), 3), "unit": "iters/s",
             "h2d_bytes_per_step": int(gts[0].numel() * 4), "d2h_bytes_per_step": 24 * ws, "steps": e2e_steps,
-            "h2d_per_rank_bytes": int((r1 - r0) * gts[0][0].numel() * 4),
+            "h2d_per_rank_bytes": int((r1 - r0) * gts[0][0].numel() * 4), "h2d_gbs_measured": bw,
             "path": (("msplat_route_*" if st.route is not None else "msplat_shard_*") +
                      " C ABI + NCCL per rank: each rank copies 1/N of the target's rows host->device "
                      "from pinned memory and the row blocks are all-gathered over NVLink, for the next "
