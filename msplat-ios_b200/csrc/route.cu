@@ -9,9 +9,10 @@
 //      difference array) and two histograms of its tile rectangles' first and
 //      last rows;
 //   2. the summaries of all ranks are gathered (the caller's all-gather) and
-//      every rank computes the same work-balanced bands (band_cut over the
-//      summed counts) and, from the histograms, how many Gaussians every rank
-//      sends to every rank, so the all-to-all needs no count exchange;
+//      every rank computes the same work-balanced bands (the least maximum
+//      band cost over the summed counts, halo rows included) and, from the
+//      histograms, how many Gaussians every rank sends to every rank, so the
+//      all-to-all needs no count exchange;
 //   3. each projected Gaussian goes, as a 128-byte payload (raster record,
 //      cull record, tile rectangle, depth, global id), to every rank whose
 //      band plus its one-tile-row halo its rectangle meets, in increasing id
@@ -133,33 +134,95 @@ __global__ void __launch_bounds__(256) k_route_row_work(const int32_t* __restric
     if (lane == 0) row_work[y] = work;
 }
 
-// Bands of every rank (band_cut over the row work, one thread per cut; every
-// rank computes identical bands) and the items from rank r to rank q:
-// r's routable Gaussians whose rectangle rows [y0, y1) meet q's band with its
-// one-row halo [lo, hi), i.e. all of them but those with y0 >= hi and those
-// with y1 <= lo (disjoint when y0 < y1 and lo < hi); 0 for an empty band.
+// Band cost in tenths of a row-work unit: the band's rows, plus 0.4 of each
+// halo row it renders but does not own (forward and binning, about 0.4 of a
+// row's step work). Integer arithmetic, so every rank (and a CPU restatement)
+// computes identical cuts. P10[y] = 10 x the row work of rows [0, y);
+// H[y] = 4 x the row work of row y.
+constexpr int64_t kRowTenths = 10, kHaloTenths = 4;
+
+// Greedy cover of rows [0, ty) by at most `world` bands of cost <= L, each
+// band as long as possible: the largest end b1 whose rows alone fit (binary
+// search over the increasing P10), then back while the halo rows push the
+// cost over L. cuts[1..] receive the band ends (when given). Returns whether
+// the rows are covered.
+__device__ bool greedy_bands(const int64_t* P10, const int64_t* H, int ty, int world, int64_t L, int* cuts) {
+    int b0 = 0;
+    for (int r = 0; r < world; ++r) {
+        if (b0 < ty) {
+            int lo = b0, hi = ty;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (P10[mid] - P10[b0] <= L) lo = mid;
+                else hi = mid - 1;
+            }
+            const int64_t left = b0 > 0 ? H[b0 - 1] : 0;
+            int b1 = lo;
+            while (b1 > b0 && P10[b1] - P10[b0] + left + (b1 < ty ? H[b1] : 0) > L) --b1;
+            if (b1 == b0) return false;
+            b0 = b1;
+        }
+        if (cuts) cuts[r + 1] = b0;
+    }
+    return b0 == ty;
+}
+
+// Bands of every rank: the least L (to within one unit) for which the greedy
+// cover succeeds, found by kCutThreads-way search rounds (thread k tests
+// lo + (hi - lo) (k + 1) / kCutThreads), then the greedy cover at that L.
+// Then the items from rank r to rank q: r's routable Gaussians whose
+// rectangle rows [y0, y1) meet q's band with its one-row halo [lo, hi),
+// i.e. all of them but those with y0 >= hi and those with y1 <= lo (disjoint
+// when y0 < y1 and lo < hi); 0 for an empty band.
 constexpr int kCutThreads = 256;
 __global__ void __launch_bounds__(kCutThreads) k_route_cuts(const int32_t* __restrict__ summaries, int64_t len,
                                                             int tx, int ty, int world,
                                                             const int64_t* __restrict__ row_work,
                                                             int32_t* __restrict__ bands, int64_t* __restrict__ matrix) {
-    extern __shared__ int64_t swork[];
+    extern __shared__ int64_t sdyn[];
+    int64_t* H = sdyn;            // [ty]
+    int64_t* P10 = sdyn + ty;     // [ty + 1]
     __shared__ int sb[kMaxPeerRanks + 1];
-    __shared__ double stotal;
-    for (int y = threadIdx.x; y < ty; y += blockDim.x) swork[y] = row_work[y];
+    __shared__ int64_t s_lo, s_hi;
+    __shared__ int s_kmin;
+    for (int y = threadIdx.x; y < ty; y += blockDim.x) H[y] = kHaloTenths * row_work[y];
     __syncthreads();
     if (threadIdx.x == 0) {
-        double total = 0;
-        for (int y = 0; y < ty; ++y) total += (double)swork[y];
-        stotal = total;
+        int64_t run = 0, wmax = 0;
+        P10[0] = 0;
+        for (int y = 0; y < ty; ++y) {
+            const int64_t wy = H[y] / kHaloTenths;
+            run += wy;
+            P10[y + 1] = kRowTenths * run;
+            wmax = max(wmax, wy);
+        }
+        s_lo = 0;
+        s_hi = kRowTenths * run + 2 * kHaloTenths * wmax;  // one band over every row fits
     }
     __syncthreads();
-    if (threadIdx.x <= world) {
-        const int c = band_cut(swork, ty, stotal, threadIdx.x, world);
-        sb[threadIdx.x] = c;
-        bands[threadIdx.x] = c;
+    for (int round = 0; round < 12; ++round) {
+        const int64_t lo = s_lo, hi = s_hi;
+        if (hi - lo <= 1) break;
+        if (threadIdx.x == 0) s_kmin = kCutThreads - 1;
+        __syncthreads();
+        const int64_t L = lo + ((hi - lo) * (threadIdx.x + 1)) / kCutThreads;
+        if (greedy_bands(P10, H, ty, world, L, nullptr)) atomicMin(&s_kmin, (int)threadIdx.x);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const int k = s_kmin;
+            s_hi = lo + ((hi - lo) * (k + 1)) / kCutThreads;
+            s_lo = k > 0 ? lo + ((hi - lo) * k) / kCutThreads : lo;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        sb[0] = 0;
+        if (!greedy_bands(P10, H, ty, world, s_hi, sb))
+            for (int r = 1; r <= world; ++r) sb[r] = ty;  // not reached: s_hi stays feasible
+        sb[world] = ty;
     }
     __syncthreads();
+    if (threadIdx.x <= world) bands[threadIdx.x] = sb[threadIdx.x];
     for (int k = threadIdx.x; k < world * world; k += blockDim.x) {
         const int r = k / world, q = k % world;
         const int b0 = sb[q], b1 = sb[q + 1];
@@ -426,7 +489,7 @@ void launch_route_plan(const int32_t* summaries, int tx, int ty, int world, int6
     const int64_t len = route_summary_len(tx, ty);
     note_launches(nblocks > 0 ? 4 : 3);
     k_route_row_work<<<(ty + 7) / 8, 256, 0, s>>>(summaries, len, tx, ty, world, row_work);
-    const size_t smem = (size_t)(ty > 0 ? ty : 1) * sizeof(int64_t);
+    const size_t smem = (size_t)(2 * ty + 1) * sizeof(int64_t);
     if (smem > 48 * 1024)
         (void)cudaFuncSetAttribute(k_route_cuts, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k_route_cuts<<<1, kCutThreads, smem, s>>>(summaries, len, tx, ty, world, row_work, bands, matrix);

@@ -3,8 +3,9 @@ C ABI.
 
 A slice's summary must hold the oracle's uncapped tile counts of the slice
 (summed over slices: the oracle's) and the histograms of its tile
-rectangles' first and last rows; the bands must follow the half-row rule
-over the row work (min(count, 2048) + 430 per tile) and the send and
+rectangles' first and last rows; the bands must be the least-maximum-cost
+cover over the row work (min(count, 2048) + 430 per tile; halo rows at 0.4)
+and the send and
 receive counts the count matrix restated from the histograms; every
 projected Gaussian must be packed for exactly the ranks whose band plus a
 one-tile-row halo its rectangle meets, in increasing id order. A routed step of `world` ranks,
@@ -18,7 +19,7 @@ import pytest
 
 from _cases import Case
 from test_binning_chunks import _tile_rects
-from test_routed_gloo import _band_cuts, route_matrix
+from test_routed_gloo import route_band_cuts, route_matrix
 
 pytestmark = pytest.mark.gpu
 
@@ -75,7 +76,7 @@ def test_route_summaries_bands_and_payloads(name):
     sm = summaries.cpu().numpy().astype(np.int64)
     np.testing.assert_array_equal(sm[:, :tiles].sum(0), bins["raw_counts"])
     work = np.minimum(bins["raw_counts"].reshape(ty, tx).astype(np.int64), CAP).sum(1) + ROW_WORK_PER_TILE * tx
-    want_bands = _band_cuts(work, world)
+    want_bands = route_band_cuts(work, world)
     matrix = route_matrix(sm[:, tiles:tiles + ty + 1], sm[:, tiles + ty + 1:], want_bands, ty)
     for r, (a, b) in enumerate(slices):
         B.route_project(g, cam, case.degree, a, b, torch.zeros(L, dtype=torch.int32, device="cuda"))

@@ -9,9 +9,10 @@ Gaussian to the ranks whose band (with a one-tile-row halo) its rectangle
 meets, rasterises each band over what it received, and returns the gradient
 records to the owners, which apply the projection VJP and Adam to their
 slice. The stand-in calls restate the device side (route.cu): row work =
-sum over the row's tiles of min(count, 2048) + 430, bands by the half-row
-rule, the count matrix from the histograms (checked against each slice's
-own destinations), destinations by the halo rule, packing grouped by
+sum over the row's tiles of min(count, 2048) + 430, bands as the
+least-maximum-cost cover with the halo rows costed (route_band_cuts), the
+count matrix from the histograms (checked against each slice's own
+destinations), destinations by the halo rule, packing grouped by
 destination in increasing id. The slices put together must equal one single-process oracle
 step, every Gaussian that has a gradient in a band must have reached that
 band, and nothing may reach a band it does not touch.
@@ -35,19 +36,49 @@ def _free_port():
     return port
 
 
-def _band_cuts(work, world):
-    """Restates band_cut (common.cuh): rows are added to a band while less
-    than half of the next row's work overshoots the band's target."""
-    total = float(np.sum(work, dtype=np.float64))
-    cuts = [0]
-    for r in range(1, world):
-        target = total * r / world
-        run, y = 0.0, 0
-        while y < len(work) and run + float(work[y]) / 2 < target:
-            run += float(work[y])
-            y += 1
-        cuts.append(y)
-    cuts.append(len(work))
+ROW_TENTHS, HALO_TENTHS = 10, 4
+
+
+def route_band_cuts(work, world):
+    """Restates k_route_cuts (route.cu): band cost in tenths of a row-work
+    unit = 10 x the band's rows + 4 x each halo row it renders but does not
+    own; the least L (to within one) for which the greedy cover (each band
+    as long as possible, at most `world` bands) succeeds, found by 256-way
+    search rounds, then the greedy cover at that L. Integer arithmetic."""
+    w = [int(x) for x in work]
+    ty = len(w)
+    P = [0]
+    for x in w:
+        P.append(P[-1] + x)
+
+    def cost(b0, b1):
+        return ROW_TENTHS * (P[b1] - P[b0]) + (HALO_TENTHS * w[b0 - 1] if b0 > 0 else 0) + \
+            (HALO_TENTHS * w[b1] if b1 < ty else 0)
+
+    def greedy(L):
+        cuts, b0 = [0], 0
+        for _ in range(world):
+            if b0 < ty:
+                best, b1 = -1, b0 + 1
+                while b1 <= ty and ROW_TENTHS * (P[b1] - P[b0]) <= L:
+                    if cost(b0, b1) <= L:
+                        best = b1
+                    b1 += 1
+                if best < 0:
+                    return None
+                b0 = best
+            cuts.append(b0)
+        return cuts if b0 == ty else None
+
+    lo, hi = 0, ROW_TENTHS * P[ty] + 2 * HALO_TENTHS * max(w)
+    for _ in range(12):
+        if hi - lo <= 1:
+            break
+        cand = [lo + ((hi - lo) * (k + 1)) // 256 for k in range(256)]
+        k = next(k for k in range(256) if greedy(cand[k]) is not None)
+        lo, hi = (cand[k - 1] if k > 0 else lo), cand[k]
+    cuts = greedy(hi)
+    cuts[world] = ty
     return cuts
 
 
@@ -105,7 +136,7 @@ class _OracleRouteCalls:
         assert sm.shape == (world, tiles + 2 * (self.ty + 1))
         c = sm[:, :tiles].sum(0).reshape(self.ty, self.tx)
         work = np.minimum(c, CAP).sum(1) + ROW_WORK_PER_TILE * self.tx
-        self.bands = _band_cuts(work, world)
+        self.bands = route_band_cuts(work, world)
         matrix = route_matrix(sm[:, tiles:tiles + self.ty + 1], sm[:, tiles + self.ty + 1:], self.bands, self.ty)
         self.dest = []
         for q in range(world):
@@ -203,6 +234,32 @@ def _rank_main(rank, ws, port, out_path):
     np.savez(out_path + f".{rank}.npz", *[p[sl] for p in params], parts=parts.numpy(), bands=np.array(bands),
              g_begin=plan.g_begin, g_end=plan.g_end, row0=plan.row0, row1=plan.row1)
     dist.destroy_process_group()
+
+
+def _band_cost(w, b0, b1):
+    ty = len(w)
+    if b1 <= b0:
+        return 0
+    return ROW_TENTHS * sum(w[b0:b1]) + (HALO_TENTHS * w[b0 - 1] if b0 > 0 else 0) + \
+        (HALO_TENTHS * w[b1] if b1 < ty else 0)
+
+
+def test_route_band_cuts_minimise_the_largest_band_cost():
+    """The cuts cover every row with ordered bands and reach the least
+    possible largest band cost (brute force over every cut placement)."""
+    import itertools
+    import random
+    rng = random.Random(1)
+    for _ in range(300):
+        ty, world = rng.randint(1, 9), rng.randint(1, 4)
+        w = [rng.randint(1, 1000) for _ in range(ty)]
+        c = route_band_cuts(w, world)
+        assert len(c) == world + 1 and c[0] == 0 and c[-1] == ty
+        assert all(c[i] <= c[i + 1] for i in range(world))
+        got = max(_band_cost(w, c[i], c[i + 1]) for i in range(world))
+        best = min(max(_band_cost(w, cc[i], cc[i + 1]) for i in range(world))
+                   for cc in ([0, *m, ty] for m in itertools.combinations_with_replacement(range(ty + 1), world - 1)))
+        assert got == best, (w, world, c, got, best)
 
 
 def _check(ws, tmp_path):
