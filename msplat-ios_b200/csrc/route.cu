@@ -16,15 +16,18 @@
 //   3. each projected Gaussian goes, as a 128-byte payload (raster record,
 //      cull record, tile rectangle, depth, global id), to every rank whose
 //      band plus its one-tile-row halo its rectangle meets, in increasing id
-//      order per destination (the caller's all-to-all);
+//      order per destination: packed for the caller's all-to-all, or stored
+//      by the pack kernel straight into the destination GPU's inbox (CUDA
+//      IPC mapping, NVLink stores);
 //   4. a rank bins, sorts and rasterises its band over what it received;
 //      the received Gaussians are in increasing global id order (sources in
 //      rank order, each in id order), so sorting by (depth, local index)
 //      gives the single-GPU order and the overfull-tile policy keeps the
 //      same 2048 ids;
 //   5. the band's per-Gaussian raster-gradient records go back to their
-//      owners (the reverse all-to-all), which add them up, run the
-//      projection VJP and Adam on their slice. Parameters are never gathered.
+//      owners (the reverse all-to-all, or peer stores into the owner's
+//      return box), which add them up, run the projection VJP and Adam on
+//      their slice. Parameters are never gathered.
 #include "common.cuh"
 #include "kernels.cuh"
 
