@@ -217,8 +217,10 @@ def compute_roofline(per_stage_ms, counters, sm_mhz):
     """The rasterisers against the SM issue peak (4 warp instructions per
     clock per SM). counters: msplat raster_counters [forward blended pairs,
     forward visits, backward visits, backward blended pairs]; each (warp,
-    surfel) visit evaluates 32 pixels. Instructions per visit come from the
-    committed ncu capture (profiles/raster_issue.json) when present."""
+    surfel) visit evaluates 32 pixels; the counts come from one untimed step
+    right after the timed region (the timed steps run without counting).
+    Instructions per visit come from the committed ncu capture
+    (profiles/raster_issue.json) when present."""
     ipv = {}
     try:
         ipv = json.load(open(os.path.join(REPO, "profiles", "raster_issue.json"))).get("instructions_per_visit", {})
@@ -548,6 +550,14 @@ def timed_run(B, dist, st, steps, warmup, ws, dev, local, collect_phases):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     per_stage = {k: (v[0] / max(v[1], 1)) for k, v in stage.items()}
+    # the rasteriser work counters are compiled out of the timed steps; one
+    # more (untimed) step counts the visits and blended pairs for the compute
+    # roofline (last_tensor("raster_counters"))
+    B.set_raster_counters(True)
+    st.step(warmup + steps)
+    st.finish()
+    torch.cuda.synchronize()
+    B.set_raster_counters(False)
     return ms, per_stage, launches, clk
 
 

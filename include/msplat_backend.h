@@ -427,6 +427,12 @@ uint32_t msplat_last_status_flags(void);
  * samples per stage, and returns the number of stages (or -1 on error). */
 int msplat_set_stage_timing(int32_t enable);
 int32_t msplat_stage_times(double* total_ms, int64_t* counts, int32_t max_stages);
+/* Rasteriser work counters (off by default: the kernels are then launched
+ * without the per-visit counting). While enabled, every forward/backward pair
+ * leaves in msplat_last_tensor("raster_counters") (int64 [4]): forward
+ * blended (pixel, surfel) pairs, forward (warp, surfel) visits past the cull,
+ * backward visits, backward blended pairs. */
+int msplat_set_raster_counters(int32_t enable);
 const char* msplat_stage_name(int32_t i);
 /* Kernel launches issued by this library since load (for launch accounting). */
 int64_t msplat_launch_count(void);

@@ -154,6 +154,9 @@ const char* kStageNames[kNumStages] = {"project_forward", "tile_counts", "emit_k
                                        // start, incl. the caller's collectives), then the unpack
                                        "route_exchange", "route_unpack"};
 bool g_timing = false;
+// rasteriser work counters (msplat_set_raster_counters): off, the kernels are
+// built without the per-visit counting
+bool g_counting = false;
 double g_stage_ms[kNumStages] = {};
 int64_t g_stage_n[kNumStages] = {};
 
@@ -398,7 +401,7 @@ void stage_forward(Workspace& w, const MsplatGaussians* g, const CameraDev& cam,
     ra.blend_mask = w.blend_mask.as<uint8_t>();
     w.counters.ensure(4 * sizeof(unsigned long long));
     CK(cudaMemsetAsync(w.counters.p, 0, 4 * sizeof(unsigned long long), s));
-    ra.counters = w.counters.as<unsigned long long>();
+    ra.counters = g_counting ? w.counters.as<unsigned long long>() : nullptr;
     ra.aux_outputs = aux_out ? 1 : 0;
     mark(w, kStRasterFwd, s);
     launch_rasterize_forward(ra, s);
@@ -446,7 +449,7 @@ void stage_raster_backward(Workspace& w, const CameraDev& cam, const float bg[3]
     ba.dL_dout_distortion = ldist * (1.0f / (float)((double)cam.height * (double)cam.width * 3.0)) * 3.0f;  // lambda_dist / HW
     ba.raster_grads = raster_grads;
     ba.blend_mask = w.blend_mask.as<uint8_t>();
-    ba.counters = w.counters.as<unsigned long long>();
+    ba.counters = g_counting ? w.counters.as<unsigned long long>() : nullptr;
     mark(w, kStRasterBwd, s);
     launch_rasterize_backward(ba, s);
 }
@@ -1232,6 +1235,10 @@ int msplat_set_stage_timing(int32_t enable) {
             g_stage_n[k] = 0;
         }
     });
+}
+
+int msplat_set_raster_counters(int32_t enable) {
+    return guarded([&] { g_counting = enable != 0; });
 }
 
 int32_t msplat_stage_times(double* total_ms, int64_t* counts, int32_t max_stages) {

@@ -129,7 +129,8 @@ __device__ __forceinline__ void flush_blend_flags(uint8_t* mask, const uint2* sf
 // AUXOUT: every output of the reference's forward; otherwise only what a
 // colour-only training step consumes (the image, the final transmittance and
 // the last contributor), skipping depth, normal, median and distortion.
-template <bool AUXOUT>
+// COUNT: accumulate the work counters (a.counters); compiled out otherwise.
+template <bool AUXOUT, bool COUNT>
 __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
     __shared__ float4 srec[kRecordF4][kThreads];
     __shared__ float4 scull[kCullF4][kThreads];
@@ -199,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
                 const float4 q1 = srec[1][s], q2 = srec[2][s];
                 const bool cand = (!done) & pair_stage1(px, py, srec[0][s], q1, q2, srec[4][s].z, e);
                 if (!__any_sync(full, cand)) continue;
-                ++n_visits;
+                if (COUNT) ++n_visits;
                 if (!(pair_stage2<true>(q1, q2, e) & cand)) continue;
                 contributor = base + s;
                 const float next_T = fmul(T, fsub(1.0f, e.alpha));
@@ -233,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
                 }
                 T = next_T;
                 last_c = contributor;
-                ++n_blend;
+                if (COUNT) ++n_blend;
                 reinterpret_cast<uint8_t*>(&sflag[s])[warp] = 1;
             }
             if (__all_sync(full, done)) break;
@@ -243,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
         __syncthreads();
         flush_blend_flags(a.blend_mask, sflag, flush_b0, range.y);
     }
-    if (a.counters) {
+    if (COUNT && a.counters) {
         const unsigned blended = __reduce_add_sync(full, n_blend);
         if (lane == 0) {
             atomicAdd(a.counters + 0, (unsigned long long)blended);
@@ -283,7 +284,8 @@ constexpr size_t bwd_dynamic_smem() {
            sizeof(float) * (kThreads / 32) * bwd_values<AUX>() * 36;
 }
 
-template <bool AUX>
+// COUNT: accumulate the work counters (a.counters); compiled out otherwise.
+template <bool AUX, bool COUNT>
 __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
     extern __shared__ __align__(16) unsigned char dsm[];
     constexpr int NV = bwd_values<AUX>();
@@ -388,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
                 const int s = c + __ffs(bits) - 1;
                 bits &= bits - 1;
                 const int rel = srel[s];
-                ++n_visits;
+                if (COUNT) ++n_visits;
                 float g[16];
 #pragma unroll
                 for (int k = 0; k < 16; ++k) g[k] = 0.f;
@@ -396,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
                 const float4 r0 = srec[0][s], r1 = srec[1][s], r2 = srec[2][s];
                 pair_stage1(px, py, r0, r1, r2, 0.f, e);
                 if ((rel < last_c) & pair_stage2<false>(r1, r2, e)) {
-                    ++n_blend;
+                    if (COUNT) ++n_blend;
                     const float4 r3 = srec[3][s], r4 = srec[4][s];
                     const float alpha = e.alpha, G = e.G, opa = r2.w;
                     const float r1ma = __fdividef(1.0f, 1.0f - alpha);
@@ -548,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
             }
         }
     }
-    if (a.counters) {
+    if (COUNT && a.counters) {
         const unsigned blended = __reduce_add_sync(full, n_blend);
         if (lane == 0) {
             atomicAdd(a.counters + 2, (unsigned long long)n_visits);
@@ -559,14 +561,29 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
 
 }  // namespace
 
+namespace {
+template <bool AUXOUT, bool COUNT>
+void fwd_launch(const RasterFwdArgs& a, int rows, cudaStream_t s) {
+    k_raster_fwd<AUXOUT, COUNT><<<dim3(a.tiles_x, rows), kThreads, 0, s>>>(a);
+}
+template <bool AUX, bool COUNT>
+void bwd_launch(const RasterBwdArgs& a, int rows, cudaStream_t s) {
+    constexpr size_t smem = bwd_dynamic_smem<AUX>();
+    cudaFuncSetAttribute(k_raster_bwd<AUX, COUNT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(k_raster_bwd<AUX, COUNT>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    k_raster_bwd<AUX, COUNT><<<dim3(a.tiles_x, rows), kThreads, smem, s>>>(a);
+}
+}  // namespace
+
 void launch_rasterize_forward(const RasterFwdArgs& a, cudaStream_t s) {
     const int rows = a.tile_row_end - a.tile_row_begin;
     if (rows <= 0 || a.tiles_x <= 0) return;
     note_launches(1);
+    const bool count = a.counters != nullptr;
     if (a.aux_outputs)
-        k_raster_fwd<true><<<dim3(a.tiles_x, rows), kThreads, 0, s>>>(a);
+        count ? fwd_launch<true, true>(a, rows, s) : fwd_launch<true, false>(a, rows, s);
     else
-        k_raster_fwd<false><<<dim3(a.tiles_x, rows), kThreads, 0, s>>>(a);
+        count ? fwd_launch<false, true>(a, rows, s) : fwd_launch<false, false>(a, rows, s);
 }
 
 void launch_rasterize_backward(const RasterBwdArgs& a, cudaStream_t s) {
@@ -575,17 +592,11 @@ void launch_rasterize_backward(const RasterBwdArgs& a, cudaStream_t s) {
     const bool aux = a.dL_dout_depth || a.dL_dout_alpha || a.dL_dout_normal || a.dL_dout_median_depth ||
                      a.dL_dout_distortion != 0.0f;
     note_launches(1);
-    if (aux) {
-        constexpr size_t smem = bwd_dynamic_smem<true>();
-        cudaFuncSetAttribute(k_raster_bwd<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(k_raster_bwd<true>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-        k_raster_bwd<true><<<dim3(a.tiles_x, rows), kThreads, smem, s>>>(a);
-    } else {
-        constexpr size_t smem = bwd_dynamic_smem<false>();
-        cudaFuncSetAttribute(k_raster_bwd<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(k_raster_bwd<false>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-        k_raster_bwd<false><<<dim3(a.tiles_x, rows), kThreads, smem, s>>>(a);
-    }
+    const bool count = a.counters != nullptr;
+    if (aux)
+        count ? bwd_launch<true, true>(a, rows, s) : bwd_launch<true, false>(a, rows, s);
+    else
+        count ? bwd_launch<false, true>(a, rows, s) : bwd_launch<false, false>(a, rows, s);
 }
 
 }  // namespace msplat

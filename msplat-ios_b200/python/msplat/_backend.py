@@ -138,6 +138,8 @@ def load():
     L.msplat_launch_count.restype = i64
     L.msplat_set_stage_timing.argtypes = [i32]
     L.msplat_set_stage_timing.restype = C.c_int
+    L.msplat_set_raster_counters.argtypes = [i32]
+    L.msplat_set_raster_counters.restype = C.c_int
     L.msplat_stage_times.argtypes = [C.POINTER(C.c_double), C.POINTER(C.c_int64), i32]
     L.msplat_stage_times.restype = i32
     L.msplat_stage_name.argtypes = [i32]
@@ -459,6 +461,11 @@ def launch_count() -> int:
 
 def set_stage_timing(enable: bool):
     _check(load().msplat_set_stage_timing(1 if enable else 0))
+
+
+def set_raster_counters(enable: bool):
+    """Rasteriser work counters (last_tensor("raster_counters")); off by default."""
+    _check(load().msplat_set_raster_counters(1 if enable else 0))
 
 
 def stage_times() -> dict:

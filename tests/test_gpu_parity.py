@@ -257,3 +257,29 @@ def test_fused_step_light_forward_matches_full_forward():
     for k in ("out_depth", "out_distortion", "final_Ts", "final_idx"):
         with pytest.raises(B.MsplatError):
             B.last_tensor(k)
+
+
+def test_raster_counters_switch():
+    """msplat_set_raster_counters: off (the default) leaves the counters at
+    zero; on, a step counts forward visits and blended pairs (at most 32 per
+    visit), and the backward visits at most the forward's visits and replays
+    about the same blended pairs (its replay uses the hardware exponential)."""
+    case = Case("sh3_small")
+    B = _B()
+    g = _device_scene(case)
+    cam = B.camera_from_oracle(case.ocam)
+    gt = torch.as_tensor(case.gt).cuda()
+    adam = B.AdamState(g)
+    B.train_step_fused(g, cam, case.degree, case.bg, gt, 0.8, 0.0, 0.2, adam)
+    torch.cuda.synchronize()
+    assert not _np(B.last_tensor("raster_counters")).any()
+    B.set_raster_counters(True)
+    try:
+        B.train_step_fused(g, cam, case.degree, case.bg, gt, 0.8, 0.0, 0.2, adam)
+        torch.cuda.synchronize()
+        fb, fv, bv, bb = (int(x) for x in _np(B.last_tensor("raster_counters")))
+    finally:
+        B.set_raster_counters(False)
+    assert fv > 0 and 0 < fb <= 32 * fv
+    assert 0 < bv <= fv and 0 < bb <= 32 * bv
+    assert abs(bb - fb) <= 1e-3 * fb
