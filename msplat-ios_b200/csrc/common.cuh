@@ -82,6 +82,16 @@ __device__ inline int band_cut(const int64_t* work, int ty, double total, int r,
     return y;
 }
 
+// 16-byte asynchronous copy global -> shared (cp.async, cached in L1 and L2:
+// the CTAs of neighbouring tiles on one SM share many records) and the wait
+// for every copy the thread issued (commit + wait for the group). Both
+// addresses 16-byte aligned.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
 __device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
 __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
 __device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }

@@ -13,7 +13,8 @@
 // 8x8 groups per tile, each re-reading the tile list); the tile's surfels are
 // streamed in batches of 256: ids are read coalesced, the 80-byte per-Gaussian
 // records (written once by the projection) are gathered into shared memory
-// structure-of-arrays. Each warp owns an 8x4 pixel block: it tests 32
+// structure-of-arrays with cp.async (16-byte asynchronous copies, waited on
+// before the batch barrier). Each warp owns an 8x4 pixel block: it tests 32
 // surfels at a time (one per lane) against its block with the exact
 // screen-space conic of rho3d <= rmax and the 2-D filter disc (32-byte cull
 // records from the projection), and walks only the surfels that can reach
@@ -170,11 +171,12 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_fwd(RasterFwdArgs a) {
             const float4* r = a.records + (size_t)g * kRecordF4;
             const float4* cr = a.cull + (size_t)g * kCullF4;
 #pragma unroll
-            for (int k = 0; k < kRecordF4; ++k) srec[k][threadIdx.x] = __ldg(r + k);
+            for (int k = 0; k < kRecordF4; ++k) cp_async16(&srec[k][threadIdx.x], r + k);
 #pragma unroll
-            for (int k = 0; k < kCullF4; ++k) scull[k][threadIdx.x] = __ldg(cr + k);
+            for (int k = 0; k < kCullF4; ++k) cp_async16(&scull[k][threadIdx.x], cr + k);
         }
         sflag[threadIdx.x] = make_uint2(0u, 0u);
+        cp_async_wait_all();
         __syncthreads();
         flush_b0 = b0;
         if (__all_sync(full, done)) continue;
@@ -377,12 +379,13 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
             smask[pos] = (uint8_t)m;
             const float4* r = a.records + (size_t)g * kRecordF4;
 #pragma unroll
-            for (int k = 0; k < kRecordF4; ++k) srec[k][pos] = __ldg(r + k);
+            for (int k = 0; k < kRecordF4; ++k) cp_async16(&srec[k][pos], r + k);
         }
         if ((int)threadIdx.x < total) {
 #pragma unroll
             for (int k = 0; k < kGradStride; ++k) sacc[threadIdx.x][k] = 0.f;
         }
+        cp_async_wait_all();
         __syncthreads();
         for (int c = 0; c < total; c += 32) {
             unsigned bits = __ballot_sync(full, c + lane < total && ((smask[c + lane] >> warp) & 1u));
