@@ -36,16 +36,29 @@ __device__ __forceinline__ ParamPtrs param_ptrs(const ProjFwdArgs& a, int i) {
 
 // SH colour of Gaussian i for the camera position: raw colour (reference
 // output) and the clamped colour max(raw + 0.5, 0) the rasteriser blends.
+// rest_smem: the Gaussian's 3K rest coefficients already in shared memory
+// (null: read them from global memory).
 __device__ __forceinline__ void gaussian_color(const ProjFwdArgs& a, const ParamPtrs& pp, int i, V3 p, float col[3],
-                                               float rgb[3]) {
+                                               float rgb[3], const float* rest_smem = nullptr) {
     const CameraDev& cam = a.cam;
     V3 v = v3(p.x - cam.cam_pos[0], p.y - cam.cam_pos[1], p.z - cam.cam_pos[2]);
     float inv = 1.0f / sqrtf(dot3(v, v));
     V3 dir = scale3(v, inv);
     const int K = a.rest_bases;
-    const float* rest = pp.f_rest + (size_t)K * 3 * i;
-    sh_to_color(a.degrees_to_use, dir, pp.f_dc + 3 * i, [&](int k) { return __ldg(rest + k); }, col);
+    if (rest_smem) {
+        sh_to_color(a.degrees_to_use, dir, pp.f_dc + 3 * i, [&](int k) { return rest_smem[k]; }, col);
+    } else {
+        const float* rest = pp.f_rest + (size_t)K * 3 * i;
+        sh_to_color(a.degrees_to_use, dir, pp.f_dc + 3 * i, [&](int k) { return __ldg(rest + k); }, col);
+    }
     for (int c = 0; c < 3; ++c) rgb[c] = smax(col[c] + 0.5f, 0.0f);
+}
+
+// Whether a launch stages the rest coefficients through shared memory: the
+// full projection (pass 0) with local coefficients on a 16-byte boundary.
+__host__ __device__ __forceinline__ bool stage_rest(const ProjFwdArgs& a) {
+    return a.pass == 0 && a.peer_world <= 1 && a.rest_bases > 0 &&
+           (reinterpret_cast<uintptr_t>(a.f_rest) & 15) == 0;
 }
 
 // Cull record of one surfel (layout in common.cuh). With k = x Tw - Tu and
@@ -95,6 +108,24 @@ __device__ void cull_record(V3 tu, V3 tv, V3 tw, float rmax, float4* out) {
 }
 
 __global__ void __launch_bounds__(256, 4) k_project_forward(ProjFwdArgs a) {
+    // pass 0: each full warp copies its 32 Gaussians' rest coefficients (one
+    // contiguous run of 32 x 3K floats, 16-byte aligned) into shared memory
+    // with coalesced 16-byte cp.async copies before any lane leaves; lane l's
+    // coefficients then sit at an odd stride (3K) of floats
+    extern __shared__ float4 srest4[];
+    const float* rest_smem = nullptr;
+    {
+        const int warp_first = blockIdx.x * blockDim.x + (threadIdx.x & ~31);
+        const int K3 = 3 * a.rest_bases;
+        if (stage_rest(a) && warp_first + 32 <= a.n) {
+            float4* dst = srest4 + (size_t)(threadIdx.x >> 5) * (8 * K3);  // 32 x 3K floats = 8 x 3K float4
+            const float4* src = reinterpret_cast<const float4*>(a.f_rest + (size_t)warp_first * K3);
+            for (int k = threadIdx.x & 31; k < 8 * K3; k += 32) cp_async16(dst + k, src + k);
+            cp_async_wait_all();
+            __syncwarp();
+            rest_smem = reinterpret_cast<const float*>(dst) + (threadIdx.x & 31) * K3;
+        }
+    }
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= a.n) return;
     const CameraDev& cam = a.cam;
@@ -192,7 +223,7 @@ __global__ void __launch_bounds__(256, 4) k_project_forward(ProjFwdArgs a) {
     atomicAdd(&diff[y1 * dw + x1], 1);
 
     float col[3] = {0.f, 0.f, 0.f}, rgb[3] = {0.f, 0.f, 0.f};
-    if (a.pass == 0) gaussian_color(a, pp, i, p, col, rgb);
+    if (a.pass == 0) gaussian_color(a, pp, i, p, col, rgb, rest_smem);
     float opac = 1.f / (1.f + det_exp(-opac_raw));
     V3 nrm = R[2];
     rec[0] = make_float4(T0.x, T0.y, T0.z, T1.x);
@@ -288,8 +319,12 @@ void launch_project_forward(const ProjFwdArgs& a, cudaStream_t s) {
     note_launches(1);
     if (a.pass == 2 && a.peer_world > 1)
         k_project_color_peers<<<(a.n + 255) / 256, 256, 0, s>>>(a);
-    else
-        k_project_forward<<<(a.n + 255) / 256, 256, 0, s>>>(a);
+    else {
+        const size_t smem = stage_rest(a) ? (size_t)256 * 3 * a.rest_bases * sizeof(float) : 0;
+        if (smem > 48 * 1024)
+            (void)cudaFuncSetAttribute(k_project_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        k_project_forward<<<(a.n + 255) / 256, 256, smem, s>>>(a);
+    }
 }
 
 }  // namespace msplat
