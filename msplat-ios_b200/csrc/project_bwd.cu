@@ -17,12 +17,15 @@ constexpr int kBwdThreads = 128;  // Gaussians per CTA
 
 // Coalesced copy of n floats between global and shared memory (float4 when
 // both ends are 16-byte aligned).
+// Copies n floats into shared memory: 16-byte cp.async copies when both
+// pointers are 16-byte aligned (the caller waits with cp_async_wait_all
+// before its barrier, so the copies of several groups are in flight
+// together), plain loads for the rest.
 __device__ __forceinline__ void copy_in(float* dst, const float* __restrict__ src, int n) {
     if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
         const int n4 = n >> 2;
-#pragma unroll 4
         for (int q = threadIdx.x; q < n4; q += blockDim.x)
-            reinterpret_cast<float4*>(dst)[q] = __ldg(reinterpret_cast<const float4*>(src) + q);
+            cp_async16(reinterpret_cast<float4*>(dst) + q, reinterpret_cast<const float4*>(src) + q);
         for (int q = (n4 << 2) + threadIdx.x; q < n; q += blockDim.x) dst[q] = __ldg(src + q);
     } else {
         for (int q = threadIdx.x; q < n; q += blockDim.x) dst[q] = __ldg(src + q);
@@ -163,15 +166,20 @@ __global__ void __launch_bounds__(kBwdThreads, 6) k_project_backward(ProjBwdArgs
     copy_in(sQuat, a.quats + 4 * (size_t)b0, 4 * cnt);
     copy_in(sDc, a.f_dc + 3 * (size_t)b0, 3 * cnt);
     copy_in(sOp, a.opacities + (size_t)b0, cnt);
+    const int t = threadIdx.x;
+    // this Gaussian's raster-gradient record, loaded while the copies run
+    float4 q0 = make_float4(0.f, 0.f, 0.f, 0.f), q1 = q0, q2 = q0, q3 = q0;
+    if (t < cnt) {
+        const float4* gr4 = reinterpret_cast<const float4*>(a.raster_grads + (size_t)(b0 + t) * kGradStride);
+        q0 = __ldg(gr4); q1 = __ldg(gr4 + 1); q2 = __ldg(gr4 + 2); q3 = __ldg(gr4 + 3);
+    }
+    cp_async_wait_all();
     __syncthreads();
 
-    const int t = threadIdx.x;
     if (t < cnt) {
         const int i = b0 + t;
         const CameraDev& cam = a.cam;
         const float* pm = cam.projmat;
-        const float4* gr4 = reinterpret_cast<const float4*>(a.raster_grads + (size_t)i * kGradStride);
-        const float4 q0 = __ldg(gr4), q1 = __ldg(gr4 + 1), q2 = __ldg(gr4 + 2), q3 = __ldg(gr4 + 3);
         const float dT[9] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w, q2.x};
         const float d_opac = q2.y;
         float dC[3] = {q2.z, q2.w, q3.x};
