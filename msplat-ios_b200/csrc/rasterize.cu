@@ -361,6 +361,8 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
         // back-to-front order
         const int rel_t = bend - 1 - (int)threadIdx.x - range.x;
         const uint32_t m = ((int)threadIdx.x < bs) ? a.blend_mask[range.x + rel_t] : 0u;
+        // the id is read with the flags (one round trip less before the copies)
+        const int g_pre = ((int)threadIdx.x < bs) ? a.gaussian_ids[range.x + rel_t] : 0;
         const unsigned bal = __ballot_sync(full, m != 0u);
         if (lane == 0) swarp_cnt[warp] = __popc(bal);
         __syncthreads();
@@ -373,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_raster_bwd(RasterBwdArgs a) {
         }
         if (m != 0u) {
             const int pos = off + __popc(bal & ((1u << lane) - 1u));
-            const int g = a.gaussian_ids[range.x + rel_t];
+            const int g = g_pre;
             sid[pos] = g;
             srel[pos] = rel_t;
             smask[pos] = (uint8_t)m;
