@@ -26,6 +26,12 @@ def case_config(name: str) -> S.SceneConfig:
         # ellipses exercise the rasteriser's conic cull at its boundary
         return S.small_config(12_000, 1, 256, 192, focal=230.0, num_cameras=2,
                               log_scale_mean=math.log(0.02), log_scale_std=1.6)
+    if name == "dense":
+        # large surfels on a small image: the middle tile rows hold 50,000 to
+        # 126,000 Gaussians per tile, far over the 2048 cap (route summaries,
+        # bands and payloads under heavy tiles)
+        return S.small_config(150_000, 1, 48, 96, focal=60.0, num_cameras=1,
+                              log_scale_mean=math.log(0.15), log_scale_std=0.2)
     if name in ("cfg1", "cfg2", "cfg3", "cfg4"):
         return S.CONFIGS[int(name[3:])]
     raise KeyError(name)

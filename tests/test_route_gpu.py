@@ -19,7 +19,7 @@ import pytest
 
 from _cases import Case
 from test_binning_chunks import _tile_rects
-from test_routed_gloo import route_band_cuts, route_matrix
+from test_routed_gloo import route_band_cuts, route_matrix, route_row_work
 
 pytestmark = pytest.mark.gpu
 
@@ -47,7 +47,7 @@ def _slices(n, world):
     return [(min(r * chunk, n), min((r + 1) * chunk, n)) for r in range(world)]
 
 
-@pytest.mark.parametrize("name", ["sh3_small", "overflow", "thin", "sh1_odd"])
+@pytest.mark.parametrize("name", ["sh3_small", "overflow", "thin", "sh1_odd", "dense"])
 def test_route_summaries_bands_and_payloads(name):
     case = Case(name)
     B = _B()
@@ -75,7 +75,7 @@ def test_route_summaries_bands_and_payloads(name):
         np.testing.assert_array_equal(got[tiles + ty + 1:], np.bincount(y1[sel], minlength=ty + 1))
     sm = summaries.cpu().numpy().astype(np.int64)
     np.testing.assert_array_equal(sm[:, :tiles].sum(0), bins["raw_counts"])
-    work = np.minimum(bins["raw_counts"].reshape(ty, tx).astype(np.int64), CAP).sum(1) + ROW_WORK_PER_TILE * tx
+    work = route_row_work(bins["raw_counts"].reshape(ty, tx).astype(np.int64))
     want_bands = route_band_cuts(work, world)
     matrix = route_matrix(sm[:, tiles:tiles + ty + 1], sm[:, tiles + ty + 1:], want_bands, ty)
     for r, (a, b) in enumerate(slices):

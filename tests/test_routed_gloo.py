@@ -9,7 +9,8 @@ Gaussian to the ranks whose band (with a one-tile-row halo) its rectangle
 meets, rasterises each band over what it received, and returns the gradient
 records to the owners, which apply the projection VJP and Adam to their
 slice. The stand-in calls restate the device side (route.cu): row work =
-sum over the row's tiles of min(count, 2048) + 430, bands as the
+sum over the row's tiles of min(count, 2048) + 430 (route_row_work), bands
+as the
 least-maximum-cost cover with the halo rows costed (route_band_cuts), the
 count matrix from the histograms (checked against each slice's own
 destinations), destinations by the halo rule, packing grouped by
@@ -37,6 +38,13 @@ def _free_port():
 
 
 ROW_TENTHS, HALO_TENTHS = 10, 4
+
+
+def route_row_work(counts):
+    """Restates k_route_row_work (route.cu): per tile min(raw, 2048) + 430,
+    summed per tile row. counts: int64 [ty, tx]."""
+    c = np.asarray(counts, np.int64)
+    return (np.minimum(c, CAP) + ROW_WORK_PER_TILE).sum(1)
 
 
 def route_band_cuts(work, world):
@@ -135,7 +143,7 @@ class _OracleRouteCalls:
         sm = summaries.numpy().astype(np.int64)
         assert sm.shape == (world, tiles + 2 * (self.ty + 1))
         c = sm[:, :tiles].sum(0).reshape(self.ty, self.tx)
-        work = np.minimum(c, CAP).sum(1) + ROW_WORK_PER_TILE * self.tx
+        work = route_row_work(c)
         self.bands = route_band_cuts(work, world)
         matrix = route_matrix(sm[:, tiles:tiles + self.ty + 1], sm[:, tiles + self.ty + 1:], self.bands, self.ty)
         self.dest = []
