@@ -4,15 +4,15 @@ C ABI.
 A slice's summary must hold the oracle's uncapped tile counts of the slice
 (summed over slices: the oracle's) and the histograms of its tile
 rectangles' first and last rows; the bands must be the least-maximum-cost
-cover over the row work (min(count, 2048) + 430 per tile; halo rows at 0.4)
-and the send and
-receive counts the count matrix restated from the histograms; every
-projected Gaussian must be packed for exactly the ranks whose band plus a
-one-tile-row halo its rectangle meets, in increasing id order. A routed step of `world` ranks,
-emulated on one GPU by running the ranks' calls one after another (the
-payloads and returned records are handed over in device memory instead of
-an all-to-all), must equal the single-GPU fused step: the bands are
-rasterised over exactly the Gaussians that touch them, in the same order.
+cover over the row work (min(count, 2048) + 430 per tile; halo rows at
+0.4) and the send and receive counts the count matrix restated from the
+histograms; every projected Gaussian must be packed for exactly the ranks
+whose band plus a one-tile-row halo its rectangle meets, in increasing id
+order. A routed step of `world` ranks, emulated on one GPU by running the
+ranks' calls one after another (the payloads and returned records are
+handed over in device memory instead of an all-to-all), must equal the
+single-GPU fused step: the bands are rasterised over exactly the Gaussians
+that touch them, in the same order.
 """
 import numpy as np
 import pytest

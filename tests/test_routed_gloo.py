@@ -10,13 +10,13 @@ meets, rasterises each band over what it received, and returns the gradient
 records to the owners, which apply the projection VJP and Adam to their
 slice. The stand-in calls restate the device side (route.cu): row work =
 sum over the row's tiles of min(count, 2048) + 430 (route_row_work), bands
-as the
-least-maximum-cost cover with the halo rows costed (route_band_cuts), the
-count matrix from the histograms (checked against each slice's own
-destinations), destinations by the halo rule, packing grouped by
-destination in increasing id. The slices put together must equal one single-process oracle
-step, every Gaussian that has a gradient in a band must have reached that
-band, and nothing may reach a band it does not touch.
+as the least-maximum-cost cover with the halo rows costed
+(route_band_cuts), the count matrix from the histograms (checked against
+each slice's own destinations), destinations by the halo rule, packing
+grouped by destination in increasing id. The slices put together must
+equal one single-process oracle step, every Gaussian that has a gradient in
+a band must have reached that band, and nothing may reach a band it does
+not touch.
 """
 import os
 import socket
