@@ -410,7 +410,8 @@ int msplat_loss_ssim_noalloc(const float* out_img, const float* gt, const float*
  * l1 term, distortion term), raster_counters (i64 [4]: blended
  * (pixel, surfel) pairs of the forward rasteriser, its (warp, surfel) visits
  * past the cull, the backward's (warp, surfel) visits and its blended pairs;
- * each visit evaluates 32 pixels) and intersection_totals (i64 [5]: emitted
+ * each visit evaluates 32 pixels; zeros unless msplat_set_raster_counters
+ * enabled them) and intersection_totals (i64 [5]: emitted
  * keys, kept intersections, band begin and end, tiles with more than 512
  * keys). Returns MSPLAT_ERR_ARGUMENT for an unknown
  * name or a tensor the last call did not produce. */
