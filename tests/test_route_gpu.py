@@ -152,7 +152,8 @@ def _routed_step_one_gpu(B, case, g, cam, adam, gt, world):
     return parts_sum.cpu().numpy(), bands
 
 
-@pytest.mark.parametrize("name,world", [("sh3_small", 1), ("sh3_small", 3), ("overflow", 2), ("sh1_odd", 4)])
+@pytest.mark.parametrize("name,world", [("sh3_small", 1), ("sh3_small", 3), ("overflow", 2), ("sh1_odd", 4),
+                                        ("sh3_small", 8)])
 def test_routed_step_equals_fused_step(name, world):
     from msplat import sharding
     case = Case(name)
